@@ -1,0 +1,193 @@
+/*
+ * ttl_moe.h -- C ABI of the B200 gpt-oss MoE backend for tt-lab.
+ *
+ * This is the whole boundary between tt-lab's host code and the CUDA kernels:
+ * plain C, scalars and pointers only (the rule tt-lab states for its own native
+ * kernels at src/tt_matvec.h:9).  Every entry point returns TTL_OK (0) or a
+ * negative status; ttl_moe_last_error() gives the message.  A C++ caller turns a
+ * failure into std::runtime_error (tt-lab's error style, src/main.cpp:414-417);
+ * tt-lab_b200/host/cuda_moe.hpp does exactly that.
+ *
+ * Reference interfaces replaced (paths inside tenstorrent/tt-lab):
+ *   ttl_moe_decode        GptOssModel::moe          src/model.cpp:292-338
+ *   ttl_moe_prefill       GptOssModel::moe_batch    src/model.cpp:340-461
+ *   ttl_moe_forward       the per-layer RMSNorm -> moe -> residual sequence of
+ *                         GptOssModel::forward      src/model.cpp:586-595
+ *   ttl_moe_upload_layer  the weight binding of the GptOssModel constructor
+ *                         (require_tensor)          src/model.cpp:157-169
+ *   ttl_moe_create        backend start-up, as run_tt_firmware_inference's
+ *                         runtime open              src/tt_backend.h:38-41
+ *   ttl_pack_mxfp4        the requant payload packer write_bfp8_strip_payload
+ *                                                   src/requant.cpp:258-277
+ *   ttl_ttq_*             the TTQ container writer  src/requant.cpp:23-68,
+ *                                                   :415-504; src/requant.h:31-52
+ *
+ * Memory: device buffers are allocated once in ttl_moe_create and
+ * ttl_moe_upload_layer and freed in ttl_moe_destroy ("allocate dynamic memory at
+ * startup only", tt-lab AGENTS.md).  Compute calls allocate nothing.
+ * Threading: one host thread per handle; calls on one handle are serialised on
+ * the handle's CUDA stream.
+ */
+#ifndef TTL_MOE_H
+#define TTL_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTL_MOE_ABI_VERSION 1
+#define TTL_MOE_DIM 2880          /* hidden = expert intermediate (src/model.h:34, :43) */
+#define TTL_MOE_TOPK 4            /* experts per token (src/model.h:42) */
+#define TTL_MOE_BLOCK_BYTES 17    /* GGUF MXFP4 block: E8M0 scale + 16 quant bytes */
+#define TTL_MOE_NCCL_ID_BYTES 128 /* sizeof(ncclUniqueId) */
+
+enum {
+    TTL_OK = 0,
+    TTL_ERR_ARGUMENT = -1,    /* bad argument; nothing was enqueued */
+    TTL_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+    TTL_ERR_STATE = -3,       /* layer not uploaded, capacity exceeded, ... */
+    TTL_ERR_NCCL = -4,        /* a NCCL call failed or its communicator broke */
+    TTL_ERR_DEVICE = -5,      /* a kernel reported an error in the device status word */
+    TTL_ERR_UNSUPPORTED = -6, /* no sm_100 device, or a feature not built */
+    TTL_ERR_IO = -7           /* TTQ file I/O */
+};
+
+typedef struct ttl_moe ttl_moe;
+
+typedef struct {
+    uint32_t experts;    /* 32 (gpt-oss-20b) or 128 (gpt-oss-120b) */
+    uint32_t layers;     /* MoE layers the handle holds, 1..36 */
+    uint32_t max_tokens; /* prefill capacity per call; 0 = decode only */
+    int32_t device;      /* CUDA device ordinal, -1 = the calling thread's current device */
+    uint32_t rank;       /* expert-parallel rank in [0, world) */
+    uint32_t world;      /* 1, 2, 4 or 8 ranks, one process (and one GPU) each */
+    const void *nccl_id; /* world > 1: the TTL_MOE_NCCL_ID_BYTES id from ttl_moe_nccl_id() on rank 0 */
+    uint32_t flags;      /* reserved, 0 */
+} ttl_moe_config;
+
+int ttl_moe_abi_version(void);
+
+/* Message of the last failed call on `handle`, or of the calling thread's last
+ * failed ttl_moe_create / ttl_pack / ttl_ttq call when `handle` is NULL. */
+const char *ttl_moe_last_error(const ttl_moe *handle);
+
+/* Writes a fresh NCCL unique id (TTL_MOE_NCCL_ID_BYTES) for a multi-rank handle. */
+int ttl_moe_nccl_id(void *id_out);
+
+int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out);
+void ttl_moe_destroy(ttl_moe *handle);
+
+/* Copies one layer's MoE tensors to the device and packs the experts this rank
+ * owns (experts [rank*E/world, (rank+1)*E/world)).  The arrays are the GGUF
+ * tensors bound at src/model.cpp:157-169, for all E experts:
+ *   router_w  f32 [E][2880]            ffn_gate_inp.weight
+ *   router_b  f32 [E]                  ffn_gate_inp.bias
+ *   gate_w    MXFP4 [E][2880][90][17]  ffn_gate_exps.weight   (GGUF blocks)
+ *   gate_b    f32 [E][2880]            ffn_gate_exps.bias
+ *   up_w/up_b, down_w/down_b           ffn_up_exps.*, ffn_down_exps.*
+ * Host or device pointers.  Synchronous. */
+int ttl_moe_upload_layer(ttl_moe *handle, int layer, const float *router_w, const float *router_b,
+                         const void *gate_w, const float *gate_b, const void *up_w, const float *up_b,
+                         const void *down_w, const float *down_b);
+
+/* Post-attention RMSNorm weights (blk.N.post_attention_norm.weight, f32 [2880])
+ * applied by ttl_moe_forward before layer `layer`'s MoE.  Default: all ones. */
+int ttl_moe_upload_norm(ttl_moe *handle, int layer, const float *norm_w);
+
+/* Decode MoE of one token on layer `layer`: GptOssModel::moe.
+ * x, out: HOST f32 [2880]; top4_idx/top4_w: optional host [4] (rank order).
+ * Blocking: returns after `out` is written. */
+int ttl_moe_decode(ttl_moe *handle, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w);
+
+/* Prefill MoE of `tokens` tokens: GptOssModel::moe_batch.
+ * x, out: HOST f32 [tokens][2880]; idx/w: optional host [tokens][4].
+ * tokens <= max_tokens.  With world > 1 each rank passes its own contiguous
+ * share of the tokens.  Blocking. */
+int ttl_moe_prefill(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
+                    float *top4_w);
+
+/* Decode `tokens` independent tokens, one after another, each through layers
+ * [layer_begin, layer_end): per layer h = RMSNorm(x) * norm_w, x = x + MoE(h)
+ * (src/model.cpp:590-594 with the attention block left out).
+ * x: HOST f32 [tokens][2880] residual inputs; y: HOST f32 [tokens][2880]
+ * outputs (may alias x).  Blocking. */
+int ttl_moe_forward(ttl_moe *handle, int layer_begin, int layer_end, const float *x, float *y, size_t tokens);
+
+/* Device-pointer forms of the three calls above: all pointers are device
+ * memory of the handle's GPU; the work is enqueued on the handle's stream and
+ * the call returns without waiting.  ttl_moe_sync() waits and reports. */
+int ttl_moe_decode_async(ttl_moe *handle, int layer, const float *x, float *out, int32_t *top4_idx,
+                         float *top4_w);
+int ttl_moe_prefill_async(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out,
+                          int32_t *top4_idx, float *top4_w);
+int ttl_moe_forward_async(ttl_moe *handle, int layer_begin, int layer_end, const float *x, float *y,
+                          size_t tokens);
+
+/* Waits for the handle's stream, then checks the device status word that the
+ * kernels set on a bounds or bounded-wait failure (TTL_ERR_DEVICE). */
+int ttl_moe_sync(ttl_moe *handle);
+
+/* The handle's cudaStream_t, as void *. */
+void *ttl_moe_stream(ttl_moe *handle);
+
+/* Diagnostic counters: [0] decode router exact re-evaluations at near-ties,
+ * [1] prefill tokens re-evaluated, [2] kernels launched by this handle.
+ * Returns the number written (<= n). */
+int ttl_moe_counters(const ttl_moe *handle, uint64_t *out, size_t n);
+
+/* Kernel timing for benchmarks: with `enable` set, forward graphs captured
+ * afterwards record CUDA events around the router, gate/up and down kernels of
+ * every layer of their first token.  ttl_moe_kernel_ms() then returns the mean
+ * duration in ms of [router, gate/up, down] over those layers from the last
+ * completed replay.  No counterpart in tt-lab (it profiles with device cycle
+ * stamps, src/tt_backend.cpp:2338-2380). */
+int ttl_moe_profile(ttl_moe *handle, int enable);
+int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
+
+/* ---- GPU weight-layout packer (requant) -------------------------------- */
+
+/* Bytes of the packed layout (TTQ format TTL_TTQ_FORMAT_MXFP4_GPU) of
+ * `matrices` MXFP4 matrices of 2880 rows x 2880 columns. */
+size_t ttl_packed_bytes(size_t matrices);
+
+/* Packs `matrices` GGUF MXFP4 matrices (2880 x 2880 each, 17-byte blocks) into
+ * the GPU layout on device `device`.  src/dst host or device.  Lossless:
+ * ttl_unpack_mxfp4 restores the GGUF bytes exactly. */
+int ttl_pack_mxfp4(const void *gguf, size_t matrices, void *packed, int device);
+int ttl_unpack_mxfp4(const void *packed, size_t matrices, void *gguf, int device);
+
+/* ---- TTQ container (TTLBQNT1, src/requant.h:31-52) ----------------------- */
+
+#define TTL_TTQ_FORMAT_MXFP4_GPU 6 /* new format id next to tt-lab's 1..5 */
+
+typedef struct ttl_ttq_writer ttl_ttq_writer;
+
+/* Opens `path` for an atomic write: data goes to a temporary file beside it and
+ * ttl_ttq_finish renames it over `path` (src/requant.cpp:23-68).  model is 20
+ * or 120; layers/experts as in the GGUF. */
+int ttl_ttq_open(const char *path, uint32_t model, uint32_t layers, uint32_t experts, uint32_t tensor_count,
+                 ttl_ttq_writer **writer_out);
+/* Appends one tensor record and its payload (64-byte aligned). */
+int ttl_ttq_add(ttl_ttq_writer *writer, const char *name, uint32_t format, uint32_t rank, const uint64_t *shape,
+                const void *payload, uint64_t size);
+int ttl_ttq_finish(ttl_ttq_writer *writer);
+/* Frees the writer; an unfinished file is removed. */
+void ttl_ttq_close(ttl_ttq_writer *writer);
+
+/* ---- synthetic inputs (benchmarks and tests) ---------------------------- */
+
+/* Fills GGUF-layout MXFP4 blocks from (seed, stream): quant bytes uniform,
+ * scale bytes uniform over [scale_lo, scale_lo + scale_count).  dst host or
+ * device. */
+int ttl_synth_mxfp4(void *dst, size_t blocks, uint64_t seed, uint64_t stream, uint32_t scale_lo,
+                    uint32_t scale_count);
+/* Fills n f32 values sigma * IrwinHall12(seed, stream) + mean.  dst host or device. */
+int ttl_synth_normal(float *dst, size_t n, uint64_t seed, uint64_t stream, float sigma, float mean);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

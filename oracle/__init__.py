@@ -1,0 +1,175 @@
+"""CPU oracle for the gpt-oss MoE path -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+legs use this package, and only as the checker; the product (libttl_moe) never
+links or calls it.
+
+Two oracles, both built by oracle/Makefile:
+  * ``port``      -- oracle/moe_oracle.c, a plain-C restatement of tt-lab's
+                     algorithm with each function citing the reference file:line;
+  * ``reference`` -- oracle/_ref/libttlref.so, tt-lab's own src/tensor.cpp,
+                     src/gguf.cpp and src/model.cpp compiled unmodified, driven
+                     through ref_shim.cpp (GptOssModel::moe / moe_batch).
+The port is pinned against the reference's known-answer vectors and against the
+compiled reference bit for bit (tests/test_oracle.py).
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+PORT_PATH = HERE / "_build" / "libmoe_oracle.so"
+REF_PATH = HERE / "_ref" / "libttlref.so"
+DIM = 2880
+ISA_DEFAULT = 0
+ISA_V4 = 1
+
+_port = None
+_ref = None
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [("experts", ctypes.c_size_t)] + [
+        (n, ctypes.c_void_p) for n in ("router_w", "router_b", "gate_w", "up_w", "down_w", "gate_b", "up_b",
+                                        "down_b")]
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def port():
+    global _port
+    if _port is None:
+        if not PORT_PATH.exists():
+            raise OSError(f"oracle not built: {PORT_PATH} (make -C oracle oracle)")
+        L = ctypes.CDLL(str(PORT_PATH))
+        vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+        L.oref_mxfp4_scale.restype = ctypes.c_float
+        L.oref_mxfp4_scale.argtypes = [ctypes.c_uint8]
+        L.oref_matvec_add_mxfp4.argtypes = [vp, vp, vp, vp, i32]
+        L.oref_matmul_add_mxfp4_selected.argtypes = [vp, vp, vp, vp, sz, vp, i32]
+        L.oref_moe_decode.argtypes = [ctypes.POINTER(_Layer), vp, vp, vp, vp, i32]
+        L.oref_moe_prefill.argtypes = [ctypes.POINTER(_Layer), vp, sz, vp, vp, vp, i32]
+        L.oref_moe_prefill.restype = i32
+        L.oref_rms_norm.argtypes = [vp, vp, ctypes.c_float, vp, sz]
+        L.oref_select_top4.argtypes = [vp, sz, vp]
+        L.oref_softmax4.argtypes = [vp, vp, vp]
+        L.oref_swiglu.restype = ctypes.c_float
+        L.oref_swiglu.argtypes = [ctypes.c_float, ctypes.c_float]
+        _port = L
+    return _port
+
+
+def ref_available() -> bool:
+    return REF_PATH.exists()
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        if not REF_PATH.exists():
+            raise OSError(f"reference oracle not built: {REF_PATH} (make -C oracle ref)")
+        L = ctypes.CDLL(str(REF_PATH))
+        vp, sz, i32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+        L.tref_last_error.restype = ctypes.c_char_p
+        L.tref_isa_v4.restype = i32
+        L.tref_mxfp4_scale.restype = ctypes.c_float
+        L.tref_mxfp4_scale.argtypes = [ctypes.c_uint8]
+        L.tref_matvec_add_mxfp4.argtypes = [vp, vp, sz, sz, vp, vp, i32]
+        L.tref_matmul_add_mxfp4_selected.argtypes = [vp, vp, sz, sz, vp, vp, sz, vp, i32]
+        L.tref_rms_norm.argtypes = [vp, vp, ctypes.c_float, vp, sz]
+        L.tref_moe_decode.argtypes = [sz] + [vp] * 12
+        L.tref_moe_prefill.argtypes = [sz] + [vp] * 9 + [sz, vp, vp, vp]
+        L.tref_moe_decode_threaded.argtypes = [sz] + [vp] * 10 + [i32]
+        _ref = L
+    return _ref
+
+
+def _ref_check(rc):
+    if rc != 0:
+        raise RuntimeError("reference oracle: " + (ref().tref_last_error() or b"").decode())
+
+
+def _layer(t):
+    experts = t["router_b"].shape[0]
+    return _Layer(experts, *[t[n].ctypes.data for n in ("router_w", "router_b", "gate_w", "up_w", "down_w",
+                                                          "gate_b", "up_b", "down_b")])
+
+
+def moe_decode(t, x, isa=ISA_V4, impl="port"):
+    """Decode MoE of one token.  Returns (out [2880], idx [4], w [4])."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(DIM, np.float32)
+    idx = np.empty(4, np.int32)
+    w = np.empty(4, np.float32)
+    if impl == "port":
+        lay = _layer(t)
+        port().oref_moe_decode(ctypes.byref(lay), _p(x), _p(out), _p(idx), _p(w), isa)
+    else:
+        _ref_check(ref().tref_moe_decode(t["router_b"].shape[0], _p(t["router_w"]), _p(t["router_b"]),
+                                         _p(t["gate_w"]), _p(t["gate_b"]), _p(t["up_w"]), _p(t["up_b"]),
+                                         _p(t["down_w"]), _p(t["down_b"]), _p(x), _p(out), _p(idx), _p(w)))
+    return out, idx, w
+
+
+def moe_prefill(t, x, isa=ISA_V4, impl="port"):
+    """Prefill MoE of x [T, 2880].  Returns (out [T,2880], idx [T,4], w [T,4])."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, DIM)
+    T = x.shape[0]
+    out = np.empty((T, DIM), np.float32)
+    idx = np.empty((T, 4), np.int32)
+    w = np.empty((T, 4), np.float32)
+    if impl == "port":
+        lay = _layer(t)
+        if port().oref_moe_prefill(ctypes.byref(lay), _p(x), T, _p(out), _p(idx), _p(w), isa) != 0:
+            raise MemoryError("oracle prefill allocation failed")
+    else:
+        _ref_check(ref().tref_moe_prefill(t["router_b"].shape[0], _p(t["router_w"]), _p(t["router_b"]),
+                                          _p(t["gate_w"]), _p(t["gate_b"]), _p(t["up_w"]), _p(t["up_b"]),
+                                          _p(t["down_w"]), _p(t["down_b"]), _p(x), T, _p(out), _p(idx), _p(w)))
+    return out, idx, w
+
+
+def rms_norm(x, g, eps=1.0e-5, impl="port"):
+    x = np.ascontiguousarray(x, np.float32)
+    g = np.ascontiguousarray(g, np.float32)
+    out = np.empty_like(x)
+    if impl == "port":
+        port().oref_rms_norm(_p(x), _p(g), ctypes.c_float(eps), _p(out), x.size)
+    else:
+        _ref_check(ref().tref_rms_norm(_p(x), _p(g), ctypes.c_float(eps), _p(out), x.size))
+    return out
+
+
+def forward(layers, x, isa=ISA_V4, impl="port"):
+    """Per token: for each layer h = rms_norm(x, norm_w); x = x + moe(h)
+    (tt-lab src/model.cpp:590-594).  layers: list of tensor dicts."""
+    x = np.array(x, np.float32).reshape(-1, DIM)
+    ones = np.ones(DIM, np.float32)
+    for t in range(x.shape[0]):
+        cur = x[t].copy()
+        for lay in layers:
+            h = rms_norm(cur, lay.get("norm_w", ones), impl=impl)
+            out, _, _ = moe_decode(lay, h, isa, impl)
+            cur = (cur + out).astype(np.float32)
+        x[t] = cur
+    return x
+
+
+def compare(a, b):
+    """tt-lab's compare_vectors metrics (src/tt_backend.cpp:3100-3128) plus the
+    max error relative to max |b| used as the parity bar."""
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    err = a - b
+    rms_b = np.sqrt(np.mean(b * b))
+    return {
+        "max_abs": float(np.max(np.abs(err))),
+        "max_rel": float(np.max(np.abs(err)) / max(np.max(np.abs(b)), 1e-30)),
+        "rel_rms": float(np.sqrt(np.mean(err * err)) / max(rms_b, 1e-30)),
+        "cosine": float(np.dot(a, b) / max(np.sqrt(np.dot(a, a) * np.dot(b, b)), 1e-30)),
+    }

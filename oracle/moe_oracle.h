@@ -1,0 +1,76 @@
+/*
+ * moe_oracle.h -- CPU restatement of tt-lab's gpt-oss MoE path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This header and moe_oracle.c are the checker that
+ * the parity tests, the smoke check and the CPU-baseline leg of the benchmark
+ * compare the CUDA path against.  Nothing in the product library links or calls
+ * this code.
+ *
+ * Every function restates one piece of the reference (tenstorrent/tt-lab) and
+ * cites the file:line it follows.  Floating-point order is kept exactly:
+ * products are rounded before the add unless the reference uses an explicit
+ * fused multiply-add (the reference builds with -ffp-contract=off).  The
+ * reference's MXFP4 kernels exist as two ISA clones with different rounding
+ * (src/tensor.cpp:239-304 and :319-495); both are restated and selected with
+ * `isa` (OREF_ISA_V4 = AVX-512 clone, OREF_ISA_DEFAULT = scalar clone).
+ *
+ * Parity of this restatement is pinned two ways (tests/test_oracle.py):
+ *   - the reference's own known-answer vectors (tests/host_dispatch.cpp:92-127,
+ *     src/tests.cpp:42);
+ *   - bit-exact agreement with the reference compiled from its own sources
+ *     (oracle/_ref, built by oracle/Makefile) on seeded inputs.
+ */
+#ifndef TTL_MOE_ORACLE_H
+#define TTL_MOE_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { OREF_ISA_DEFAULT = 0, OREF_ISA_V4 = 1 };
+
+enum {
+    OREF_DIM = 2880,                /* src/model.h:34, :43 */
+    OREF_BLOCKS = 90,               /* src/tensor.cpp:78 */
+    OREF_ROW_BYTES = 1530,          /* src/tensor.cpp:79 (90 blocks x 17 B) */
+    OREF_TOPK = 4,                  /* src/model.h:42 */
+    OREF_MATVEC_SELECTED_MAX = 4    /* src/model.cpp:22 */
+};
+
+/* One MoE layer, all arrays in GGUF order (src/model.cpp:157-169). */
+typedef struct {
+    size_t experts;            /* E: 32 (20b) or 128 (120b) */
+    const float *router_w;     /* [E][2880] f32, ffn_gate_inp.weight */
+    const float *router_b;     /* [E] f32, ffn_gate_inp.bias */
+    const uint8_t *gate_w;     /* [E][2880 rows][90 blocks][17 B] MXFP4 */
+    const uint8_t *up_w;
+    const uint8_t *down_w;
+    const float *gate_b;       /* [E][2880] f32 */
+    const float *up_b;
+    const float *down_b;
+} oref_layer;
+
+float oref_mxfp4_scale(uint8_t exponent);
+void oref_matvec_add_f32(const float *w, const float *bias, const float *x, float *y, size_t rows, size_t cols);
+void oref_matvec_add_mxfp4(const uint8_t *w_expert, const float *bias_expert, const float *x, float *y, int isa);
+void oref_matmul_add_mxfp4_selected(const uint8_t *w_expert, const float *bias_expert, const float *xt,
+                                    const size_t *tokens, size_t n, float *out, int isa);
+void oref_select_top4(const float *logits, size_t experts, int32_t idx[4]);
+void oref_softmax4(const float *logits, const int32_t idx[4], float w[4]);
+float oref_swiglu(float gate, float up);
+void oref_rms_norm(const float *x, const float *g, float eps, float *out, size_t n);
+
+/* Decode MoE for one token (src/model.cpp:292-338).  idx/w may be NULL. */
+void oref_moe_decode(const oref_layer *layer, const float *x, float *out, int32_t *idx, float *w, int isa);
+/* Prefill MoE for T tokens (src/model.cpp:340-461).  Returns 0, or -1 on
+ * allocation failure.  idx/w ([T][4]) may be NULL. */
+int oref_moe_prefill(const oref_layer *layer, const float *x, size_t tokens, float *out, int32_t *idx, float *w,
+                     int isa);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

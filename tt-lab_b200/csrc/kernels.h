@@ -1,0 +1,92 @@
+// kernels.h -- launchers of the MoE kernels (internal to libttl_moe).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace ttl {
+
+// Device view of one layer's weights on this rank.
+struct LayerDev {
+    const float *router_w;  // [E][2880]
+    const float *router_b;  // [E]
+    const float *norm_w;    // [2880]
+    const uint8_t *gate;    // packed [E_local] matrices
+    const uint8_t *up;
+    const uint8_t *down;
+    const float *gate_b;    // [E_local][2880]
+    const float *up_b;
+    const float *down_b;
+};
+
+// Decode scratch, allocated once per handle.
+struct DecodeWork {
+    float *h;               // [2880] router / expert input of the current layer
+    float *logits;          // [E] fast logits
+    float *bounds;          // [E] error bounds of the fast logits
+    int32_t *top_idx;       // [4]
+    float *top_w;           // [4]
+    float *hidden;          // [4][2880]
+    float *partial;         // [2880] combined output of this rank's experts
+    unsigned int *arrive;   // last-CTA arrival counter (self-resetting)
+    unsigned long long *counters;  // [4] device counters
+    uint32_t *status;       // device status word
+};
+
+struct DecodeShape {
+    int experts;       // E
+    int expert_begin;  // first expert owned by this rank
+    int expert_count;  // experts owned by this rank
+    int sms;           // multiprocessors of the device
+};
+
+// Router + top-4 + softmax.  mode 0: h = x (x already normalized);
+// mode 1: h = RMSNorm(x) * norm_w (eps 1e-5).
+void launch_decode_router(const LayerDev &L, const DecodeWork &w, const DecodeShape &s, const float *x, int mode,
+                          cudaStream_t stream);
+// gate/up matvecs of the selected experts with the SwiGLU epilogue.
+void launch_decode_gateup(const LayerDev &L, const DecodeWork &w, const DecodeShape &s, cudaStream_t stream);
+// down matvecs + weighted combine in rank order.  residual: if non-null,
+// out = residual + moe, else out = moe (this rank's partial when EP).
+void launch_decode_down(const LayerDev &L, const DecodeWork &w, const DecodeShape &s, const float *residual,
+                        float *out, cudaStream_t stream);
+// out[i] = residual[i] + moe[i]
+void launch_add(const float *residual, const float *moe, float *out, int n, cudaStream_t stream);
+
+// GGUF -> packed layout on the device.
+void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream);
+
+// ---- prefill ----
+struct PrefillWork {
+    float *logits;            // [T][E]
+    int32_t *top_idx;         // [T][4]
+    float *top_w;             // [T][4]
+    int32_t *counts;          // [E]
+    int32_t *offsets;         // [E + 1]
+    int32_t *pair_token;      // [4T] token of each routed pair, grouped by expert
+    int32_t *pair_slot;       // [T][4] position of (token, rank) in the grouped order, -1 if not local
+    int32_t *tiles;           // [4T / 8 + E] work list: (expert << 20) | first pair
+    int32_t *tile_count;      // [1]
+    float *hidden;            // [4T][2880] SwiGLU output per pair
+    float *down;              // [4T][2880] down output per pair
+    uint32_t *status;
+};
+
+struct PrefillShape {
+    int experts;
+    int expert_begin;
+    int expert_count;
+    int tokens;
+    int sms;
+};
+
+void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
+                           cudaStream_t stream);
+void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStream_t stream);
+void launch_prefill_gateup(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
+                           cudaStream_t stream);
+void launch_prefill_down(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, cudaStream_t stream);
+void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream);
+
+} // namespace ttl

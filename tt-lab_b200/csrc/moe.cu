@@ -1,0 +1,839 @@
+// moe.cu -- the ttl_moe handle: start-up, weight upload, and the decode,
+// prefill and layer-stack entry points of include/ttl_moe.h.
+//
+// One handle drives one GPU.  Expert parallelism (world > 1) runs one process
+// per GPU; each rank holds experts [rank*E/world, (rank+1)*E/world) and the
+// ranks combine their partial outputs with NCCL over NVLink.  The router is
+// replicated (it is 0.7% of a layer's bytes) so every rank derives the same
+// top-4 without an exchange.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+#include "kernels.h"
+
+namespace ttl {
+void configure_decode_kernels();
+void configure_prefill_kernels();
+} // namespace ttl
+
+using namespace ttl;
+
+namespace {
+
+struct LayerStore {
+    bool uploaded = false;
+    float *router_w = nullptr;
+    float *router_b = nullptr;
+    float *norm_w = nullptr;
+    uint8_t *gate = nullptr;
+    uint8_t *up = nullptr;
+    uint8_t *down = nullptr;
+    float *gate_b = nullptr;
+    float *up_b = nullptr;
+    float *down_b = nullptr;
+};
+
+struct GraphKey {
+    const void *x;
+    const void *y;
+    size_t tokens;
+    int begin;
+    int end;
+    bool operator<(const GraphKey &o) const {
+        return std::tie(x, y, tokens, begin, end) < std::tie(o.x, o.y, o.tokens, o.begin, o.end);
+    }
+};
+
+} // namespace
+
+struct ttl_moe {
+    ttl_moe_config cfg{};
+    int device = 0;
+    int sms = 148;
+    cudaStream_t stream = nullptr;
+    std::string error;
+    int expert_begin = 0;
+    int expert_count = 0;
+    std::vector<LayerStore> layers;
+    std::vector<void *> allocations;
+    uint8_t *staging = nullptr;  // one GGUF expert tensor (this rank's experts)
+    size_t staging_bytes = 0;
+    DecodeWork dw{};
+    PrefillWork pw{};
+    float *d_x = nullptr;        // [max(1, max_tokens)][2880]
+    float *d_y = nullptr;
+    float *d_fwd = nullptr;      // forward staging for host calls [fwd_cap][2880]
+    size_t fwd_cap = 0;
+    float *d_ones = nullptr;
+    uint32_t *d_status = nullptr;
+    unsigned long long *d_counters = nullptr;
+    uint64_t launches = 0;
+    ncclComm_t comm = nullptr;
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    bool use_graphs = true;
+    bool profile = false;
+    int profile_layers = 0;        // layers covered by the recorded events
+    std::vector<cudaEvent_t> events;  // [layers][4]
+};
+
+namespace ttl {
+
+std::string &thread_error() {
+    thread_local std::string message;
+    return message;
+}
+
+int fail(ttl_moe *handle, int code, const std::string &message) {
+    if (handle) {
+        handle->error = message;
+    } else {
+        thread_error() = message;
+    }
+    return code;
+}
+
+const char *handle_error(const ttl_moe *handle) {
+    return handle ? handle->error.c_str() : thread_error().c_str();
+}
+
+bool is_device_pointer(const void *p) {
+    if (!p) {
+        return false;
+    }
+    cudaPointerAttributes attr{};
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged;
+}
+
+} // namespace ttl
+
+namespace {
+
+int alloc(ttl_moe *h, void **p, size_t bytes) {
+    if (bytes == 0) {
+        *p = nullptr;
+        return TTL_OK;
+    }
+    const cudaError_t e = cudaMalloc(p, bytes);
+    if (e != cudaSuccess) {
+        return fail(h, TTL_ERR_CUDA, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    }
+    h->allocations.push_back(*p);
+    return TTL_OK;
+}
+
+template <class T> int alloc_n(ttl_moe *h, T **p, size_t n) {
+    return alloc(h, reinterpret_cast<void **>(p), n * sizeof(T));
+}
+
+LayerDev layer_view(const ttl_moe *h, int layer) {
+    const LayerStore &s = h->layers[size_t(layer)];
+    LayerDev L;
+    L.router_w = s.router_w;
+    L.router_b = s.router_b;
+    L.norm_w = s.norm_w ? s.norm_w : h->d_ones;
+    L.gate = s.gate;
+    L.up = s.up;
+    L.down = s.down;
+    L.gate_b = s.gate_b;
+    L.up_b = s.up_b;
+    L.down_b = s.down_b;
+    return L;
+}
+
+DecodeShape decode_shape(const ttl_moe *h) {
+    return DecodeShape{int(h->cfg.experts), h->expert_begin, h->expert_count, h->sms};
+}
+
+int check_layer(ttl_moe *h, int layer) {
+    if (layer < 0 || layer >= int(h->cfg.layers)) {
+        return fail(h, TTL_ERR_ARGUMENT, "layer " + std::to_string(layer) + " out of range");
+    }
+    if (!h->layers[size_t(layer)].uploaded) {
+        return fail(h, TTL_ERR_STATE, "layer " + std::to_string(layer) + " was not uploaded");
+    }
+    return TTL_OK;
+}
+
+int set_device(ttl_moe *h) {
+    TTL_TRY_CUDA(h, cudaSetDevice(h->device));
+    return TTL_OK;
+}
+
+int nccl_check(ttl_moe *h, ncclResult_t r, const char *what) {
+    if (r != ncclSuccess) {
+        return fail(h, TTL_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+    }
+    return TTL_OK;
+}
+
+// Sum of the ranks' partial outputs, in place on the handle's stream.
+int allreduce(ttl_moe *h, float *buf, size_t n) {
+    if (h->cfg.world <= 1) {
+        return TTL_OK;
+    }
+    return nccl_check(h, ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, h->comm, h->stream), "ncclAllReduce");
+}
+
+// Enqueues one decode layer: router -> gate/up -> down (+ combine, residual).
+int enqueue_decode_layer(ttl_moe *h, int layer, const float *x, int mode, const float *residual, float *out,
+                         cudaEvent_t *ev = nullptr) {
+    const LayerDev L = layer_view(h, layer);
+    const DecodeShape s = decode_shape(h);
+    if (ev) {
+        cudaEventRecordWithFlags(ev[0], h->stream, cudaEventRecordExternal);
+    }
+    launch_decode_router(L, h->dw, s, x, mode, h->stream);
+    if (ev) {
+        cudaEventRecordWithFlags(ev[1], h->stream, cudaEventRecordExternal);
+    }
+    launch_decode_gateup(L, h->dw, s, h->stream);
+    if (ev) {
+        cudaEventRecordWithFlags(ev[2], h->stream, cudaEventRecordExternal);
+    }
+    if (h->cfg.world > 1) {
+        launch_decode_down(L, h->dw, s, nullptr, h->dw.partial, h->stream);
+        if (ev) {
+            cudaEventRecordWithFlags(ev[3], h->stream, cudaEventRecordExternal);
+        }
+        h->launches += 3;
+        int rc = allreduce(h, h->dw.partial, kDim);
+        if (rc) {
+            return rc;
+        }
+        if (residual) {
+            launch_add(residual, h->dw.partial, out, kDim, h->stream);
+        } else {
+            TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->dw.partial, kDim * sizeof(float), cudaMemcpyDeviceToDevice,
+                                            h->stream));
+        }
+        h->launches += 1;
+    } else {
+        launch_decode_down(L, h->dw, s, residual, out, h->stream);
+        if (ev) {
+            cudaEventRecordWithFlags(ev[3], h->stream, cudaEventRecordExternal);
+        }
+        h->launches += 3;
+    }
+    TTL_TRY_CUDA(h, cudaGetLastError());
+    return TTL_OK;
+}
+
+int enqueue_forward(ttl_moe *h, int begin, int end, const float *x, float *y, size_t tokens) {
+    for (size_t t = 0; t < tokens; ++t) {
+        const float *cur = x + t * kDim;
+        float *dst = y + t * kDim;
+        for (int l = begin; l < end; ++l) {
+            cudaEvent_t *ev = nullptr;
+            if (h->profile && t == 0 && h->events.size() >= size_t(4 * (l - begin + 1))) {
+                ev = &h->events[size_t(4 * (l - begin))];
+                h->profile_layers = l - begin + 1;
+            }
+            int rc = enqueue_decode_layer(h, l, cur, 1, cur, dst, ev);
+            if (rc) {
+                return rc;
+            }
+            cur = dst;
+        }
+        if (begin == end && x != y) {
+            TTL_TRY_CUDA(h, cudaMemcpyAsync(dst, cur, kDim * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
+        }
+    }
+    return TTL_OK;
+}
+
+int check_status(ttl_moe *h) {
+    uint32_t status = 0;
+    TTL_TRY_CUDA(h, cudaMemcpy(&status, h->d_status, sizeof(status), cudaMemcpyDeviceToHost));
+    if (status) {
+        cudaMemset(h->d_status, 0, sizeof(uint32_t));
+        std::string what;
+        if (status & kStatusBadExpert) {
+            what += " expert-index-out-of-range";
+        }
+        if (status & kStatusCapacity) {
+            what += " capacity-exceeded";
+        }
+        if (status & kStatusWaitTimeout) {
+            what += " bounded-wait-timeout";
+        }
+        if (status & kStatusBadShape) {
+            what += " bad-shape";
+        }
+        return fail(h, TTL_ERR_DEVICE, "device status:" + what);
+    }
+    return TTL_OK;
+}
+
+int sync_and_check(ttl_moe *h) {
+    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    return check_status(h);
+}
+
+int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float *out) {
+    const LayerDev L = layer_view(h, layer);
+    PrefillShape s{int(h->cfg.experts), h->expert_begin, h->expert_count, int(tokens), h->sms};
+    launch_prefill_router(L, h->pw, s, x, h->stream);
+    launch_prefill_route(h->pw, s, h->stream);
+    launch_prefill_gateup(L, h->pw, s, x, h->stream);
+    launch_prefill_down(L, h->pw, s, h->stream);
+    launch_prefill_combine(h->pw, s, out, h->stream);
+    h->launches += 6;
+    TTL_TRY_CUDA(h, cudaGetLastError());
+    if (h->cfg.world > 1) {
+        return allreduce(h, out, tokens * kDim);
+    }
+    return TTL_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+int ttl_moe_abi_version(void) {
+    return TTL_MOE_ABI_VERSION;
+}
+
+const char *ttl_moe_last_error(const ttl_moe *handle) {
+    return handle_error(handle);
+}
+
+int ttl_moe_nccl_id(void *id_out) {
+    if (!id_out) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null id buffer");
+    }
+    ncclUniqueId id;
+    const ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) {
+        return fail(nullptr, TTL_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    }
+    static_assert(sizeof(id) == TTL_MOE_NCCL_ID_BYTES, "ncclUniqueId size");
+    std::memcpy(id_out, &id, sizeof(id));
+    return TTL_OK;
+}
+
+int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
+    if (!config || !handle_out) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null config or handle pointer");
+    }
+    *handle_out = nullptr;
+    const ttl_moe_config &c = *config;
+    if (c.experts != 32 && c.experts != 128) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "experts must be 32 or 128");
+    }
+    if (c.layers < 1 || c.layers > 36) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "layers must be in 1..36");
+    }
+    if (c.world != 1 && c.world != 2 && c.world != 4 && c.world != 8) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "world must be 1, 2, 4 or 8");
+    }
+    if (c.rank >= c.world) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "rank must be below world");
+    }
+    if (c.world > 1 && !c.nccl_id) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "world > 1 needs an NCCL id");
+    }
+    if (c.max_tokens > (1u << 16)) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "max_tokens above 65536");
+    }
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return fail(nullptr, TTL_ERR_UNSUPPORTED, "no CUDA device");
+    }
+    int device = c.device;
+    if (device < 0) {
+        if (cudaGetDevice(&device) != cudaSuccess) {
+            return fail(nullptr, TTL_ERR_CUDA, "cudaGetDevice failed");
+        }
+    }
+    if (device >= count) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "device ordinal out of range");
+    }
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+        return fail(nullptr, TTL_ERR_CUDA, "cudaGetDeviceProperties failed");
+    }
+    if (prop.major != 10) {
+        return fail(nullptr, TTL_ERR_UNSUPPORTED,
+                    "the kernels are built for sm_100a (B200); device is sm_" + std::to_string(prop.major) +
+                        std::to_string(prop.minor));
+    }
+
+    ttl_moe *h = new ttl_moe();
+    h->cfg = c;
+    h->cfg.nccl_id = nullptr;
+    h->device = device;
+    h->sms = prop.multiProcessorCount;
+    h->expert_count = int(c.experts / c.world);
+    h->expert_begin = int(c.rank) * h->expert_count;
+    h->layers.resize(c.layers);
+    const char *no_graph = std::getenv("TTL_MOE_NO_GRAPHS");
+    h->use_graphs = !(no_graph && no_graph[0] == '1');
+
+    auto bail = [&](int rc) {
+        std::string msg = h->error;
+        ttl_moe_destroy(h);
+        fail(nullptr, rc, msg);
+        return rc;
+    };
+    if (cudaSetDevice(device) != cudaSuccess) {
+        return bail(fail(h, TTL_ERR_CUDA, "cudaSetDevice failed"));
+    }
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        return bail(fail(h, TTL_ERR_CUDA, "cudaStreamCreate failed"));
+    }
+    configure_decode_kernels();
+    configure_prefill_kernels();
+
+    const size_t E = c.experts;
+    const size_t T = std::max<uint32_t>(c.max_tokens, 1u);
+    int rc = TTL_OK;
+    rc = rc ? rc : alloc_n(h, &h->d_status, 1);
+    rc = rc ? rc : alloc_n(h, &h->d_counters, 4);
+    rc = rc ? rc : alloc_n(h, &h->d_ones, kDim);
+    rc = rc ? rc : alloc_n(h, &h->dw.h, kDim);
+    rc = rc ? rc : alloc_n(h, &h->dw.logits, E);
+    rc = rc ? rc : alloc_n(h, &h->dw.bounds, E);
+    rc = rc ? rc : alloc_n(h, &h->dw.top_idx, 4);
+    rc = rc ? rc : alloc_n(h, &h->dw.top_w, 4);
+    rc = rc ? rc : alloc_n(h, &h->dw.hidden, 4 * size_t(kDim));
+    rc = rc ? rc : alloc_n(h, &h->dw.partial, kDim);
+    rc = rc ? rc : alloc_n(h, &h->dw.arrive, 1);
+    rc = rc ? rc : alloc_n(h, &h->d_x, T * kDim);
+    rc = rc ? rc : alloc_n(h, &h->d_y, T * kDim);
+    if (rc) {
+        return bail(rc);
+    }
+    h->dw.counters = h->d_counters;
+    h->dw.status = h->d_status;
+    if (c.max_tokens > 0) {
+        const size_t pairs = 4 * T;
+        rc = rc ? rc : alloc_n(h, &h->pw.logits, T * E);
+        rc = rc ? rc : alloc_n(h, &h->pw.top_idx, pairs);
+        rc = rc ? rc : alloc_n(h, &h->pw.top_w, pairs);
+        rc = rc ? rc : alloc_n(h, &h->pw.counts, E);
+        rc = rc ? rc : alloc_n(h, &h->pw.offsets, E + 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.pair_token, pairs);
+        rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
+        rc = rc ? rc : alloc_n(h, &h->pw.tiles, pairs / 8 + E + 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.tile_count, 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.hidden, pairs * kDim);
+        rc = rc ? rc : alloc_n(h, &h->pw.down, pairs * kDim);
+        h->pw.status = h->d_status;
+        if (rc) {
+            return bail(rc);
+        }
+    }
+    std::vector<float> ones(kDim, 1.0f);
+    if (cudaMemcpy(h->d_ones, ones.data(), kDim * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(h->d_status, 0, sizeof(uint32_t)) != cudaSuccess ||
+        cudaMemset(h->d_counters, 0, 4 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(h->dw.arrive, 0, sizeof(unsigned int)) != cudaSuccess ||
+        cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
+        cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess) {
+        return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
+    }
+    if (c.world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, c.nccl_id, sizeof(id));
+        const ncclResult_t r = ncclCommInitRank(&h->comm, int(c.world), id, int(c.rank));
+        if (r != ncclSuccess) {
+            h->comm = nullptr;
+            return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(r)));
+        }
+    }
+    *handle_out = h;
+    return TTL_OK;
+}
+
+void ttl_moe_destroy(ttl_moe *h) {
+    if (!h) {
+        return;
+    }
+    cudaSetDevice(h->device);
+    if (h->stream) {
+        cudaStreamSynchronize(h->stream);
+    }
+    for (auto &g : h->graphs) {
+        cudaGraphExecDestroy(g.second);
+    }
+    h->graphs.clear();
+    for (cudaEvent_t e : h->events) {
+        cudaEventDestroy(e);
+    }
+    if (h->comm) {
+        ncclCommDestroy(h->comm);
+    }
+    for (void *p : h->allocations) {
+        cudaFree(p);
+    }
+    if (h->stream) {
+        cudaStreamDestroy(h->stream);
+    }
+    delete h;
+}
+
+int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const float *router_b, const void *gate_w,
+                         const float *gate_b, const void *up_w, const float *up_b, const void *down_w,
+                         const float *down_b) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (layer < 0 || layer >= int(h->cfg.layers)) {
+        return fail(h, TTL_ERR_ARGUMENT, "layer out of range");
+    }
+    if (!router_w || !router_b || !gate_w || !gate_b || !up_w || !up_b || !down_w || !down_b) {
+        return fail(h, TTL_ERR_ARGUMENT, "null tensor pointer");
+    }
+    int rc = set_device(h);
+    if (rc) {
+        return rc;
+    }
+    LayerStore &s = h->layers[size_t(layer)];
+    const size_t E = h->cfg.experts;
+    const size_t El = size_t(h->expert_count);
+    if (!s.router_w) {
+        rc = rc ? rc : alloc_n(h, &s.router_w, E * kDim);
+        rc = rc ? rc : alloc_n(h, &s.router_b, E);
+        rc = rc ? rc : alloc_n(h, &s.gate, El * kPackedMatrixBytes);
+        rc = rc ? rc : alloc_n(h, &s.up, El * kPackedMatrixBytes);
+        rc = rc ? rc : alloc_n(h, &s.down, El * kPackedMatrixBytes);
+        rc = rc ? rc : alloc_n(h, &s.gate_b, El * kDim);
+        rc = rc ? rc : alloc_n(h, &s.up_b, El * kDim);
+        rc = rc ? rc : alloc_n(h, &s.down_b, El * kDim);
+        if (rc) {
+            return rc;
+        }
+    }
+    const size_t expert_gguf = size_t(kDim) * kGgufRowBytes;
+    const size_t first = size_t(h->expert_begin);
+    TTL_TRY_CUDA(h, cudaMemcpy(s.router_w, router_w, E * kDim * sizeof(float), cudaMemcpyDefault));
+    TTL_TRY_CUDA(h, cudaMemcpy(s.router_b, router_b, E * sizeof(float), cudaMemcpyDefault));
+    TTL_TRY_CUDA(h, cudaMemcpy(s.gate_b, gate_b + first * kDim, El * kDim * sizeof(float), cudaMemcpyDefault));
+    TTL_TRY_CUDA(h, cudaMemcpy(s.up_b, up_b + first * kDim, El * kDim * sizeof(float), cudaMemcpyDefault));
+    TTL_TRY_CUDA(h, cudaMemcpy(s.down_b, down_b + first * kDim, El * kDim * sizeof(float), cudaMemcpyDefault));
+    const void *srcs[3] = {gate_w, up_w, down_w};
+    uint8_t *dsts[3] = {s.gate, s.up, s.down};
+    for (int m = 0; m < 3; ++m) {
+        const uint8_t *src = (const uint8_t *)srcs[m] + first * expert_gguf;
+        if (!is_device_pointer(srcs[m])) {
+            if (!h->staging) {
+                h->staging_bytes = El * expert_gguf;
+                rc = alloc(h, reinterpret_cast<void **>(&h->staging), h->staging_bytes);
+                if (rc) {
+                    return rc;
+                }
+            }
+            TTL_TRY_CUDA(h, cudaMemcpy(h->staging, src, El * expert_gguf, cudaMemcpyHostToDevice));
+            src = h->staging;
+        }
+        launch_pack(src, dsts[m], El, h->stream);
+        TTL_TRY_CUDA(h, cudaGetLastError());
+        TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    }
+    s.uploaded = true;
+    return TTL_OK;
+}
+
+int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (layer < 0 || layer >= int(h->cfg.layers) || !norm_w) {
+        return fail(h, TTL_ERR_ARGUMENT, "bad layer or null weights");
+    }
+    int rc = set_device(h);
+    LayerStore &s = h->layers[size_t(layer)];
+    if (!s.norm_w) {
+        rc = rc ? rc : alloc_n(h, &s.norm_w, kDim);
+    }
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpy(s.norm_w, norm_w, kDim * sizeof(float), cudaMemcpyDefault));
+    return TTL_OK;
+}
+
+int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !out) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    int rc = check_layer(h, layer);
+    rc = rc ? rc : set_device(h);
+    rc = rc ? rc : enqueue_decode_layer(h, layer, x, 0, nullptr, out);
+    if (rc) {
+        return rc;
+    }
+    if (top4_idx) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToDevice,
+                                        h->stream));
+    }
+    if (top4_w) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToDevice,
+                                        h->stream));
+    }
+    return TTL_OK;
+}
+
+int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !out) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    int rc = check_layer(h, layer);
+    rc = rc ? rc : set_device(h);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    rc = enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->d_y, kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    if (top4_idx) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                        h->stream));
+    }
+    if (top4_w) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    }
+    return sync_and_check(h);
+}
+
+int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
+                          float *top4_w) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !out) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    if (tokens == 0) {
+        return fail(h, TTL_ERR_ARGUMENT, "prefill needs at least one token");  // src/model.cpp:464-466
+    }
+    if (tokens > h->cfg.max_tokens) {
+        return fail(h, TTL_ERR_STATE, "prefill exceeds startup batch capacity");  // src/model.cpp:470-472
+    }
+    int rc = check_layer(h, layer);
+    rc = rc ? rc : set_device(h);
+    rc = rc ? rc : enqueue_prefill(h, layer, x, tokens, out);
+    if (rc) {
+        return rc;
+    }
+    if (top4_idx) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->pw.top_idx, tokens * 4 * sizeof(int32_t),
+                                        cudaMemcpyDeviceToDevice, h->stream));
+    }
+    if (top4_w) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->pw.top_w, tokens * 4 * sizeof(float), cudaMemcpyDeviceToDevice,
+                                        h->stream));
+    }
+    return TTL_OK;
+}
+
+int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
+                    float *top4_w) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !out) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    if (tokens == 0) {
+        return fail(h, TTL_ERR_ARGUMENT, "prefill needs at least one token");
+    }
+    if (tokens > h->cfg.max_tokens) {
+        return fail(h, TTL_ERR_STATE, "prefill exceeds startup batch capacity");
+    }
+    int rc = check_layer(h, layer);
+    rc = rc ? rc : set_device(h);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, tokens * kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    rc = enqueue_prefill(h, layer, h->d_x, tokens, h->d_y);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->d_y, tokens * kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    if (top4_idx) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->pw.top_idx, tokens * 4 * sizeof(int32_t),
+                                        cudaMemcpyDeviceToHost, h->stream));
+    }
+    if (top4_w) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->pw.top_w, tokens * 4 * sizeof(float), cudaMemcpyDeviceToHost,
+                                        h->stream));
+    }
+    return sync_and_check(h);
+}
+
+int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const float *x, float *y, size_t tokens) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !y) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    if (layer_begin < 0 || layer_end < layer_begin || layer_end > int(h->cfg.layers)) {
+        return fail(h, TTL_ERR_ARGUMENT, "bad layer range");
+    }
+    int rc = set_device(h);
+    for (int l = layer_begin; l < layer_end && !rc; ++l) {
+        rc = check_layer(h, l);
+    }
+    if (rc || tokens == 0) {
+        return rc;
+    }
+    if (!h->use_graphs) {
+        return enqueue_forward(h, layer_begin, layer_end, x, y, tokens);
+    }
+    // The token loop is captured once per (buffers, count, layers) and replayed.
+    const GraphKey key{x, y, tokens, layer_begin, layer_end};
+    auto found = h->graphs.find(key);
+    if (found == h->graphs.end()) {
+        cudaGraph_t graph = nullptr;
+        TTL_TRY_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        const uint64_t launches = h->launches;
+        rc = enqueue_forward(h, layer_begin, layer_end, x, y, tokens);
+        const cudaError_t end = cudaStreamEndCapture(h->stream, &graph);
+        if (rc) {
+            if (graph) {
+                cudaGraphDestroy(graph);
+            }
+            return rc;
+        }
+        if (end != cudaSuccess) {
+            return fail(h, TTL_ERR_CUDA, std::string("stream capture: ") + cudaGetErrorString(end));
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (inst != cudaSuccess) {
+            return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
+        }
+        h->launches = launches;  // counted per replay below
+        found = h->graphs.emplace(key, exec).first;
+    }
+    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second, h->stream));
+    h->launches += tokens * size_t(layer_end - layer_begin) * (h->cfg.world > 1 ? 4 : 3);
+    return TTL_OK;
+}
+
+int ttl_moe_forward(ttl_moe *h, int layer_begin, int layer_end, const float *x, float *y, size_t tokens) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (!x || !y) {
+        return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    int rc = set_device(h);
+    if (rc || tokens == 0) {
+        return rc;
+    }
+    if (tokens > h->fwd_cap) {
+        // Grows the staging buffer; the first call with a larger count pays it.
+        float *p = nullptr;
+        rc = alloc_n(h, &p, tokens * kDim);
+        if (rc) {
+            return rc;
+        }
+        h->d_fwd = p;
+        h->fwd_cap = tokens;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_fwd, x, tokens * kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+    rc = ttl_moe_forward_async(h, layer_begin, layer_end, h->d_fwd, h->d_fwd, tokens);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(y, h->d_fwd, tokens * kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    return sync_and_check(h);
+}
+
+int ttl_moe_profile(ttl_moe *h, int enable) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    int rc = set_device(h);
+    if (rc) {
+        return rc;
+    }
+    if (enable && h->events.empty()) {
+        h->events.resize(size_t(4) * h->cfg.layers);
+        for (cudaEvent_t &e : h->events) {
+            TTL_TRY_CUDA(h, cudaEventCreate(&e));
+        }
+    }
+    h->profile = enable != 0;
+    return TTL_OK;
+}
+
+int ttl_moe_kernel_ms(ttl_moe *h, float *ms, size_t n) {
+    if (!h || !ms) {
+        return fail(h, TTL_ERR_ARGUMENT, "null argument");
+    }
+    if (h->profile_layers == 0) {
+        return fail(h, TTL_ERR_STATE, "no profiled forward graph has run");
+    }
+    double sum[3] = {0, 0, 0};
+    for (int l = 0; l < h->profile_layers; ++l) {
+        for (int k = 0; k < 3; ++k) {
+            float v = 0.0f;
+            TTL_TRY_CUDA(h, cudaEventElapsedTime(&v, h->events[size_t(4 * l + k)], h->events[size_t(4 * l + k + 1)]));
+            sum[k] += v;
+        }
+    }
+    for (size_t k = 0; k < n && k < 3; ++k) {
+        ms[k] = float(sum[k] / h->profile_layers);
+    }
+    return TTL_OK;
+}
+
+int ttl_moe_sync(ttl_moe *h) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    int rc = set_device(h);
+    return rc ? rc : sync_and_check(h);
+}
+
+void *ttl_moe_stream(ttl_moe *h) {
+    return h ? (void *)h->stream : nullptr;
+}
+
+int ttl_moe_counters(const ttl_moe *h, uint64_t *out, size_t n) {
+    if (!h || !out) {
+        return 0;
+    }
+    unsigned long long dev[4] = {0, 0, 0, 0};
+    cudaSetDevice(h->device);
+    cudaMemcpy(dev, h->d_counters, sizeof(dev), cudaMemcpyDeviceToHost);
+    const uint64_t vals[3] = {dev[0], dev[1], h->launches};
+    const size_t k = std::min<size_t>(n, 3);
+    for (size_t i = 0; i < k; ++i) {
+        out[i] = vals[i];
+    }
+    return int(k);
+}
+
+} // extern "C"

@@ -1,0 +1,285 @@
+"""ctypes binding of libttl_moe (include/ttl_moe.h) for Python callers.
+
+The product is the C ABI and the CUDA kernels behind it; this module is the
+thin Python mirror that tt-lab-style Python tooling, the tests and bench.py use.
+It loads ``tt-lab_b200/lib/libttl_moe.so`` and raises if the library is missing:
+there is no Python or CPU fallback for any compute call.
+
+Method names follow tt-lab's model interface: ``moe`` is GptOssModel::moe
+(src/model.cpp:292-338), ``moe_batch`` is GptOssModel::moe_batch
+(src/model.cpp:340-461), and failures raise RuntimeError with the library's
+message, as tt-lab raises std::runtime_error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+
+import numpy as np
+
+from . import synth  # noqa: F401  (re-exported helper module)
+
+DIM = 2880
+TOPK = 4
+BLOCK_BYTES = 17
+GGUF_MATRIX_BYTES = DIM * (DIM // 32) * BLOCK_BYTES  # 4,406,400
+NCCL_ID_BYTES = 128
+TTQ_FORMAT_MXFP4_GPU = 6
+
+TTL_OK = 0
+TTL_ERR_ARGUMENT = -1
+TTL_ERR_CUDA = -2
+TTL_ERR_STATE = -3
+TTL_ERR_NCCL = -4
+TTL_ERR_DEVICE = -5
+TTL_ERR_UNSUPPORTED = -6
+TTL_ERR_IO = -7
+
+_HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = pathlib.Path(os.environ.get("TTL_MOE_LIB", _HERE.parent.parent / "lib" / "libttl_moe.so"))
+HEADER_PATH = _HERE.parent.parent.parent / "include" / "ttl_moe.h"
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("experts", ctypes.c_uint32),
+        ("layers", ctypes.c_uint32),
+        ("max_tokens", ctypes.c_uint32),
+        ("device", ctypes.c_int32),
+        ("rank", ctypes.c_uint32),
+        ("world", ctypes.c_uint32),
+        ("nccl_id", ctypes.c_void_p),
+        ("flags", ctypes.c_uint32),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    """The loaded libttl_moe (raises OSError when it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise OSError(f"libttl_moe not built: {LIB_PATH} (run `make -C tt-lab_b200`)")
+    L = ctypes.CDLL(str(LIB_PATH))
+    vp, sz, i32, u32, u64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64
+    fp = ctypes.c_void_p
+    sig = {
+        "ttl_moe_abi_version": (i32, []),
+        "ttl_moe_last_error": (ctypes.c_char_p, [vp]),
+        "ttl_moe_nccl_id": (i32, [vp]),
+        "ttl_moe_create": (i32, [ctypes.POINTER(Config), ctypes.POINTER(vp)]),
+        "ttl_moe_destroy": (None, [vp]),
+        "ttl_moe_upload_layer": (i32, [vp, i32, fp, fp, vp, fp, vp, fp, vp, fp]),
+        "ttl_moe_upload_norm": (i32, [vp, i32, fp]),
+        "ttl_moe_decode": (i32, [vp, i32, fp, fp, vp, fp]),
+        "ttl_moe_prefill": (i32, [vp, i32, fp, sz, fp, vp, fp]),
+        "ttl_moe_forward": (i32, [vp, i32, i32, fp, fp, sz]),
+        "ttl_moe_decode_async": (i32, [vp, i32, fp, fp, vp, fp]),
+        "ttl_moe_prefill_async": (i32, [vp, i32, fp, sz, fp, vp, fp]),
+        "ttl_moe_forward_async": (i32, [vp, i32, i32, fp, fp, sz]),
+        "ttl_moe_sync": (i32, [vp]),
+        "ttl_moe_stream": (vp, [vp]),
+        "ttl_moe_counters": (i32, [vp, ctypes.POINTER(u64), sz]),
+        "ttl_moe_profile": (i32, [vp, i32]),
+        "ttl_moe_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float), sz]),
+        "ttl_packed_bytes": (sz, [sz]),
+        "ttl_pack_mxfp4": (i32, [vp, sz, vp, i32]),
+        "ttl_unpack_mxfp4": (i32, [vp, sz, vp, i32]),
+        "ttl_ttq_open": (i32, [ctypes.c_char_p, u32, u32, u32, u32, ctypes.POINTER(vp)]),
+        "ttl_ttq_add": (i32, [vp, ctypes.c_char_p, u32, u32, ctypes.POINTER(u64), vp, u64]),
+        "ttl_ttq_finish": (i32, [vp]),
+        "ttl_ttq_close": (None, [vp]),
+        "ttl_synth_mxfp4": (i32, [vp, sz, u64, u64, u32, u32]),
+        "ttl_synth_normal": (i32, [vp, sz, u64, u64, ctypes.c_float, ctypes.c_float]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def last_error(handle=None) -> str:
+    msg = lib().ttl_moe_last_error(handle)
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, handle=None):
+    if rc != TTL_OK:
+        raise RuntimeError(f"cuda moe ({rc}): {last_error(handle)}")
+
+
+def _ptr(a):
+    """Address of a numpy array, a torch tensor, or an int device pointer."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        if not a.flags["C_CONTIGUOUS"]:
+            raise ValueError("array must be C-contiguous")
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        if not a.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return a.data_ptr()
+    raise TypeError(f"unsupported buffer type {type(a)}")
+
+
+def nccl_id() -> bytes:
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    check(lib().ttl_moe_nccl_id(buf))
+    return buf.raw
+
+
+class MoE:
+    """One ttl_moe handle: one GPU, one expert-parallel rank."""
+
+    def __init__(self, experts=32, layers=1, max_tokens=0, device=-1, rank=0, world=1, nccl_id_bytes=None):
+        self._id = ctypes.create_string_buffer(nccl_id_bytes, NCCL_ID_BYTES) if nccl_id_bytes else None
+        cfg = Config(experts, layers, max_tokens, device, rank, world,
+                     ctypes.cast(self._id, ctypes.c_void_p) if self._id is not None else None, 0)
+        h = ctypes.c_void_p()
+        check(lib().ttl_moe_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+        self.experts, self.layers, self.max_tokens = experts, layers, max_tokens
+        self.rank, self.world = rank, world
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().ttl_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def _check(self, rc):
+        check(rc, self.h)
+
+    def upload_layer(self, layer, t):
+        """Binds layer `layer` from a dict of GGUF tensors (host or device)."""
+        self._check(lib().ttl_moe_upload_layer(
+            self.h, layer, _ptr(t["router_w"]), _ptr(t["router_b"]), _ptr(t["gate_w"]), _ptr(t["gate_b"]),
+            _ptr(t["up_w"]), _ptr(t["up_b"]), _ptr(t["down_w"]), _ptr(t["down_b"])))
+        if t.get("norm_w") is not None:
+            self._check(lib().ttl_moe_upload_norm(self.h, layer, _ptr(t["norm_w"])))
+
+    def moe(self, layer, x):
+        """GptOssModel::moe on host f32 [2880]; returns (out, top4 idx, top4 weights)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(DIM, np.float32)
+        idx = np.empty(TOPK, np.int32)
+        w = np.empty(TOPK, np.float32)
+        self._check(lib().ttl_moe_decode(self.h, layer, _ptr(x), _ptr(out), _ptr(idx), _ptr(w)))
+        return out, idx, w
+
+    def moe_batch(self, layer, x):
+        """GptOssModel::moe_batch on host f32 [T, 2880]; returns (out, idx [T,4], w [T,4])."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, DIM)
+        T = x.shape[0]
+        out = np.empty((T, DIM), np.float32)
+        idx = np.empty((T, TOPK), np.int32)
+        w = np.empty((T, TOPK), np.float32)
+        self._check(lib().ttl_moe_prefill(self.h, layer, _ptr(x), T, _ptr(out), _ptr(idx), _ptr(w)))
+        return out, idx, w
+
+    def forward(self, begin, end, x):
+        """RMSNorm -> MoE -> residual through layers [begin, end) for host x [T, 2880]."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, DIM)
+        y = np.empty_like(x)
+        self._check(lib().ttl_moe_forward(self.h, begin, end, _ptr(x), _ptr(y), x.shape[0]))
+        return y
+
+    def decode_async(self, layer, x, out, idx=None, w=None):
+        self._check(lib().ttl_moe_decode_async(self.h, layer, _ptr(x), _ptr(out), _ptr(idx), _ptr(w)))
+
+    def prefill_async(self, layer, x, tokens, out, idx=None, w=None):
+        self._check(lib().ttl_moe_prefill_async(self.h, layer, _ptr(x), tokens, _ptr(out), _ptr(idx), _ptr(w)))
+
+    def forward_async(self, begin, end, x, y, tokens):
+        self._check(lib().ttl_moe_forward_async(self.h, begin, end, _ptr(x), _ptr(y), tokens))
+
+    def forward_host(self, begin, end, x, y, tokens):
+        """ttl_moe_forward on caller-owned host buffers (pinned or pageable)."""
+        self._check(lib().ttl_moe_forward(self.h, begin, end, _ptr(x), _ptr(y), tokens))
+
+    def sync(self):
+        self._check(lib().ttl_moe_sync(self.h))
+
+    def stream(self) -> int:
+        return lib().ttl_moe_stream(self.h) or 0
+
+    def profile(self, enable=True):
+        self._check(lib().ttl_moe_profile(self.h, 1 if enable else 0))
+
+    def kernel_ms(self):
+        """Mean [router, gate/up, down] kernel ms over the profiled layers."""
+        out = (ctypes.c_float * 3)()
+        self._check(lib().ttl_moe_kernel_ms(self.h, out, 3))
+        return {"router": out[0], "gateup": out[1], "down": out[2]}
+
+    def counters(self):
+        out = (ctypes.c_uint64 * 3)()
+        n = lib().ttl_moe_counters(self.h, out, 3)
+        vals = [int(out[i]) for i in range(n)]
+        return {"router_exact_reevals": vals[0], "prefill_reevals": vals[1], "launches": vals[2]}
+
+
+def packed_bytes(matrices: int) -> int:
+    return lib().ttl_packed_bytes(matrices)
+
+
+def pack_mxfp4(gguf, matrices, packed=None, device=0):
+    if packed is None:
+        packed = np.empty(packed_bytes(matrices), np.uint8)
+    check(lib().ttl_pack_mxfp4(_ptr(gguf), matrices, _ptr(packed), device))
+    return packed
+
+
+def unpack_mxfp4(packed, matrices, gguf=None, device=0):
+    if gguf is None:
+        gguf = np.empty(matrices * GGUF_MATRIX_BYTES, np.uint8)
+    check(lib().ttl_unpack_mxfp4(_ptr(packed), matrices, _ptr(gguf), device))
+    return gguf
+
+
+class TtqWriter:
+    """Atomic TTLBQNT1 writer (tt-lab src/requant.cpp:23-68, :415-504)."""
+
+    def __init__(self, path, model, layers, experts, tensor_count):
+        w = ctypes.c_void_p()
+        check(lib().ttl_ttq_open(str(path).encode(), model, layers, experts, tensor_count, ctypes.byref(w)))
+        self.w = w
+
+    def add(self, name, fmt, shape, payload):
+        payload = np.ascontiguousarray(payload)
+        shp = (ctypes.c_uint64 * 4)(*([int(s) for s in shape] + [0] * (4 - len(shape))))
+        check(lib().ttl_ttq_add(self.w, name.encode(), fmt, len(shape), shp, _ptr(payload), payload.nbytes))
+
+    def finish(self):
+        check(lib().ttl_ttq_finish(self.w))
+
+    def close(self):
+        if self.w:
+            lib().ttl_ttq_close(self.w)
+            self.w = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
