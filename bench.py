@@ -283,7 +283,13 @@ def main():
     value = tokens / (ms_step / 1e3)
     e2e_value = tokens * args.steps / e2e_s
     hbm_peak, peak_kind = peaks()
-    gateup_gbs = GATEUP_BYTES / (kms["gateup"] * 1e-3) / 1e9
+    if kms["persistent"]:
+        kernel = "decode_stack_kernel"
+        bytes_launch = LAYER_BYTES_20B * kms["steps"]
+    else:  # expert-parallel handles: the gate/up kernel of one layer
+        kernel = "decode_gateup_kernel"
+        bytes_launch = GATEUP_BYTES
+    kernel_gbs = bytes_launch / (kms["ms"] * 1e-3) / 1e9
     # numerical spot check of this run against the oracle (first token, layer 0)
     ok_note = None
 
@@ -321,15 +327,17 @@ def main():
             "hbm_gbs_step": LAYER_BYTES_20B * layers * value / 1e9,
             "roofline": {
                 "bound": "hbm",
-                "kernel": "decode_gateup_kernel",
-                "achieved": gateup_gbs,
+                "kernel": kernel,
+                "achieved": kernel_gbs,
                 "peak": hbm_peak,
                 "unit": "GB/s",
-                "frac": gateup_gbs / hbm_peak,
+                "frac": kernel_gbs / hbm_peak,
                 "peak_kind": peak_kind,
                 "traffic": None,
-                "bytes_per_launch": GATEUP_BYTES,
-                "kernel_ms": kms,
+                "bytes_per_launch": bytes_launch,
+                "bytes_per_token_layer": LAYER_BYTES_20B,
+                "launch_ms": kms["ms"],
+                "token_layers_per_launch": kms["steps"],
             },
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -139,11 +139,14 @@ void *ttl_moe_stream(ttl_moe *handle);
 int ttl_moe_counters(const ttl_moe *handle, uint64_t *out, size_t n);
 
 /* Kernel timing for benchmarks: with `enable` set, forward graphs captured
- * afterwards record CUDA events around the router, gate/up and down kernels of
- * every layer of their first token.  ttl_moe_kernel_ms() then returns the mean
- * duration in ms of [router, gate/up, down] over those layers from the last
- * completed replay.  No counterpart in tt-lab (it profiles with device cycle
- * stamps, src/tt_backend.cpp:2338-2380). */
+ * afterwards record CUDA events around their main decode kernel.
+ * ttl_moe_kernel_ms() then writes, for the last completed replay:
+ *   [0] duration in ms of one launch of the dominant decode kernel (the
+ *       persistent kernel, or for expert-parallel handles the gate/up kernel),
+ *   [1] (token, layer) steps that launch covered,
+ *   [2] 1 for the persistent kernel, 0 for the per-layer kernels.
+ * No counterpart in tt-lab (it profiles with device cycle stamps,
+ * src/tt_backend.cpp:2338-2380). */
 int ttl_moe_profile(ttl_moe *handle, int enable);
 int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
 

@@ -57,6 +57,45 @@ void launch_add(const float *residual, const float *moe, float *out, int n, cuda
 // GGUF -> packed layout on the device.
 void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream);
 
+// ---- persistent decode (decode_stack.cu) ----
+struct StackLayer {
+    const float *router_w;
+    const float *router_b;
+    const float *norm_w;
+    const uint8_t *gate;
+    const uint8_t *up;
+    const uint8_t *down;
+    const float *gate_b;
+    const float *up_b;
+    const float *down_b;
+};
+
+struct StackArgs {
+    const StackLayer *layers;  // device array indexed by layer
+    int layer_begin;
+    int layer_end;
+    const float *x;            // [tokens][2880] input (h in mode 0, residual x in mode 1)
+    float *y;                  // [tokens][2880] output
+    int tokens;
+    int mode;                  // 0: one plain MoE per token (h given); 1: RMSNorm + MoE + residual
+    int experts;
+    int expert_begin;
+    int expert_count;
+    double *acc;               // [2][129] router sums (f64), zeroed by the host before a launch
+    float *logits;             // [E] mode 0
+    float *bounds;             // [E] mode 0
+    float *hidden;             // [4][2880]
+    int32_t *top_idx;          // [4] selection of the last (token, layer)
+    float *top_w;              // [4]
+    unsigned *barrier;         // [2] arrival count (zeroed by the host), generation
+    uint32_t *status;
+    unsigned long long *counters;
+};
+
+size_t stack_smem_bytes();
+void configure_stack_kernel();
+cudaError_t launch_decode_stack(const StackArgs &args, int sms, cudaStream_t stream);
+
 // ---- prefill ----
 struct PrefillWork {
     float *logits;            // [T][E]

@@ -80,11 +80,20 @@ struct ttl_moe {
     unsigned long long *d_counters = nullptr;
     uint64_t launches = 0;
     ncclComm_t comm = nullptr;
-    std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;  // exec, kernels per replay
     bool use_graphs = true;
     bool profile = false;
     int profile_layers = 0;        // layers covered by the recorded events
     std::vector<cudaEvent_t> events;  // [layers][4]
+    // persistent decode kernel
+    bool use_stack = true;
+    StackLayer *d_layers = nullptr;   // [layers]
+    std::vector<StackLayer> host_layers;
+    double *d_acc = nullptr;          // [2][kMaxExperts + 1]
+    unsigned *d_barrier = nullptr;    // [2]
+    cudaEvent_t stack_ev[2] = {nullptr, nullptr};
+    bool stack_profiled = false;
+    int stack_steps = 0;              // (token, layer) steps of the profiled launch
 };
 
 namespace ttl {
@@ -233,7 +242,56 @@ int enqueue_decode_layer(ttl_moe *h, int layer, const float *x, int mode, const 
     return TTL_OK;
 }
 
+int push_layer_descriptor(ttl_moe *h, int layer) {
+    const LayerDev L = layer_view(h, layer);
+    StackLayer d{L.router_w, L.router_b, L.norm_w, L.gate, L.up, L.down, L.gate_b, L.up_b, L.down_b};
+    h->host_layers[size_t(layer)] = d;
+    TTL_TRY_CUDA(h, cudaMemcpy(h->d_layers + layer, &d, sizeof(d), cudaMemcpyHostToDevice));
+    return TTL_OK;
+}
+
+// One cooperative launch covering `tokens` tokens x layers [begin, end).
+int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size_t tokens, int mode) {
+    StackArgs a{};
+    a.layers = h->d_layers;
+    a.layer_begin = begin;
+    a.layer_end = end;
+    a.x = x;
+    a.y = y;
+    a.tokens = int(tokens);
+    a.mode = mode;
+    a.experts = int(h->cfg.experts);
+    a.expert_begin = h->expert_begin;
+    a.expert_count = h->expert_count;
+    a.acc = h->d_acc;
+    a.logits = h->dw.logits;
+    a.bounds = h->dw.bounds;
+    a.hidden = h->dw.hidden;
+    a.top_idx = h->dw.top_idx;
+    a.top_w = h->dw.top_w;
+    a.barrier = h->d_barrier;
+    a.status = h->d_status;
+    a.counters = h->d_counters;
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
+    const bool prof = h->profile && mode == 1;
+    if (prof) {
+        TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
+    }
+    TTL_TRY_CUDA(h, launch_decode_stack(a, h->sms, h->stream));
+    if (prof) {
+        TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[1], h->stream, cudaEventRecordExternal));
+        h->stack_profiled = true;
+        h->stack_steps = int(tokens) * (end - begin);
+    }
+    h->launches += 1;
+    return TTL_OK;
+}
+
 int enqueue_forward(ttl_moe *h, int begin, int end, const float *x, float *y, size_t tokens) {
+    if (h->use_stack && h->cfg.world == 1 && end > begin) {
+        return enqueue_stack(h, begin, end, x, y, tokens, 1);
+    }
     for (size_t t = 0; t < tokens; ++t) {
         const float *cur = x + t * kDim;
         float *dst = y + t * kDim;
@@ -384,6 +442,9 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     h->layers.resize(c.layers);
     const char *no_graph = std::getenv("TTL_MOE_NO_GRAPHS");
     h->use_graphs = !(no_graph && no_graph[0] == '1');
+    const char *no_stack = std::getenv("TTL_MOE_NO_STACK");
+    h->use_stack = !(no_stack && no_stack[0] == '1');
+    h->host_layers.resize(c.layers);
 
     auto bail = [&](int rc) {
         std::string msg = h->error;
@@ -399,6 +460,10 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     }
     configure_decode_kernels();
     configure_prefill_kernels();
+    configure_stack_kernel();
+    if (cudaEventCreate(&h->stack_ev[0]) != cudaSuccess || cudaEventCreate(&h->stack_ev[1]) != cudaSuccess) {
+        return bail(fail(h, TTL_ERR_CUDA, "cudaEventCreate failed"));
+    }
 
     const size_t E = c.experts;
     const size_t T = std::max<uint32_t>(c.max_tokens, 1u);
@@ -416,6 +481,9 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->dw.arrive, 1);
     rc = rc ? rc : alloc_n(h, &h->d_x, T * kDim);
     rc = rc ? rc : alloc_n(h, &h->d_y, T * kDim);
+    rc = rc ? rc : alloc_n(h, &h->d_layers, c.layers);
+    rc = rc ? rc : alloc_n(h, &h->d_acc, 2 * (kMaxExperts + 1));
+    rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
     if (rc) {
         return bail(rc);
     }
@@ -445,7 +513,9 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->d_counters, 0, 4 * sizeof(unsigned long long)) != cudaSuccess ||
         cudaMemset(h->dw.arrive, 0, sizeof(unsigned int)) != cudaSuccess ||
         cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
-        cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess) {
+        cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
+        cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_layers, 0, c.layers * sizeof(StackLayer)) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
     }
     if (c.world > 1) {
@@ -470,11 +540,16 @@ void ttl_moe_destroy(ttl_moe *h) {
         cudaStreamSynchronize(h->stream);
     }
     for (auto &g : h->graphs) {
-        cudaGraphExecDestroy(g.second);
+        cudaGraphExecDestroy(g.second.first);
     }
     h->graphs.clear();
     for (cudaEvent_t e : h->events) {
         cudaEventDestroy(e);
+    }
+    for (cudaEvent_t e : h->stack_ev) {
+        if (e) {
+            cudaEventDestroy(e);
+        }
     }
     if (h->comm) {
         ncclCommDestroy(h->comm);
@@ -547,7 +622,7 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
         TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
     }
     s.uploaded = true;
-    return TTL_OK;
+    return push_layer_descriptor(h, layer);
 }
 
 int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
@@ -566,7 +641,7 @@ int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
         return rc;
     }
     TTL_TRY_CUDA(h, cudaMemcpy(s.norm_w, norm_w, kDim * sizeof(float), cudaMemcpyDefault));
-    return TTL_OK;
+    return push_layer_descriptor(h, layer);
 }
 
 int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
@@ -578,7 +653,11 @@ int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int3
     }
     int rc = check_layer(h, layer);
     rc = rc ? rc : set_device(h);
-    rc = rc ? rc : enqueue_decode_layer(h, layer, x, 0, nullptr, out);
+    if (!rc && h->use_stack && h->cfg.world == 1) {
+        rc = enqueue_stack(h, layer, layer + 1, x, out, 1, 0);
+    } else if (!rc) {
+        rc = enqueue_decode_layer(h, layer, x, 0, nullptr, out);
+    }
     if (rc) {
         return rc;
     }
@@ -606,7 +685,11 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
         return rc;
     }
     TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    rc = enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
+    if (h->use_stack && h->cfg.world == 1) {
+        rc = enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0);
+    } else {
+        rc = enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
+    }
     if (rc) {
         return rc;
     }
@@ -732,11 +815,12 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
         if (inst != cudaSuccess) {
             return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
         }
+        const uint64_t per_replay = h->launches - launches;
         h->launches = launches;  // counted per replay below
-        found = h->graphs.emplace(key, exec).first;
+        found = h->graphs.emplace(key, std::make_pair(exec, per_replay)).first;
     }
-    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second, h->stream));
-    h->launches += tokens * size_t(layer_end - layer_begin) * (h->cfg.world > 1 ? 4 : 3);
+    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.first, h->stream));
+    h->launches += found->second.second;
     return TTL_OK;
 }
 
@@ -792,19 +876,26 @@ int ttl_moe_kernel_ms(ttl_moe *h, float *ms, size_t n) {
     if (!h || !ms) {
         return fail(h, TTL_ERR_ARGUMENT, "null argument");
     }
-    if (h->profile_layers == 0) {
+    float out[3] = {0.0f, 0.0f, 0.0f};
+    if (h->stack_profiled) {
+        TTL_TRY_CUDA(h, cudaEventElapsedTime(&out[0], h->stack_ev[0], h->stack_ev[1]));
+        out[1] = float(h->stack_steps);
+        out[2] = 1.0f;
+    } else if (h->profile_layers > 0) {
+        double sum = 0.0;
+        for (int l = 0; l < h->profile_layers; ++l) {
+            float v = 0.0f;
+            TTL_TRY_CUDA(h, cudaEventElapsedTime(&v, h->events[size_t(4 * l + 1)], h->events[size_t(4 * l + 2)]));
+            sum += v;
+        }
+        out[0] = float(sum / h->profile_layers);
+        out[1] = 1.0f;
+        out[2] = 0.0f;
+    } else {
         return fail(h, TTL_ERR_STATE, "no profiled forward graph has run");
     }
-    double sum[3] = {0, 0, 0};
-    for (int l = 0; l < h->profile_layers; ++l) {
-        for (int k = 0; k < 3; ++k) {
-            float v = 0.0f;
-            TTL_TRY_CUDA(h, cudaEventElapsedTime(&v, h->events[size_t(4 * l + k)], h->events[size_t(4 * l + k + 1)]));
-            sum[k] += v;
-        }
-    }
     for (size_t k = 0; k < n && k < 3; ++k) {
-        ms[k] = float(sum[k] / h->profile_layers);
+        ms[k] = out[k];
     }
     return TTL_OK;
 }

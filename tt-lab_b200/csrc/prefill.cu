@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
     }
     __syncthreads();
     for (int i = threadIdx.x; i < tokens * kTopK; i += blockDim.x) {
+        w.pair_slot[i] = -1;
         const int e = w.top_idx[i];
         if (e < 0 || e >= experts) {
             set_status(w.status, kStatusBadExpert);
@@ -120,7 +121,6 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
         if (le >= 0 && le < expert_count) {
             atomicAdd(&counts[le], 1);
         }
-        w.pair_slot[i] = -1;
     }
     __syncthreads();
     if (threadIdx.x == 0) {

@@ -227,10 +227,10 @@ class MoE:
         self._check(lib().ttl_moe_profile(self.h, 1 if enable else 0))
 
     def kernel_ms(self):
-        """Mean [router, gate/up, down] kernel ms over the profiled layers."""
+        """Duration of the last profiled decode-kernel launch: (ms, steps, persistent)."""
         out = (ctypes.c_float * 3)()
         self._check(lib().ttl_moe_kernel_ms(self.h, out, 3))
-        return {"router": out[0], "gateup": out[1], "down": out[2]}
+        return {"ms": out[0], "steps": int(out[1]), "persistent": bool(out[2])}
 
     def counters(self):
         out = (ctypes.c_uint64 * 3)()
