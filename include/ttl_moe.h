@@ -150,6 +150,12 @@ int ttl_moe_counters(const ttl_moe *handle, uint64_t *out, size_t n);
 int ttl_moe_profile(ttl_moe *handle, int enable);
 int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
 
+/* One expert matrix on the tensor cores: y = bias + W x, tt-lab's
+ * matvec_add_mxfp4_2880 (src/tensor.cpp:239-304).  packed: one 2880 x 2880
+ * matrix in the GPU layout (ttl_pack_mxfp4); bias, x, y: f32 [2880].  Device
+ * pointers on `device`; synchronous. */
+int ttl_matvec_mxfp4(const void *packed, const float *bias, const float *x, float *y, int device);
+
 /* ---- GPU weight-layout packer (requant) -------------------------------- */
 
 /* Bytes of the packed layout (TTQ format TTL_TTQ_FORMAT_MXFP4_GPU) of

@@ -90,7 +90,18 @@ struct StackArgs {
     unsigned *barrier;         // [2] arrival count (zeroed by the host), generation
     uint32_t *status;
     unsigned long long *counters;
+    // tensor-core decode workspace
+    float *part_gu;            // [4 * 45 tiles][16 slots][128] gate/up tile partials
+    float *part_dn;            // [23 tiles][16 slots][128] down tile partials
+    unsigned *cnt_gu;          // [4 * 45] contributor counters (zeroed by the host)
+    unsigned *cnt_dn;          // [23]
+    uint8_t *bdown;            // [4][180][8][16] down B operand: E4M3 terms of w * hidden
+    uint8_t *sfb_down;         // [4][90][4] their E8M0 scales
 };
+
+size_t decode_tc_smem_bytes();
+void configure_decode_tc();
+cudaError_t launch_decode_tc(const StackArgs &args, int sms, cudaStream_t stream);
 
 size_t stack_smem_bytes();
 void configure_stack_kernel();

@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "kernels.h"
+#include "nccl_dl.h"
 
 namespace ttl {
 void configure_decode_kernels();
@@ -87,6 +88,12 @@ struct ttl_moe {
     std::vector<cudaEvent_t> events;  // [layers][4]
     // persistent decode kernel
     bool use_stack = true;
+    bool use_tc = true;               // tensor-core persistent kernel (else the CUDA-core one)
+    float *d_part_gu = nullptr;
+    float *d_part_dn = nullptr;
+    unsigned *d_cnt = nullptr;        // [4 * 45 + 23]
+    uint8_t *d_bdown = nullptr;
+    uint8_t *d_sfb_down = nullptr;
     StackLayer *d_layers = nullptr;   // [layers]
     std::vector<StackLayer> host_layers;
     double *d_acc = nullptr;          // [2][kMaxExperts + 1]
@@ -185,7 +192,8 @@ int set_device(ttl_moe *h) {
 
 int nccl_check(ttl_moe *h, ncclResult_t r, const char *what) {
     if (r != ncclSuccess) {
-        return fail(h, TTL_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+        const NcclApi *api = nccl(nullptr);
+        return fail(h, TTL_ERR_NCCL, std::string(what) + ": " + (api ? api->GetErrorString(r) : "nccl unavailable"));
     }
     return TTL_OK;
 }
@@ -195,7 +203,8 @@ int allreduce(ttl_moe *h, float *buf, size_t n) {
     if (h->cfg.world <= 1) {
         return TTL_OK;
     }
-    return nccl_check(h, ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, h->comm, h->stream), "ncclAllReduce");
+    return nccl_check(h, nccl(nullptr)->AllReduce(buf, buf, n, ncclFloat32, ncclSum, h->comm, h->stream),
+                      "ncclAllReduce");
 }
 
 // Enqueues one decode layer: router -> gate/up -> down (+ combine, residual).
@@ -272,13 +281,24 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.barrier = h->d_barrier;
     a.status = h->d_status;
     a.counters = h->d_counters;
+    a.part_gu = h->d_part_gu;
+    a.part_dn = h->d_part_dn;
+    a.cnt_gu = h->d_cnt;
+    a.cnt_dn = h->d_cnt + 4 * 45;
+    a.bdown = h->d_bdown;
+    a.sfb_down = h->d_sfb_down;
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned), h->stream));
     const bool prof = h->profile && mode == 1;
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
     }
-    TTL_TRY_CUDA(h, launch_decode_stack(a, h->sms, h->stream));
+    if (h->use_tc) {
+        TTL_TRY_CUDA(h, launch_decode_tc(a, h->sms, h->stream));
+    } else {
+        TTL_TRY_CUDA(h, launch_decode_stack(a, h->sms, h->stream));
+    }
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[1], h->stream, cudaEventRecordExternal));
         h->stack_profiled = true;
@@ -374,10 +394,15 @@ int ttl_moe_nccl_id(void *id_out) {
     if (!id_out) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null id buffer");
     }
+    const char *why = nullptr;
+    const NcclApi *api = nccl(&why);
+    if (!api) {
+        return fail(nullptr, TTL_ERR_NCCL, std::string("NCCL unavailable: ") + why);
+    }
     ncclUniqueId id;
-    const ncclResult_t r = ncclGetUniqueId(&id);
+    const ncclResult_t r = api->GetUniqueId(&id);
     if (r != ncclSuccess) {
-        return fail(nullptr, TTL_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+        return fail(nullptr, TTL_ERR_NCCL, std::string("ncclGetUniqueId: ") + api->GetErrorString(r));
     }
     static_assert(sizeof(id) == TTL_MOE_NCCL_ID_BYTES, "ncclUniqueId size");
     std::memcpy(id_out, &id, sizeof(id));
@@ -444,6 +469,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     h->use_graphs = !(no_graph && no_graph[0] == '1');
     const char *no_stack = std::getenv("TTL_MOE_NO_STACK");
     h->use_stack = !(no_stack && no_stack[0] == '1');
+    const char *simt = std::getenv("TTL_MOE_SIMT_DECODE");
+    h->use_tc = !(simt && simt[0] == '1');
     h->host_layers.resize(c.layers);
 
     auto bail = [&](int rc) {
@@ -461,6 +488,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     configure_decode_kernels();
     configure_prefill_kernels();
     configure_stack_kernel();
+    configure_decode_tc();
     if (cudaEventCreate(&h->stack_ev[0]) != cudaSuccess || cudaEventCreate(&h->stack_ev[1]) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "cudaEventCreate failed"));
     }
@@ -484,6 +512,11 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_layers, c.layers);
     rc = rc ? rc : alloc_n(h, &h->d_acc, 2 * (kMaxExperts + 1));
     rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
+    rc = rc ? rc : alloc_n(h, &h->d_part_gu, size_t(4 * 45) * 16 * 128);
+    rc = rc ? rc : alloc_n(h, &h->d_part_dn, size_t(23) * 16 * 128);
+    rc = rc ? rc : alloc_n(h, &h->d_cnt, 4 * 45 + 23);
+    rc = rc ? rc : alloc_n(h, &h->d_bdown, size_t(4) * 180 * 8 * 16);
+    rc = rc ? rc : alloc_n(h, &h->d_sfb_down, size_t(4) * 90 * 4);
     if (rc) {
         return bail(rc);
     }
@@ -515,16 +548,23 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_bdown, 0, size_t(4) * 180 * 8 * 16) != cudaSuccess ||
         cudaMemset(h->d_layers, 0, c.layers * sizeof(StackLayer)) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
     }
     if (c.world > 1) {
+        const char *why = nullptr;
+        const NcclApi *api = nccl(&why);
+        if (!api) {
+            return bail(fail(h, TTL_ERR_NCCL, std::string("NCCL unavailable: ") + why));
+        }
         ncclUniqueId id;
         std::memcpy(&id, c.nccl_id, sizeof(id));
-        const ncclResult_t r = ncclCommInitRank(&h->comm, int(c.world), id, int(c.rank));
+        const ncclResult_t r = api->CommInitRank(&h->comm, int(c.world), id, int(c.rank));
         if (r != ncclSuccess) {
             h->comm = nullptr;
-            return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(r)));
+            return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + api->GetErrorString(r)));
         }
     }
     *handle_out = h;
@@ -552,7 +592,7 @@ void ttl_moe_destroy(ttl_moe *h) {
         }
     }
     if (h->comm) {
-        ncclCommDestroy(h->comm);
+        nccl(nullptr)->CommDestroy(h->comm);
     }
     for (void *p : h->allocations) {
         cudaFree(p);

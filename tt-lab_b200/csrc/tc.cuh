@@ -1,0 +1,188 @@
+// tc.cuh -- 5th-generation tensor core (tcgen05) building blocks for the
+// block-scaled MXFP4 x FP8 products of the MoE kernels.
+//
+// Operands (kind::mxf8f6f4, cta_group::1, M = 128):
+//   A = weights, E2M1 with one E8M0 scale per 32 K-elements (the MXFP4 data
+//       exactly as stored, no dequantisation): 16 elements per 16-byte
+//       shared-memory slot (8 packed bytes, 8 bytes of padding), K-major;
+//   B = activations as E4M3 "terms" with their own E8M0 scale per 32 K:
+//       x ~= t0 + t1 + t2 + t3, each term captures the residual of the ones
+//       before it (4 significant bits each), so 4 terms carry ~16 bits;
+//       terms are the N columns of B;
+//   D = f32 accumulators in tensor memory (lane = output row, column = term).
+// Shared-memory operands use the K-major no-swizzle canonical layout: core
+// matrices of 8 rows x 16 bytes (128 contiguous bytes); LBO is the byte
+// distance between K-adjacent core matrices, SBO between 8-row groups.
+// Scale factors live in tensor memory: per chunk of 4 K-blocks, 4 consecutive
+// 32-bit columns; column c + m1, byte k holds the scale of row m0 + 32*m1 for
+// K-block k, replicated in all four 32-lane quadrants.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ttl {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- tensor memory ----
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(cols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Warp-collective: this warp's 32 lanes, 4 consecutive columns from `taddr`.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t a) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(a) : "memory");
+}
+// Warp-collective: this warp's 32 lanes, 8 consecutive f32 columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float v[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        v[i] = __uint_as_float(r[i]);
+    }
+}
+
+// ---- mbarrier (bounded waits) ----
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    // suspend hint of 1 us per attempt
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+        : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` to complete; gives up after `limit` attempts of at
+// most ~1 us each (about 2 s) and returns false -- the caller records a
+// status bit and unwinds.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = 1u << 21) {
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait(bar, parity)) {
+            return true;
+        }
+    }
+    return false;
+}
+// Arrives on `bar` when all previously issued tcgen05.mma of this thread complete.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---- descriptors ----
+// K-major, no swizzle.  lbo/sbo in bytes (multiples of 16).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= uint64_t((saddr >> 4) & 0x3FFFu);
+    d |= uint64_t((lbo >> 4) & 0x3FFFu) << 16;
+    d |= uint64_t((sbo >> 4) & 0x3FFFu) << 32;
+    d |= uint64_t(1) << 46;  // descriptor version for tcgen05
+    // base offset 0, lbo mode 0, layout type 0 (no swizzle)
+    return d;
+}
+
+// Instruction descriptor: kind::mxf8f6f4, A = E2M1, B = E4M3, scales E8M0,
+// K-major A and B, M = 128, N = n.  sfa_id / sfb_id select the scale byte.
+__device__ __forceinline__ uint32_t instr_desc(uint32_t n, uint32_t sfa_id, uint32_t sfb_id) {
+    uint32_t d = 0;
+    d |= (sfb_id & 3u) << 4;
+    d |= 5u << 7;             // a_format = E2M1
+    d |= 0u << 10;            // b_format = E4M3
+    d |= (n >> 3) << 17;      // N >> 3
+    d |= 1u << 23;            // scale format E8M0
+    d |= (128u >> 4) << 24;   // M >> 4
+    d |= (sfa_id & 3u) << 29;
+    return d;
+}
+
+// D (+)= A x B with block scales; issued by one thread.
+__device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                    uint32_t sfa_tmem, uint32_t sfb_tmem, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        :
+        : "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+}
+
+// ---- activation terms ----
+// Splits the 32 values of one K-block (one per lane) into kTerms E4M3 terms
+// with one E8M0 scale each: returns this lane's term bytes packed in a u32
+// (term j in byte j) and writes the scale bytes to scales (lane 0's view).
+template <int kTerms>
+__device__ __forceinline__ uint32_t split_terms(float v, uint32_t &scale_bytes) {
+    uint32_t bytes = 0;
+    scale_bytes = 0;
+    float r = v;
+#pragma unroll
+    for (int j = 0; j < kTerms; ++j) {
+        float m = fabsf(r);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        }
+        // scale 2^(E-7) where 2^E <= m < 2^(E+1): m / scale in [128, 256) <= 448
+        int e8 = 127;
+        if (m > 0.0f && m == m) {
+            const int E = int((__float_as_uint(m) >> 23) & 0xFF) - 127;  // m normal here
+            e8 = E - 7 + 127;
+            e8 = e8 < 1 ? 1 : (e8 > 253 ? 253 : e8);
+        }
+        const float inv = __uint_as_float(uint32_t(254 - e8) << 23);  // 2^-(e8-127), exact
+        const float sc = __uint_as_float(uint32_t(e8) << 23);
+        const __nv_fp8_e4m3 q(__fmul_rn(r, inv));
+        const float back = __fmul_rn(float(q), sc);
+        r = __fsub_rn(r, back);
+        bytes |= uint32_t(q.__x) << (8 * j);
+        scale_bytes |= uint32_t(e8) << (8 * j);
+    }
+    return bytes;
+}
+
+} // namespace tc
+} // namespace ttl

@@ -86,6 +86,7 @@ def lib():
         "ttl_moe_counters": (i32, [vp, ctypes.POINTER(u64), sz]),
         "ttl_moe_profile": (i32, [vp, i32]),
         "ttl_moe_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float), sz]),
+        "ttl_matvec_mxfp4": (i32, [vp, vp, vp, vp, i32]),
         "ttl_packed_bytes": (sz, [sz]),
         "ttl_pack_mxfp4": (i32, [vp, sz, vp, i32]),
         "ttl_unpack_mxfp4": (i32, [vp, sz, vp, i32]),
@@ -248,6 +249,12 @@ def pack_mxfp4(gguf, matrices, packed=None, device=0):
         packed = np.empty(packed_bytes(matrices), np.uint8)
     check(lib().ttl_pack_mxfp4(_ptr(gguf), matrices, _ptr(packed), device))
     return packed
+
+
+def matvec_mxfp4(packed, bias, x, y, device=0):
+    """y = bias + W x on the tensor cores (device tensors)."""
+    check(lib().ttl_matvec_mxfp4(_ptr(packed), _ptr(bias), _ptr(x), _ptr(y), device))
+    return y
 
 
 def unpack_mxfp4(packed, matrices, gguf=None, device=0):
