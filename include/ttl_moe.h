@@ -148,6 +148,15 @@ int ttl_moe_counters(const ttl_moe *handle, uint64_t *out, size_t n);
  * No counterpart in tt-lab (it profiles with device cycle stamps,
  * src/tt_backend.cpp:2338-2380). */
 int ttl_moe_profile(ttl_moe *handle, int enable);
+
+/* Phase timeline of the persistent decode kernel, the counterpart of tt-lab's
+ * firmware stage stamps (src/tt_backend.cpp:2338-2380): with steps > 0, later
+ * launches record %globaltimer (ns) at 10 points of each of the first `steps`
+ * (token, layer) steps: 0 layer start, 1 selection done, 2 gate/up operands
+ * ready, 3 CTA 0 gate/up done, 4 after the barrier, 5 down operands ready,
+ * 6 CTA 0 down done, 7 after the barrier, 8/9 latest gate/up and down end
+ * over all CTAs.  With out != NULL, waits and copies steps*10 stamps. */
+int ttl_moe_trace(ttl_moe *handle, int steps, uint64_t *out);
 int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
 
 /* One expert matrix on the tensor cores: y = bias + W x, tt-lab's

@@ -47,7 +47,7 @@ constexpr int kTerms = 4;
 constexpr int kN = 8;
 constexpr int kChunks = kDim / 16;            // 180 16-element K-chunks
 constexpr int kSfChunks = (kBlocks + 3) / 4;  // 23 scale chunks of 4 K-blocks
-constexpr int kStages = 5;
+constexpr int kStages = 9;
 constexpr int kStageKB = 4;                   // K-blocks per stage
 constexpr int kEpiWarps = 4;                  // warps 0-3
 constexpr int kLoadWarps = 4;                 // warps 4-7
@@ -56,17 +56,22 @@ constexpr int kGateTiles = kDim / 64;         // 45 tiles of 64 gate + 64 up row
 constexpr int kDownTiles = (kDim + 127) / 128;  // 23 tiles of 128 rows
 constexpr int kMaxSlots = 16;                 // contributors per tile (checked)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD = 0;                 // 2 x 8 columns
-constexpr uint32_t kColSfa = 16;              // kStages x 4 columns
-constexpr uint32_t kColSfbG = 36;             // 23 scale chunks x 4 columns
-constexpr uint32_t kColSfbD = 128;            // 4 experts x 23 chunks x 4 columns (ends at 496)
+constexpr uint32_t kColD = 0;                                  // 2 x 8 columns
+constexpr uint32_t kColSfa = 16;                               // kStages x 4 columns
+constexpr uint32_t kColSfbG = kColSfa + 4 * kStages;           // 23 scale chunks x 4 columns
+constexpr uint32_t kColSfbD = kColSfbG + 4 * ((kBlocks + 3) / 4);  // kDownSlots x 23 x 4 columns
+constexpr int kDownSlots = 2;                 // down-projection experts a CTA touches (checked)
+static_assert(kColSfbD + 4 * kDownSlots * ((kBlocks + 3) / 4) <= kTmemCols, "tensor memory map");
 constexpr unsigned long long kSpinLimit = 1ull << 22;  // x ~0.6 us per poll: ~2.5 s
 
 struct alignas(128) Smem {
     uint8_t a[kStages][16][2 * kStageKB][8][16];  // A stages: [row group][chunk][row][16 B]
+    uint8_t sfa[kStages][32][4][4];               // A scales per stage: [m0][m1][K-block], rows m0 + 32*m1
     uint8_t bgu[kChunks][kN][16];                 // gate/up B: h terms
-    uint8_t bdown[kTopK][kChunks][kN][16];        // down B: w * hidden terms per expert slot
+    uint8_t bdown[kDownSlots][kChunks][kN][16];   // down B: w * hidden terms of this CTA's experts
     uint8_t sfbg[kBlocks][kTerms];                // gate/up B term scales
+    uint8_t sfbd[kDownSlots][kBlocks][kTerms];    // down B term scales
+    int dslot[kTopK];                             // expert slot -> bdown slot, -1 if unused
     float xch[64];                                // up values for the SwiGLU exchange
     float part[128];                              // scratch for the tile reduction
     float logit[kMaxExperts];
@@ -183,6 +188,25 @@ __device__ bool grid_barrier(unsigned *bar, unsigned &gen, uint32_t *status, Sme
     return s.go != 0;
 }
 
+__device__ __forceinline__ unsigned long long globaltimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Stage stamps for profiling (thread 0 of CTA 0; point 9 = latest phase-B end over CTAs).
+__device__ __forceinline__ void stamp(const StackArgs &a, int step, int point) {
+    if (a.trace && step < a.trace_steps && threadIdx.x == 0) {
+        const unsigned long long t = globaltimer();
+        if (blockIdx.x == 0) {
+            a.trace[size_t(step) * kTracePoints + point] = t;
+        }
+        if (point == 3 || point == 6) {
+            atomicMax(&a.trace[size_t(step) * kTracePoints + (point == 3 ? 8 : 9)], t);
+        }
+    }
+}
+
 // Contiguous unit range of CTA c out of g over `units` units.
 __device__ __forceinline__ int range_lo(int c, int g, int units) {
     return int((long long)c * units / g);
@@ -213,85 +237,120 @@ struct Ctx {
     uint32_t tbase;
 };
 
-// A source row of stage row i for (phase, tile, K-unit).
-__device__ __forceinline__ const uint8_t *a_matrix(const Ctx &c, const Phase &p, int tile, int ku, int i, int &row) {
-    const Smem &s = *c.s;
-    if (p.kind == 0) {
-        const int q = tile / kGateTiles;
-        const int j = tile - q * kGateTiles;
-        const int le = s.local[s.slot_of[q]];
-        row = 64 * j + (i & 63);
-        return (i < 64 ? c.L->gate : c.L->up) + size_t(le) * kPackedMatrixBytes;
-    }
-    const int q = ku / kBlocks;
-    const int le = s.local[s.slot_of[q]];
-    row = 128 * tile + i;
-    return c.L->down + size_t(le) * kPackedMatrixBytes;
+// Stages are aligned to scale chunks: K-blocks [4g, 4g+4) of one matrix (the
+// last chunk of a row has 2), clipped to the segment.  Returns the stage's
+// first K-unit offset within the tile and its K-block count.
+__device__ __forceinline__ int stage_len(const Phase &p, int ku, int seg_left) {
+    const int kb = ku % kBlocks;
+    const int chunk_end = min((kb & ~3) + 4, kBlocks);
+    return min(chunk_end - kb, seg_left);
 }
 
 // ---- loader warps (4-7) ----
+// Thread lt copies chunk lt & 7 of rows (lt >> 3) + 16k, k = 0..7, of every
+// stage, and the scale word of row lt.  Row addresses are formed once per
+// segment (and per expert change in the down phase) and kept in registers.
 __device__ void run_loader(const Ctx &c, const Phase &p, Pipe &pp) {
     Smem &s = *c.s;
     const int lt = threadIdx.x - 32 * kEpiWarps;  // 0..127
-    const int q4 = (threadIdx.x >> 5) & 3;         // TMEM quadrant of this warp
-    const int lane = threadIdx.x & 31;
+    const int ch = lt & 7;
+    const int r_first = lt >> 3;
     const int units = p.tiles * p.kunits;
     const int u0 = range_lo(blockIdx.x, gridDim.x, units);
     const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
+    const uint8_t *gate = c.L->gate;
+    const uint8_t *up = c.L->up;
+    const uint8_t *down = c.L->down;
     int u = u0;
     while (u < u1) {
         const int tile = u / p.kunits;
         const int seg_end = min(u1, (tile + 1) * p.kunits);
+        int cur_q = -1;
+        const uint8_t *rowp[8];   // nibble rows of this thread (nullptr past the matrix)
+        const uint8_t *sfrow = nullptr;
         while (u < seg_end) {
             if (warp_aborted(s)) {
                 return;
             }
             const int ku0 = u - tile * p.kunits;
-            const int nkb = min(kStageKB, seg_end - u);
+            const int q = ku0 / kBlocks;
+            if (q != cur_q) {
+                cur_q = q;
+                if (p.kind == 0) {
+                    const int qq = tile / kGateTiles;
+                    const int j = tile - qq * kGateTiles;
+                    const size_t off = size_t(s.local[s.slot_of[qq]]) * kPackedMatrixBytes;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int i = r_first + 16 * k;
+                        rowp[k] = (i < 64 ? gate : up) + off + size_t(64 * j + (i & 63)) * kNibbleRowBytes;
+                    }
+                    sfrow = (lt < 64 ? gate : up) + off + kNibbleBytes + size_t(64 * j + (lt & 63)) * kScaleRowBytes;
+                } else {
+                    const uint8_t *m = down + size_t(s.local[s.slot_of[q]]) * kPackedMatrixBytes;
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int row = 128 * tile + r_first + 16 * k;
+                        rowp[k] = row < kDim ? m + size_t(row) * kNibbleRowBytes : nullptr;
+                    }
+                    const int row = 128 * tile + lt;
+                    sfrow = row < kDim ? m + kNibbleBytes + size_t(row) * kScaleRowBytes : nullptr;
+                }
+            }
+            const int nkb = stage_len(p, ku0, seg_end - u);
+            const int kb0 = ku0 % kBlocks;
             const uint32_t st = pp.stage % kStages;
             const uint32_t use = pp.stage / kStages;
             if (use > 0 && !warp_wait(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
                 return;
             }
-            // A: 128 rows x 2*nkb chunks of 8 packed bytes; thread -> (row, chunk)
-            for (int idx = lt; idx < 128 * 2 * kStageKB; idx += 128) {
-                const int i = idx >> 3;
-                const int ch = idx & 7;
-                const int j = ch >> 1;
-                if (j < nkb) {
-                    int row;
-                    const uint8_t *m = a_matrix(c, p, tile, ku0 + j, i, row);
-                    if (row < kDim) {
-                        const int kb = (ku0 + j) % kBlocks;
-                        cp_async8(&s.a[st][i >> 3][ch][i & 7][0],
-                                  m + size_t(row) * kNibbleRowBytes + size_t(kb) * 16 + (ch & 1) * 8);
+            const int j = (ch >> 1) - (kb0 & 3);  // K-block of the stage this thread's chunk belongs to
+            if (j >= 0 && j < nkb) {
+                const size_t koff = size_t(kb0 + j) * 16 + (ch & 1) * 8;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (rowp[k]) {
+                        const int i = r_first + 16 * k;
+                        cp_async8(&s.a[st][i >> 3][ch][i & 7][0], rowp[k] + koff);
                     }
                 }
+            }
+            if (sfrow) {
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(tc::smem_u32(&s.sfa[st][lt & 31][lt >> 5][0])),
+                             "l"(sfrow + (kb0 & ~3))
+                             : "memory");
             }
             cp_async_arrive(&s.full[st]);
-            // SFA: quadrant q4, thread m0 -> rows m0 + 32*m1, byte j = K-block j
-            uint32_t v[4];
-#pragma unroll
-            for (int m1 = 0; m1 < 4; ++m1) {
-                const int i = lane + 32 * m1;
-                uint32_t w = 0;
-                for (int j = 0; j < nkb; ++j) {
-                    int row;
-                    const uint8_t *m = a_matrix(c, p, tile, ku0 + j, i, row);
-                    if (row < kDim) {
-                        const int kb = (ku0 + j) % kBlocks;
-                        w |= uint32_t(__ldg(m + kNibbleBytes + size_t(row) * kScaleRowBytes + kb)) << (8 * j);
-                    }
-                }
-                v[m1] = w;
-            }
-            tc::tmem_st4(c.tbase + (uint32_t(32 * q4) << 16) + kColSfa + 4 * st, v[0], v[1], v[2], v[3]);
-            tc::wait_st();
-            tc::fence_before_sync();
-            mbar_arrive(&s.full[st]);
             ++pp.stage;
             u += nkb;
         }
+    }
+}
+
+// L2 prefetch (idle lanes of the MMA warp during gate/up): this CTA's
+// down-phase rows, so the down phase streams from L2.
+__device__ void prefetch_down(const Ctx &c, int kunits) {
+    const Smem &s = *c.s;
+    const int lane = threadIdx.x & 31;
+    const int units = kDownTiles * kunits;
+    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
+    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
+    for (int u = u0; u < u1;) {
+        const int tile = u / kunits;
+        const int ku = u - tile * kunits;
+        const int q = ku / kBlocks;
+        const int kb0 = ku % kBlocks;
+        const int kb1 = min(kBlocks, kb0 + (u1 - u));
+        const uint8_t *m = c.L->down + size_t(s.local[s.slot_of[q]]) * kPackedMatrixBytes;
+        for (int i = lane - 1; i < 128; i += 31) {
+            const int row = 128 * tile + i;
+            if (row < kDim) {
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(m + size_t(row) * kNibbleRowBytes + kb0 * 16),
+                             "r"(uint32_t((kb1 - kb0) * 16))
+                             : "memory");
+            }
+        }
+        u += kb1 - kb0;
     }
 }
 
@@ -316,7 +375,7 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
         bool first = true;
         while (u < seg_end && !aborted(s)) {
             const int ku0 = u - tile * p.kunits;
-            const int nkb = min(kStageKB, seg_end - u);
+            const int nkb = stage_len(p, ku0, seg_end - u);
             const uint32_t st = pp.stage % kStages;
             const uint32_t use = pp.stage / kStages;
             if (!wait_bar(s, &s.full[st], use & 1, c.a->status)) {
@@ -324,6 +383,7 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc::fence_after_sync();
+            tc::sf_copy(c.tbase + kColSfa + 4 * st, tc::smem_u32(&s.sfa[st][0][0][0]));
             for (int j = 0; j < nkb; ++j) {
                 const int ku = ku0 + j;
                 const int kb = ku % kBlocks;
@@ -332,14 +392,15 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
                     bbase = tc::smem_u32(&s.bgu[0][0][0]);
                     sfb = c.tbase + kColSfbG + 4 * (kb >> 2);
                 } else {
-                    const int q = ku / kBlocks;
-                    bbase = tc::smem_u32(&s.bdown[q][0][0][0]);
-                    sfb = c.tbase + kColSfbD + 4 * (q * kSfChunks + (kb >> 2));
+                    const int ds = s.dslot[ku / kBlocks];
+                    bbase = tc::smem_u32(&s.bdown[ds][0][0][0]);
+                    sfb = c.tbase + kColSfbD + 4 * (ds * kSfChunks + (kb >> 2));
                 }
-                const uint64_t ad = tc::smem_desc(a0 + st * sizeof(s.a[0]) + uint32_t(j) * 256, 128, 2 * kStageKB * 128);
+                const uint64_t ad =
+                    tc::smem_desc(a0 + st * sizeof(s.a[0]) + uint32_t(kb & 3) * 256, 128, 2 * kStageKB * 128);
                 const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * 256, 128, kChunks * 128);
-                const uint32_t idesc = idesc0 | (uint32_t(kb & 3) << 4) | (uint32_t(j) << 29);
-                tc::mma(c.tbase + kColD + 8 * db, ad, bd, idesc, (c.tbase + kColSfa + 4 * st) | (uint32_t(j) << 30),
+                const uint32_t idesc = idesc0 | (uint32_t(kb & 3) << 4) | (uint32_t(kb & 3) << 29);
+                tc::mma(c.tbase + kColD + 8 * db, ad, bd, idesc, (c.tbase + kColSfa + 4 * st) | (uint32_t(kb & 3) << 30),
                         sfb | (uint32_t(kb & 3) << 30), !first);
                 first = false;
             }
@@ -610,7 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         s.abort = 0;
         gen = *reinterpret_cast<volatile unsigned *>(a.barrier + 1);
         for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&s.full[i], 2 * 32 * kLoadWarps);
+            tc::mbar_init(&s.full[i], 32 * kLoadWarps);
             tc::mbar_init(&s.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -629,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         const int ch = i / kN, n = i % kN;
         if (n >= kTerms) {
             *reinterpret_cast<uint4 *>(&s.bgu[ch][n][0]) = make_uint4(0, 0, 0, 0);
-            for (int q = 0; q < kTopK; ++q) {
+            for (int q = 0; q < kDownSlots; ++q) {
                 *reinterpret_cast<uint4 *>(&s.bdown[q][ch][n][0]) = make_uint4(0, 0, 0, 0);
             }
         }
@@ -668,6 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
             const int step = t * nl + li;
             const float *xcur = (li == 0) ? a.x + size_t(t) * kDim : a.y + size_t(t) * kDim;
 
+            stamp(a, step, 0);
             // ---------------- A: selection ----------------
             if (a.mode == 1) {
                 const double *acc = a.acc + size_t(step & 1) * (kMaxExperts + 1);
@@ -791,6 +853,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     __syncthreads();
                 }
             }
+            stamp(a, step, 1);
             // softmax (src/model.cpp:310-321) and ownership
             if (threadIdx.x == 0) {
                 float maximum = -INFINITY;
@@ -823,20 +886,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
             }
             __syncthreads();
             // B for gate/up: h split into terms; SFB into tensor memory.
-            for (int kb = warp; kb < kBlocks; kb += kThreads / 32) {
-                const int k = kb * 32 + lane;
-                const float xv = __ldcg(xcur + k);
-                const float h = (a.mode == 1) ? __fmul_rn(__fmul_rn(xv, s.scale), L.norm_w[k]) : xv;
-                uint32_t sc;
-                const uint32_t tb = tc::split_terms<kTerms>(h, sc);
+            // this warp's K-blocks: kb2 = warp + 9 i, 5 passes of two blocks;
+            // all x (and norm weight) loads are issued up front
+            constexpr int kPasses = (kBlocks / 2 + kThreads / 32 - 1) / (kThreads / 32);
+            float xr[kPasses][2], gr[kPasses][2];
 #pragma unroll
-                for (int n = 0; n < kTerms; ++n) {
-                    s.bgu[k >> 4][n][k & 15] = uint8_t(tb >> (8 * n));
+            for (int pi = 0; pi < kPasses; ++pi) {
+                const int kb2 = warp + pi * (kThreads / 32);
+#pragma unroll
+                for (int z = 0; z < 2; ++z) {
+                    const int k = (2 * kb2 + z) * 32 + lane;
+                    xr[pi][z] = kb2 < kBlocks / 2 ? __ldcg(xcur + k) : 0.0f;
+                    gr[pi][z] = (kb2 < kBlocks / 2 && a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
                 }
-                if (lane == 0) {
+            }
+#pragma unroll
+            for (int pi = 0; pi < kPasses; ++pi) {
+                const int kb2 = warp + pi * (kThreads / 32);
+                if (kb2 >= kBlocks / 2) {
+                    break;
+                }
+                // two independent K-blocks per pass (interleaved dependency chains)
+                float h[2];
+#pragma unroll
+                for (int z = 0; z < 2; ++z) {
+                    h[z] = (a.mode == 1) ? __fmul_rn(__fmul_rn(xr[pi][z], s.scale), gr[pi][z]) : xr[pi][z];
+                }
+                uint32_t sc[2], tb[2];
+#pragma unroll
+                for (int z = 0; z < 2; ++z) {
+                    tb[z] = tc::split_terms<kTerms>(h[z], sc[z]);
+                }
+#pragma unroll
+                for (int z = 0; z < 2; ++z) {
+                    const int kb = 2 * kb2 + z;
+                    const int k = kb * 32 + lane;
 #pragma unroll
                     for (int n = 0; n < kTerms; ++n) {
-                        s.sfbg[kb][n] = uint8_t(sc >> (8 * n));
+                        s.bgu[k >> 4][n][k & 15] = uint8_t(tb[z] >> (8 * n));
+                    }
+                    if (lane == 0) {
+#pragma unroll
+                        for (int n = 0; n < kTerms; ++n) {
+                            s.sfbg[kb][n] = uint8_t(sc[z] >> (8 * n));
+                        }
                     }
                 }
             }
@@ -861,6 +954,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
             __syncthreads();
             tc::fence_after_sync();
 
+            stamp(a, step, 2);
             // ---------------- B: gate/up ----------------
             Ctx cx{&a, &L, &s, tbase};
             const Phase pb{0, s.n_local * kGateTiles, kBlocks};
@@ -870,37 +964,95 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 run_loader(cx, pb, pipe);
             } else if (lane == 0) {
                 run_mma(cx, pb, pipe);
+            } else {
+                prefetch_down(cx, s.n_local * kBlocks);
             }
+            __syncthreads();
+            stamp(a, step, 3);
             ok = grid_barrier(a.barrier, gen, a.status, s);
             if (!ok) {
                 break;
             }
+            stamp(a, step, 4);
             // ---------------- C: down ----------------
-            // B for down: copy the w * hidden terms (written by phase B's
-            // reducers) into shared memory; their scales into tensor memory.
-            for (int i = threadIdx.x; i < s.n_local * kChunks * kTerms; i += kThreads) {
-                const int q = i / (kChunks * kTerms);
-                const int r = i - q * kChunks * kTerms;
-                const int ch = r / kTerms;
-                const int n = r - ch * kTerms;
-                *reinterpret_cast<uint4 *>(&s.bdown[q][ch][n][0]) =
-                    __ldcg(reinterpret_cast<const uint4 *>(a.bdown + ((size_t(q) * kChunks + ch) * kN + n) * 16));
+            // B for down: the w * hidden terms (written by phase B's reducers)
+            // of the experts this CTA's down units touch (at most kDownSlots),
+            // into shared memory; their scales into tensor memory.
+            if (threadIdx.x == 0) {
+                const int ku_tile = s.n_local * kBlocks;
+                const int units = kDownTiles * ku_tile;
+                const int u0 = range_lo(blockIdx.x, gridDim.x, units);
+                const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
+                for (int q = 0; q < kTopK; ++q) {
+                    s.dslot[q] = -1;
+                }
+                int nd = 0;
+                for (int u = u0; u < u1;) {
+                    const int ku = u % ku_tile;
+                    const int q = ku / kBlocks;
+                    if (s.dslot[q] < 0) {
+                        if (nd < kDownSlots) {
+                            s.dslot[q] = nd++;
+                        } else {
+                            set_status(a.status, kStatusBadShape);
+                            s.dslot[q] = 0;
+                        }
+                    }
+                    u += min(kBlocks - ku % kBlocks, u1 - u);
+                }
+            }
+            __syncthreads();
+            {
+                constexpr int kPer = (kDownSlots * kChunks * kTerms + kThreads - 1) / kThreads;
+                uint4 buf[kPer];
+                int dst[kPer];
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    const int i = threadIdx.x + k * kThreads;  // over (q in 0..3, chunk, term) of used experts
+                    dst[k] = -1;
+                    int seen = 0;
+                    for (int q = 0; q < kTopK; ++q) {
+                        if (s.dslot[q] >= 0 && q < s.n_local) {
+                            const int base = seen * kChunks * kTerms;
+                            if (i >= base && i < base + kChunks * kTerms) {
+                                const int r = i - base;
+                                const int ch = r / kTerms;
+                                const int n = r - ch * kTerms;
+                                buf[k] = __ldcg(reinterpret_cast<const uint4 *>(a.bdown + ((size_t(q) * kChunks + ch) * kN + n) * 16));
+                                dst[k] = (s.dslot[q] * kChunks + ch) * kN + n;
+                            }
+                            ++seen;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    if (dst[k] >= 0) {
+                        *reinterpret_cast<uint4 *>(&s.bdown[0][0][0][0] + size_t(dst[k]) * 16) = buf[k];
+                    }
+                }
+            }
+            for (int i = threadIdx.x; i < kTopK * kBlocks; i += kThreads) {
+                const int q = i / kBlocks;
+                if (q < s.n_local && s.dslot[q] >= 0) {
+                    const uint32_t w4 = __ldcg(reinterpret_cast<const unsigned int *>(a.sfb_down) + i);
+                    *reinterpret_cast<uint32_t *>(&s.sfbd[s.dslot[q]][i % kBlocks][0]) = w4;
+                }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
             if (warp >= kEpiWarps && warp < kEpiWarps + kLoadWarps) {
                 const int q4 = warp & 3;
-                for (int q = 0; q < s.n_local; ++q) {
+                for (int d = 0; d < kDownSlots; ++d) {
                     for (int g = 0; g < kSfChunks; ++g) {
                         uint32_t v = 0;
                         if (lane < kTerms) {
                             for (int k = 0; k < 4; ++k) {
                                 const int kb = 4 * g + k;
-                                v |= (kb < kBlocks ? uint32_t(__ldcg(a.sfb_down + (size_t(q) * kBlocks + kb) * kTerms + lane))
-                                                   : 127u)
-                                     << (8 * k);
+                                v |= (kb < kBlocks ? uint32_t(s.sfbd[d][kb][lane]) : 127u) << (8 * k);
                             }
                         }
-                        tc::tmem_st4(tbase + (uint32_t(32 * q4) << 16) + kColSfbD + 4 * (q * kSfChunks + g), v, 0u, 0u,
+                        tc::tmem_st4(tbase + (uint32_t(32 * q4) << 16) + kColSfbD + 4 * (d * kSfChunks + g), v, 0u, 0u,
                                      0u);
                     }
                 }
@@ -909,6 +1061,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
             tc::fence_before_sync();
             __syncthreads();
             tc::fence_after_sync();
+            stamp(a, step, 5);
             const bool next_router =
                 (a.mode == 1) && (li + 1 < nl || t + 1 < a.tokens);
             const Phase pc{1, kDownTiles, s.n_local * kBlocks};
@@ -919,7 +1072,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
             } else if (lane == 0) {
                 run_mma(cx, pc, pipe);
             }
+            __syncthreads();
+            stamp(a, step, 6);
             ok = grid_barrier(a.barrier, gen, a.status, s);
+            stamp(a, step, 7);
         }
     }
     // drain: this thread's copies; the MMA thread waits for its MMAs; then

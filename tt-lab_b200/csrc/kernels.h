@@ -97,7 +97,11 @@ struct StackArgs {
     unsigned *cnt_dn;          // [23]
     uint8_t *bdown;            // [4][180][8][16] down B operand: E4M3 terms of w * hidden
     uint8_t *sfb_down;         // [4][90][4] their E8M0 scales
+    unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
+    int trace_steps;
 };
+
+constexpr int kTracePoints = 10;
 
 size_t decode_tc_smem_bytes();
 void configure_decode_tc();

@@ -101,6 +101,8 @@ struct ttl_moe {
     cudaEvent_t stack_ev[2] = {nullptr, nullptr};
     bool stack_profiled = false;
     int stack_steps = 0;              // (token, layer) steps of the profiled launch
+    unsigned long long *d_trace = nullptr;  // phase stamps (ttl_moe_trace)
+    int trace_steps = 0;
 };
 
 namespace ttl {
@@ -287,6 +289,11 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.cnt_dn = h->d_cnt + 4 * 45;
     a.bdown = h->d_bdown;
     a.sfb_down = h->d_sfb_down;
+    a.trace = h->d_trace;
+    a.trace_steps = h->trace_steps;
+    if (h->d_trace) {
+        TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_trace, 0, size_t(h->trace_steps) * kTracePoints * 8, h->stream));
+    }
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned), h->stream));
@@ -909,6 +916,28 @@ int ttl_moe_profile(ttl_moe *h, int enable) {
         }
     }
     h->profile = enable != 0;
+    return TTL_OK;
+}
+
+int ttl_moe_trace(ttl_moe *h, int steps, uint64_t *out) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    int rc = set_device(h);
+    if (rc) {
+        return rc;
+    }
+    if (steps > 0 && !h->d_trace) {
+        rc = alloc_n(h, &h->d_trace, size_t(steps) * kTracePoints);
+        if (rc) {
+            return rc;
+        }
+        h->trace_steps = steps;
+    }
+    if (out && h->d_trace) {
+        TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+        TTL_TRY_CUDA(h, cudaMemcpy(out, h->d_trace, size_t(h->trace_steps) * kTracePoints * 8, cudaMemcpyDeviceToHost));
+    }
     return TTL_OK;
 }
 

@@ -85,26 +85,38 @@ __device__ __forceinline__ void fence_mbar_init() {
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
-    // suspend hint of 1 us per attempt
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(1000u)
+        : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
-// Waits for phase `parity` to complete; gives up after `limit` attempts of at
-// most ~1 us each (about 2 s) and returns false -- the caller records a
-// status bit and unwinds.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = 1u << 21) {
-    for (uint32_t i = 0; i < limit; ++i) {
-        if (mbar_try_wait(bar, parity)) {
-            return true;
+__device__ __forceinline__ unsigned long long now_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits for phase `parity` to complete; gives up after about `limit_ns`
+// (default 2 s) and returns false -- the caller records a status bit and
+// unwinds.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned long long limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) {
+        return true;
+    }
+    const unsigned long long t0 = now_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i) {
+            if (mbar_try_wait(bar, parity)) {
+                return true;
+            }
+        }
+        if (now_ns() - t0 > limit_ns) {
+            return false;
         }
     }
-    return false;
 }
 // Arrives on `bar` when all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -150,6 +162,14 @@ __device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b
         : "memory");
 }
 
+// Copies a 32-row x 16-byte scale block from shared memory into 4 tensor-memory
+// columns of all four lane quadrants (row m0 -> lane m0 of each quadrant).
+// Ordered before later tcgen05.mma of the issuing thread.
+__device__ __forceinline__ void sf_copy(uint32_t taddr, uint32_t saddr) {
+    const uint64_t d = smem_desc(saddr, 128, 128);
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(d) : "memory");
+}
+
 // ---- activation terms ----
 // Splits the 32 values of one K-block (one per lane) into kTerms E4M3 terms
 // with one E8M0 scale each: returns this lane's term bytes packed in a u32
@@ -161,15 +181,13 @@ __device__ __forceinline__ uint32_t split_terms(float v, uint32_t &scale_bytes) 
     float r = v;
 #pragma unroll
     for (int j = 0; j < kTerms; ++j) {
-        float m = fabsf(r);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        }
+        // block max of |r| (non-negative floats order like their bit patterns)
+        const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(r)));
+        const float m = __uint_as_float(mb);
         // scale 2^(E-7) where 2^E <= m < 2^(E+1): m / scale in [128, 256) <= 448
         int e8 = 127;
         if (m > 0.0f && m == m) {
-            const int E = int((__float_as_uint(m) >> 23) & 0xFF) - 127;  // m normal here
+            const int E = int((mb >> 23) & 0xFF) - 127;
             e8 = E - 7 + 127;
             e8 = e8 < 1 ? 1 : (e8 > 253 ? 253 : e8);
         }

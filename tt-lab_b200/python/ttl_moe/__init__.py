@@ -85,6 +85,7 @@ def lib():
         "ttl_moe_stream": (vp, [vp]),
         "ttl_moe_counters": (i32, [vp, ctypes.POINTER(u64), sz]),
         "ttl_moe_profile": (i32, [vp, i32]),
+        "ttl_moe_trace": (i32, [vp, i32, ctypes.POINTER(u64)]),
         "ttl_moe_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float), sz]),
         "ttl_matvec_mxfp4": (i32, [vp, vp, vp, vp, i32]),
         "ttl_packed_bytes": (sz, [sz]),
@@ -232,6 +233,17 @@ class MoE:
         out = (ctypes.c_float * 3)()
         self._check(lib().ttl_moe_kernel_ms(self.h, out, 3))
         return {"ms": out[0], "steps": int(out[1]), "persistent": bool(out[2])}
+
+    def trace_enable(self, steps):
+        self._check(lib().ttl_moe_trace(self.h, steps, None))
+        self._trace_steps = steps
+
+    def trace(self):
+        """[steps, 10] ns stamps of the persistent decode kernel's phases."""
+        n = self._trace_steps
+        out = (ctypes.c_uint64 * (n * 10))()
+        self._check(lib().ttl_moe_trace(self.h, 0, out))
+        return np.frombuffer(out, dtype=np.uint64).reshape(n, 10).astype(np.int64)
 
     def counters(self):
         out = (ctypes.c_uint64 * 3)()
