@@ -16,13 +16,33 @@ constexpr int kMaxExperts = 128;      // src/model.h:41
 // Packed GPU layout of one 2880 x 2880 MXFP4 matrix (TTQ format 6):
 //   nibbles: [2880 rows][1440 B]; element k of a row sits in byte k/2, low
 //            nibble for even k (the order TMA and the tensor cores use);
-//   scales:  [2880 rows][96 B]; bytes 0..89 are the row's E8M0 block scales,
-//            90..95 are zero padding so every row stays 16-byte aligned.
+//   scales:  the E8M0 block scales, tile-blocked: for each 128-row tile t (23;
+//            rows past 2879 are zero) and each chunk c of 4 K-blocks (23;
+//            K-blocks 90 and 91 are zero), one 512-byte block ordered
+//            [row % 32][(row % 128) / 32][K-block % 4] -- the order in which
+//            tcgen05.cp moves an M = 128 tile's scales into tensor memory, so
+//            a tile's scales for 4 K-blocks are one contiguous copy.  Blocks
+//            are stored tile-major ((t * 23 + c) * 512); the region is padded
+//            with zeros to 2880 x 96 bytes.
 constexpr int kNibbleRowBytes = kDim / 2;   // 1440
-constexpr int kScaleRowBytes = 96;
 constexpr size_t kNibbleBytes = size_t(kDim) * kNibbleRowBytes;  // 4,147,200
-constexpr size_t kScaleBytes = size_t(kDim) * kScaleRowBytes;    // 276,480
+constexpr size_t kScaleBytes = size_t(kDim) * 96;                // 276,480
 constexpr size_t kPackedMatrixBytes = kNibbleBytes + kScaleBytes;  // 4,423,680
+constexpr int kScaleTiles = (kDim + 127) / 128;  // 23
+constexpr int kScaleChunks = (kBlocks + 3) / 4;  // 23
+constexpr size_t kScaleBlockBytes = 512;
+static_assert(size_t(kScaleTiles) * kScaleChunks * kScaleBlockBytes <= kScaleBytes, "scale layout");
+
+// Byte offset, from the start of a packed matrix, of the scale of (row, K-block).
+__host__ __device__ __forceinline__ constexpr size_t scale_offset(int row, int kb) {
+    return kNibbleBytes + (size_t(row >> 7) * kScaleChunks + size_t(kb >> 2)) * kScaleBlockBytes +
+           size_t(row & 31) * 16 + size_t((row >> 5) & 3) * 4 + size_t(kb & 3);
+}
+
+// Offset of the 512-byte scale block of (128-row tile, 4-K-block chunk).
+__host__ __device__ __forceinline__ constexpr size_t scale_block_offset(int tile, int chunk) {
+    return kNibbleBytes + (size_t(tile) * kScaleChunks + size_t(chunk)) * kScaleBlockBytes;
+}
 
 // Device status word bits (set by kernels, read by ttl_moe_sync).
 enum : uint32_t {

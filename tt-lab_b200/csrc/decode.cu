@@ -392,8 +392,8 @@ __global__ void __launch_bounds__(kMatvecThreads, 1) decode_gateup_kernel(LayerD
             if (kb < kBlocks) {
                 gq[j] = ldg_stream(gm + size_t(row) * kNibbleRowBytes + kb * 16);
                 uq[j] = ldg_stream(um + size_t(row) * kNibbleRowBytes + kb * 16);
-                gsb[j] = ldg_u8(gm + kNibbleBytes + size_t(row) * kScaleRowBytes + kb);
-                usb[j] = ldg_u8(um + kNibbleBytes + size_t(row) * kScaleRowBytes + kb);
+                gsb[j] = ldg_u8(gm + scale_offset(row, kb));
+                usb[j] = ldg_u8(um + scale_offset(row, kb));
             }
         }
         float ag = 0.0f;
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(kDownThreads, 1)
                 const int kb = lane + 32 * j;
                 if (le >= 0 && kb < kBlocks) {
                     q[sel][j] = ldg_stream(m + size_t(row) * kNibbleRowBytes + kb * 16);
-                    sb[sel][j] = ldg_u8(m + kNibbleBytes + size_t(row) * kScaleRowBytes + kb);
+                    sb[sel][j] = ldg_u8(m + scale_offset(row, kb));
                 }
             }
         }

@@ -477,7 +477,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(StackArgs a) 
                 if ((threadIdx.x & 1) == 0) {
                     prefetch_l2(m + size_t(r0) * kNibbleRowBytes, uint32_t((r1 - r0) * kNibbleRowBytes));
                 } else {
-                    prefetch_l2(m + kNibbleBytes + size_t(r0) * kScaleRowBytes, uint32_t((r1 - r0) * kScaleRowBytes));
+                    const size_t lo = scale_block_offset(r0 >> 7, 0);
+                    const size_t hi = scale_block_offset(((r1 - 1) >> 7) + 1, 0);
+                    prefetch_l2(m + lo, uint32_t(hi - lo));
                 }
             }
             {
@@ -498,8 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(StackArgs a) 
                         if (kb < kBlocks) {
                             gq[j] = ldg_stream(gm + size_t(row) * kNibbleRowBytes + kb * 16);
                             uq[j] = ldg_stream(um + size_t(row) * kNibbleRowBytes + kb * 16);
-                            gs[j] = __ldg(gm + kNibbleBytes + size_t(row) * kScaleRowBytes + kb);
-                            us[j] = __ldg(um + kNibbleBytes + size_t(row) * kScaleRowBytes + kb);
+                            gs[j] = __ldg(gm + scale_offset(row, kb));
+                            us[j] = __ldg(um + scale_offset(row, kb));
                         }
                     }
                 };
@@ -564,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_stack_kernel(StackArgs a) 
                                 const int kb = lane + 32 * j;
                                 if (kb < kBlocks) {
                                     q[k][j] = *reinterpret_cast<const uint4 *>(m + size_t(row) * kNibbleRowBytes + kb * 16);
-                                    sb[k][j] = m[kNibbleBytes + size_t(row) * kScaleRowBytes + kb];
+                                    sb[k][j] = m[scale_offset(row, kb)];
                                 }
                             }
                         }

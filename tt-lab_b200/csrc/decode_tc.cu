@@ -5,28 +5,45 @@
 // (src/model.cpp:590-594).  One cooperative launch runs every token x layer of
 // a decode call; one CTA per SM.
 //
+// Roles (10 warps):
+//   warps 0-8  the compute group: selection, B-operand preparation and the
+//              grid barriers; warps 0-3 also run the epilogues (one thread
+//              per tile row, TMEM lane quadrant = warp) and lane 0 of warp 8
+//              issues the block-scaled MMAs
+//   warp 9     lane 0 issues the loads into the stage ring: per stage 32 KB
+//              of packed E2M1 weights as two 128-byte x 128-row TMA boxes
+//              (128-byte swizzle: the K-major layout of the MMA's A operand)
+//              and their scales as bulk copies of the packed layout's 512-byte
+//              tile blocks (already in tcgen05.cp order).  It follows the
+//              published selection only, so the down-projection weights stream
+//              in while the grid is still finishing the gate/up phase.
+//
+// Products are kind::mxf4 block-scaled MMAs (A = the weights' E2M1 nibbles
+// with their E8M0 scales, untouched; K = 64 per instruction).  The B operand
+// is the activation in block fixed point: 12 base-4 digit terms per value
+// (E2M1 values 0..3 with a power-of-two scale per term and K-block, N = 16),
+// exact to 2^-24 of each K-block's largest value; the accumulator's 16
+// columns are the per-term partial products, summed in the epilogue.
+//
 // Per layer:
 //   A  select   Every CTA reads the layer's router sums (f64, accumulated by
 //               the previous layer's epilogues -- the RMSNorm scale is a
 //               scalar, so logit_e = b_e + s * sum_c W_ec g_c x_c splits over
-//               row slices), picks the same top 4 and splits h = RMSNorm(x)*g
-//               into four E4M3 terms (the B operand, N = 8).  Mode 0 (one
-//               plain MoE, h given) computes the logits in a router phase with
-//               an error bound instead and re-evaluates near-ties exactly in
-//               the reference's order, so its indices equal the reference's.
-//   B  gate/up  Units are (tile, K-block): a tile is 64 gate rows + the 64 up
-//               rows of the same outputs of one selected expert (M = 128).
-//               Each CTA takes an equal contiguous range of units (stream-K).
-//               Loader warps copy the E2M1 nibbles straight from HBM into
-//               shared memory (8-byte runs into 16-byte slots) and the block
-//               scales into tensor memory; one thread issues block-scaled
-//               MXF8F6F4 MMAs (K = 32) accumulating in tensor memory; epilogue
-//               warps read the tile partial.  The last contributor to a tile
-//               sums the partials in order, adds the biases, applies SwiGLU
-//               and the routing weight, and writes the tile's 64 hidden values
-//               as E4M3 terms -- the B operand of the down projection.
+//               row slices), picks the same top 4 and, meanwhile, splits
+//               h = RMSNorm(x)*g into its digit terms (the B operand).
+//               Mode 0 (one plain MoE, h given) computes the logits in a
+//               router phase with an error bound instead and re-evaluates
+//               near-ties exactly in the reference's order, so its indices
+//               equal the reference's.
+//   B  gate/up  Units are (tile, K-block pair): a tile is 128 gate rows and the 128
+//               up rows of the same outputs of one selected expert (two M = 128
+//               accumulators).  Each CTA takes an equal contiguous range of
+//               units (stream-K).  The last contributor to a tile sums the
+//               partials in order, adds the biases, applies SwiGLU and the
+//               routing weight, and writes the tile's 128 hidden values as
+//               digit terms -- the B operand of the down projection.
 //   -- grid barrier --
-//   C  down     Units are (128-row tile, expert x K-block): the four experts'
+//   C  down     Units are (128-row tile, expert x K-block pair): the four experts'
 //               down projections accumulate into one tensor (the routing
 //               weights are already in B).  The last contributor adds
 //               sum_q w_q b_q, the residual, writes the output rows and (stack
@@ -43,45 +60,52 @@
 namespace ttl {
 namespace {
 
-constexpr int kTerms = 4;
-constexpr int kN = 8;
-constexpr int kChunks = kDim / 16;            // 180 16-element K-chunks
-constexpr int kSfChunks = (kBlocks + 3) / 4;  // 23 scale chunks of 4 K-blocks
-constexpr int kStages = 9;
-constexpr int kStageKB = 4;                   // K-blocks per stage
+constexpr int kN = 16;                        // B rows: tc::kDigitTerms digit terms + 4 zero rows
+constexpr int kPairs = kBlocks / 2;           // 45 K-block pairs (one MMA each) per row
+constexpr int kBRowBytes = 256;               // B bytes per K-block: [2 row groups][8 rows][16 B]
+constexpr int kCodeBytes = 96;                // block codes per B operand (90 + padding, 127)
+constexpr int kSfChunks = kScaleChunks;       // 23 scale chunks of 4 K-blocks
+constexpr int kTiles = kScaleTiles;           // 23 tiles of 128 rows
+constexpr int kStages = 4;
 constexpr int kEpiWarps = 4;                  // warps 0-3
-constexpr int kLoadWarps = 4;                 // warps 4-7
-constexpr int kThreads = 32 * (kEpiWarps + kLoadWarps + 1);
-constexpr int kGateTiles = kDim / 64;         // 45 tiles of 64 gate + 64 up rows
-constexpr int kDownTiles = (kDim + 127) / 128;  // 23 tiles of 128 rows
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr int kThreads = 32 * (kTmaWarp + 1);
+constexpr int kComputeWarps = kTmaWarp;       // warps 0-8
+constexpr int kComputeThreads = 32 * kComputeWarps;
 constexpr int kMaxSlots = 16;                 // contributors per tile (checked)
+constexpr uint32_t kBoxTx = 128 * 128;        // bytes of one weight box (8 K-blocks of 128 rows)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD = 0;                                  // 2 x 8 columns
-constexpr uint32_t kColSfa = 16;                               // kStages x 4 columns
-constexpr uint32_t kColSfbG = kColSfa + 4 * kStages;           // 23 scale chunks x 4 columns
-constexpr uint32_t kColSfbD = kColSfbG + 4 * ((kBlocks + 3) / 4);  // kDownSlots x 23 x 4 columns
+constexpr uint32_t kColD = 0;                                  // 2 buffers x (gate 16 + up 16) columns
+constexpr uint32_t kColSfa = 64;                               // kStages x 4 chunks x 4 columns
+constexpr uint32_t kColSfbG = kColSfa + 16 * kStages;          // 23 scale chunks x 4 columns
+constexpr uint32_t kColSfbD = kColSfbG + 4 * kSfChunks;        // kDownSlots x 23 x 4 columns
 constexpr int kDownSlots = 2;                 // down-projection experts a CTA touches (checked)
-static_assert(kColSfbD + 4 * kDownSlots * ((kBlocks + 3) / 4) <= kTmemCols, "tensor memory map");
-constexpr unsigned long long kSpinLimit = 1ull << 22;  // x ~0.6 us per poll: ~2.5 s
+static_assert(kColSfbD + 4 * kDownSlots * kSfChunks <= kTmemCols, "tensor memory map");
+constexpr int kPreE = 32;                     // next-layer router weights the down epilogue loads early
+constexpr int kOwnMax = 3;                    // tiles a CTA reduces in one phase (checked)
+constexpr unsigned long long kGridWaitNs = 2000000000ull;
 
-struct alignas(128) Smem {
-    uint8_t a[kStages][16][2 * kStageKB][8][16];  // A stages: [row group][chunk][row][16 B]
-    uint8_t sfa[kStages][32][4][4];               // A scales per stage: [m0][m1][K-block], rows m0 + 32*m1
-    uint8_t bgu[kChunks][kN][16];                 // gate/up B: h terms
-    uint8_t bdown[kDownSlots][kChunks][kN][16];   // down B: w * hidden terms of this CTA's experts
-    uint8_t sfbg[kBlocks][kTerms];                // gate/up B term scales
-    uint8_t sfbd[kDownSlots][kBlocks][kTerms];    // down B term scales
+struct alignas(1024) Smem {
+    uint8_t a[kStages][2][128][128];              // A stages: two boxes of 128 rows x 256 E2M1, swizzled
+    uint8_t sfa[kStages][4][kScaleBlockBytes];    // their scale blocks (gate/up: gate 0-1, up 2-3; down: 0-3)
+    uint8_t bgu[kBlocks][kBRowBytes];             // gate/up B: digit terms of h
+    uint8_t bdown[kDownSlots][kBlocks][kBRowBytes];  // down B: digit terms of w * hidden of this CTA's experts
+    alignas(16) uint8_t gcode[kCodeBytes];        // gate/up B block codes
+    alignas(16) uint8_t dcode[kDownSlots][kCodeBytes];  // down B block codes
+    double rsum[kEpiWarps][kMaxExperts + 1];      // next-layer router sums per epilogue warp
+    float own_part[kOwnMax][2][128];              // partials of the tiles this CTA reduces (gate, up)
     int dslot[kTopK];                             // expert slot -> bdown slot, -1 if unused
-    float xch[64];                                // up values for the SwiGLU exchange
-    float part[128];                              // scratch for the tile reduction
     float logit[kMaxExperts];
     float bound[kMaxExperts];
     float val[kMaxExperts];
-    double red[kThreads / 32];
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    double red[kComputeWarps];
+    uint64_t full[kStages];       // a stage's bytes landed
+    uint64_t empty[kStages];      // the MMAs of a stage completed
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
+    uint64_t sel_full;            // the step's selection is published
+    uint64_t setup;               // the down B operands of the step landed
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier verdict, written by thread 0 only
@@ -94,10 +118,11 @@ struct alignas(128) Smem {
     int amb;
     int abort;
     int last;
-    float scale;
 };
 
-// Role-local pipeline counters (each role walks the same unit sequence).
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory per CTA");
+
+// Role-local pipeline counters (each role walks the same stage sequence).
 struct Pipe {
     uint32_t stage = 0;  // stages issued / consumed so far
     uint32_t seg = 0;    // segments (D buffers) so far
@@ -112,7 +137,11 @@ __device__ __forceinline__ void fail_wait(Smem &s, uint32_t *status) {
     *reinterpret_cast<volatile int *>(&s.abort) = 1;
 }
 
+// Bounded wait; a phase that already completed costs one try_wait.
 __device__ __forceinline__ bool wait_bar(Smem &s, uint64_t *bar, uint32_t parity, uint32_t *status) {
+    if (tc::mbar_try_wait(bar, parity)) {
+        return true;
+    }
     if (aborted(s)) {
         return false;
     }
@@ -123,68 +152,44 @@ __device__ __forceinline__ bool wait_bar(Smem &s, uint64_t *bar, uint32_t parity
     return true;
 }
 
-// Warp-uniform variants: lane 0 decides, the warp follows (warp-collective
-// tcgen05 instructions need every lane).
-__device__ __forceinline__ bool warp_aborted(const Smem &s) {
-    return __shfl_sync(0xffffffffu, aborted(s) ? 1 : 0, 0) != 0;
-}
-
-__device__ __forceinline__ bool warp_wait(Smem &s, uint64_t *bar, uint32_t parity, uint32_t *status) {
-    int ok = 0;
-    if ((threadIdx.x & 31) == 0) {
-        ok = wait_bar(s, bar, parity, status) ? 1 : 0;
-    }
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void cp_async8(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
-}
-
 __device__ __forceinline__ void epi_sync() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 2, 128;" ::: "memory");
 }
 
-// Bounded grid barrier (all threads of every CTA).
+__device__ __forceinline__ void compute_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory");
+}
+
+// Bounded grid barrier of the compute groups.  bar[0] counts arrivals over
+// the whole launch (zeroed by the host before it); barrier n completes when
+// it reaches n * gridDim.x.
 __device__ bool grid_barrier(unsigned *bar, unsigned &gen, uint32_t *status, Smem &s) {
-    __syncthreads();
+    compute_sync();
     if (threadIdx.x == 0 && !aborted(s)) {
-        __threadfence();
-        const unsigned arrived = atomicAdd(&bar[0], 1u);
-        if (arrived == gridDim.x - 1) {
-            bar[0] = 0u;
-            __threadfence();
-            atomicExch(&bar[1], gen + 1u);
-        } else {
-            unsigned long long spins = 0;
+        gen += 1u;
+        const unsigned target = gen * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+        const unsigned long long t0 = tc::now_ns();
+        while (true) {
             unsigned cur;
-            while (true) {
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(bar + 1) : "memory");
-                if (cur != gen) {
-                    break;
-                }
-                if (++spins > kSpinLimit) {
-                    fail_wait(s, status);
-                    break;
-                }
-                __nanosleep(64);
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(bar) : "memory");
+            if (int(cur - target) >= 0) {
+                break;
+            }
+            if (tc::now_ns() - t0 > kGridWaitNs) {
+                fail_wait(s, status);
+                break;
             }
         }
-        gen += 1u;
-        __threadfence();
     }
     if (threadIdx.x == 0) {
         s.go = aborted(s) ? 0 : 1;
     }
-    __syncthreads();
+    compute_sync();
     return s.go != 0;
 }
 
@@ -194,7 +199,8 @@ __device__ __forceinline__ unsigned long long globaltimer() {
     return t;
 }
 
-// Stage stamps for profiling (thread 0 of CTA 0; point 9 = latest phase-B end over CTAs).
+// Step stamps for profiling (thread 0 of CTA 0; points 8 and 9 = latest
+// phase-B / phase-C end over CTAs).
 __device__ __forceinline__ void stamp(const StackArgs &a, int step, int point) {
     if (a.trace && step < a.trace_steps && threadIdx.x == 0) {
         const unsigned long long t = globaltimer();
@@ -207,13 +213,15 @@ __device__ __forceinline__ void stamp(const StackArgs &a, int step, int point) {
     }
 }
 
-// Contiguous unit range of CTA c out of g over `units` units.
+// Contiguous unit range of CTA c out of g over `units` units (c * units and
+// u * g stay below 2^31: g <= 1024 CTAs, units <= 2^20).
 __device__ __forceinline__ int range_lo(int c, int g, int units) {
-    return int((long long)c * units / g);
+    return int(unsigned(c) * unsigned(units) / unsigned(g));
 }
 
+// The CTA whose range holds unit u.
 __device__ __forceinline__ int cta_of(int u, int g, int units) {
-    int c = int((long long)u * g / units);
+    int c = int(unsigned(u) * unsigned(g) / unsigned(units));
     while (c + 1 < g && range_lo(c + 1, g, units) <= u) {
         ++c;
     }
@@ -227,8 +235,16 @@ __device__ __forceinline__ int cta_of(int u, int g, int units) {
 struct Phase {
     int kind;    // 0 gate/up, 1 down
     int tiles;
-    int kunits;  // K-units per tile (90 for gate/up, n_local * 90 for down)
+    int kunits;  // K-units (K-block pairs) per tile: 45 for gate/up, n_local * 45 for down
 };
+
+__device__ __forceinline__ Phase gateup_phase(int n_local) {
+    return Phase{0, n_local * kTiles, kPairs};
+}
+
+__device__ __forceinline__ Phase down_phase(int n_local) {
+    return Phase{1, kTiles, n_local * kPairs};
+}
 
 struct Ctx {
     const StackArgs *a;
@@ -237,180 +253,174 @@ struct Ctx {
     uint32_t tbase;
 };
 
-// Stages are aligned to scale chunks: K-blocks [4g, 4g+4) of one matrix (the
-// last chunk of a row has 2), clipped to the segment.  Returns the stage's
-// first K-unit offset within the tile and its K-block count.
-__device__ __forceinline__ int stage_len(const Phase &p, int ku, int seg_left) {
-    const int kb = ku % kBlocks;
-    const int chunk_end = min((kb & ~3) + 4, kBlocks);
-    return min(chunk_end - kb, seg_left);
-}
+// What one stage holds.  Gate/up: K-blocks of one aligned group of 8 (one
+// weight box), gate rows in box 0 and up rows in box 1.  Down: K-blocks of
+// one aligned group of 16, K-blocks 8b..8b+7 in box b & 1.
+struct StageRef {
+    int kind;
+    int tile;
+    int q;     // expert slot (index into slot_of)
+    int kb0;   // first K-block (even)
+    int nkb;   // K-blocks in the stage (even)
+};
 
-// ---- loader warps (4-7) ----
-// Thread lt copies chunk lt & 7 of rows (lt >> 3) + 16k, k = 0..7, of every
-// stage, and the scale word of row lt.  Row addresses are formed once per
-// segment (and per expert change in the down phase) and kept in registers.
-__device__ void run_loader(const Ctx &c, const Phase &p, Pipe &pp) {
-    Smem &s = *c.s;
-    const int lt = threadIdx.x - 32 * kEpiWarps;  // 0..127
-    const int ch = lt & 7;
-    const int r_first = lt >> 3;
+// Visits this CTA's stages of phase p in order; f(ref, seg_first, seg_last)
+// returns false to stop.
+template <class F>
+__device__ __forceinline__ bool for_each_stage(const Phase &p, F &&f) {
     const int units = p.tiles * p.kunits;
-    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
     const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    const uint8_t *gate = c.L->gate;
-    const uint8_t *up = c.L->up;
-    const uint8_t *down = c.L->down;
-    int u = u0;
+    int u = range_lo(blockIdx.x, gridDim.x, units);
+    const int span = (p.kind == 0) ? 4 : 8;  // pairs
     while (u < u1) {
         const int tile = u / p.kunits;
         const int seg_end = min(u1, (tile + 1) * p.kunits);
-        int cur_q = -1;
-        const uint8_t *rowp[8];   // nibble rows of this thread (nullptr past the matrix)
-        const uint8_t *sfrow = nullptr;
+        bool first = true;
         while (u < seg_end) {
-            if (warp_aborted(s)) {
-                return;
-            }
             const int ku0 = u - tile * p.kunits;
-            const int q = ku0 / kBlocks;
-            if (q != cur_q) {
-                cur_q = q;
-                if (p.kind == 0) {
-                    const int qq = tile / kGateTiles;
-                    const int j = tile - qq * kGateTiles;
-                    const size_t off = size_t(s.local[s.slot_of[qq]]) * kPackedMatrixBytes;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int i = r_first + 16 * k;
-                        rowp[k] = (i < 64 ? gate : up) + off + size_t(64 * j + (i & 63)) * kNibbleRowBytes;
-                    }
-                    sfrow = (lt < 64 ? gate : up) + off + kNibbleBytes + size_t(64 * j + (lt & 63)) * kScaleRowBytes;
-                } else {
-                    const uint8_t *m = down + size_t(s.local[s.slot_of[q]]) * kPackedMatrixBytes;
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int row = 128 * tile + r_first + 16 * k;
-                        rowp[k] = row < kDim ? m + size_t(row) * kNibbleRowBytes : nullptr;
-                    }
-                    const int row = 128 * tile + lt;
-                    sfrow = row < kDim ? m + kNibbleBytes + size_t(row) * kScaleRowBytes : nullptr;
-                }
+            StageRef r;
+            r.kind = p.kind;
+            r.q = ku0 / kPairs;
+            const int pr = ku0 - r.q * kPairs;
+            r.tile = tile;
+            if (p.kind == 0) {
+                r.q = tile / kTiles;
+                r.tile = tile - r.q * kTiles;
             }
-            const int nkb = stage_len(p, ku0, seg_end - u);
-            const int kb0 = ku0 % kBlocks;
-            const uint32_t st = pp.stage % kStages;
-            const uint32_t use = pp.stage / kStages;
-            if (use > 0 && !warp_wait(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
-                return;
+            const int np = min(min((pr & ~(span - 1)) + span, kPairs) - pr, seg_end - u);
+            r.kb0 = 2 * pr;
+            r.nkb = 2 * np;
+            u += np;
+            if (!f(r, first, u == seg_end)) {
+                return false;
             }
-            const int j = (ch >> 1) - (kb0 & 3);  // K-block of the stage this thread's chunk belongs to
-            if (j >= 0 && j < nkb) {
-                const size_t koff = size_t(kb0 + j) * 16 + (ch & 1) * 8;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    if (rowp[k]) {
-                        const int i = r_first + 16 * k;
-                        cp_async8(&s.a[st][i >> 3][ch][i & 7][0], rowp[k] + koff);
-                    }
-                }
-            }
-            if (sfrow) {
-                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(tc::smem_u32(&s.sfa[st][lt & 31][lt >> 5][0])),
-                             "l"(sfrow + (kb0 & ~3))
-                             : "memory");
-            }
-            cp_async_arrive(&s.full[st]);
-            ++pp.stage;
-            u += nkb;
+            first = false;
         }
     }
+    return true;
 }
 
-// L2 prefetch (idle lanes of the MMA warp during gate/up): this CTA's
-// down-phase rows, so the down phase streams from L2.
-__device__ void prefetch_down(const Ctx &c, int kunits) {
-    const Smem &s = *c.s;
-    const int lane = threadIdx.x & 31;
-    const int units = kDownTiles * kunits;
-    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    for (int u = u0; u < u1;) {
-        const int tile = u / kunits;
-        const int ku = u - tile * kunits;
-        const int q = ku / kBlocks;
-        const int kb0 = ku % kBlocks;
-        const int kb1 = min(kBlocks, kb0 + (u1 - u));
-        const uint8_t *m = c.L->down + size_t(s.local[s.slot_of[q]]) * kPackedMatrixBytes;
-        for (int i = lane - 1; i < 128; i += 31) {
-            const int row = 128 * tile + i;
-            if (row < kDim) {
-                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(m + size_t(row) * kNibbleRowBytes + kb0 * 16),
-                             "r"(uint32_t((kb1 - kb0) * 16))
-                             : "memory");
-            }
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+                 : "memory");
+}
+
+// ---- loads (warp 9, lane 0) ----
+__device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTopK], Pipe &pp) {
+    Smem &s = *c.s;
+    const TmaDesc *tm = c.L->tma;
+    const uint8_t *gate = c.L->gate;
+    const uint8_t *up = c.L->up;
+    const uint8_t *down = c.L->down;
+    return for_each_stage(p, [&](const StageRef &r, bool, bool) {
+        const uint32_t st = pp.stage % kStages;
+        const uint32_t use = pp.stage / kStages;
+        if (use > 0 && !wait_bar(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
+            return false;
         }
-        u += kb1 - kb0;
-    }
+        const int e = le[r.q];
+        const int c0 = r.kb0 >> 2;
+        const int c1 = (r.kb0 + r.nkb - 1) >> 2;
+        const uint32_t nc = uint32_t(c1 - c0 + 1);
+        const int row0 = 128 * r.tile;
+        const size_t so = size_t(e) * kPackedMatrixBytes + scale_block_offset(r.tile, c0);
+        if (r.kind == 0) {
+            const int x = 16 * (r.kb0 & ~7);  // byte offset of the stage's box in a row
+            tc::mbar_expect_tx(&s.full[st], 2 * kBoxTx + 2 * nc * uint32_t(kScaleBlockBytes));
+            tc::tma_load_3d(&s.a[st][0][0][0], tm + kTmaGate, x, row0, e, &s.full[st]);
+            tc::tma_load_3d(&s.a[st][1][0][0], tm + kTmaUp, x, row0, e, &s.full[st]);
+            bulk_load(&s.sfa[st][c0 & 1][0], gate + so, nc * kScaleBlockBytes, &s.full[st]);
+            bulk_load(&s.sfa[st][2 + (c0 & 1)][0], up + so, nc * kScaleBlockBytes, &s.full[st]);
+        } else {
+            const int b0 = r.kb0 >> 3;
+            const int b1 = (r.kb0 + r.nkb - 1) >> 3;
+            tc::mbar_expect_tx(&s.full[st], uint32_t(b1 - b0 + 1) * kBoxTx + nc * uint32_t(kScaleBlockBytes));
+            for (int b = b0; b <= b1; ++b) {
+                tc::tma_load_3d(&s.a[st][b & 1][0][0], tm + kTmaDown, 128 * b, row0, e, &s.full[st]);
+            }
+            bulk_load(&s.sfa[st][c0 & 3][0], down + so, nc * kScaleBlockBytes, &s.full[st]);
+        }
+        ++pp.stage;
+        return true;
+    });
 }
 
 // ---- MMA issuer (warp 8, lane 0) ----
 __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
     Smem &s = *c.s;
-    const int units = p.tiles * p.kunits;
-    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    const uint32_t a0 = tc::smem_u32(&s.a[0][0][0][0][0]);
-    const uint32_t idesc0 = tc::instr_desc(kN, 0, 0);
-    int u = u0;
-    while (u < u1 && !aborted(s)) {
-        const int tile = u / p.kunits;
-        const int seg_end = min(u1, (tile + 1) * p.kunits);
-        const uint32_t db = pp.seg & 1;
-        const uint32_t duse = pp.seg >> 1;
-        if (duse > 0 && !wait_bar(s, &s.acc_empty[db], (duse - 1) & 1, c.a->status)) {
-            return;
+    const uint32_t a0 = tc::smem_u32(&s.a[0][0][0][0]);
+    const uint32_t sf0 = tc::smem_u32(&s.sfa[0][0][0]);
+    const uint32_t tbase = c.tbase;
+    uint32_t db = 0;
+    bool first = true;
+    for_each_stage(p, [&](const StageRef &r, bool seg_first, bool seg_last) {
+        if (seg_first) {
+            db = pp.seg & 1;
+            const uint32_t duse = pp.seg >> 1;
+            if (duse > 0 && !wait_bar(s, &s.acc_empty[db], (duse - 1) & 1, c.a->status)) {
+                return false;
+            }
+            tc::fence_after_sync();
+            first = true;
+        }
+        const uint32_t st = pp.stage % kStages;
+        if (!wait_bar(s, &s.full[st], (pp.stage / kStages) & 1, c.a->status)) {
+            return false;
         }
         tc::fence_after_sync();
-        bool first = true;
-        while (u < seg_end && !aborted(s)) {
-            const int ku0 = u - tile * p.kunits;
-            const int nkb = stage_len(p, ku0, seg_end - u);
-            const uint32_t st = pp.stage % kStages;
-            const uint32_t use = pp.stage / kStages;
-            if (!wait_bar(s, &s.full[st], use & 1, c.a->status)) {
-                return;
+        const uint32_t abase = a0 + st * uint32_t(sizeof(s.a[0]));
+        const uint32_t sfbase = sf0 + st * uint32_t(sizeof(s.sfa[0]));
+        const uint32_t sfa_col = tbase + kColSfa + 16 * st;
+        const uint32_t dcol = tbase + kColD + 32 * db;
+        const int c0 = r.kb0 >> 2;
+        const int c1 = (r.kb0 + r.nkb - 1) >> 2;
+        if (r.kind == 0) {
+            for (int ch = c0; ch <= c1; ++ch) {
+                const uint32_t lc = uint32_t(ch & 1);
+                tc::sf_copy(sfa_col + 4 * lc, sfbase + kScaleBlockBytes * lc);
+                tc::sf_copy(sfa_col + 4 * (2 + lc), sfbase + kScaleBlockBytes * (2 + lc));
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            tc::fence_after_sync();
-            tc::sf_copy(c.tbase + kColSfa + 4 * st, tc::smem_u32(&s.sfa[st][0][0][0]));
-            for (int j = 0; j < nkb; ++j) {
-                const int ku = ku0 + j;
-                const int kb = ku % kBlocks;
-                uint32_t bbase, sfb;
-                if (p.kind == 0) {
-                    bbase = tc::smem_u32(&s.bgu[0][0][0]);
-                    sfb = c.tbase + kColSfbG + 4 * (kb >> 2);
-                } else {
-                    const int ds = s.dslot[ku / kBlocks];
-                    bbase = tc::smem_u32(&s.bdown[ds][0][0][0]);
-                    sfb = c.tbase + kColSfbD + 4 * (ds * kSfChunks + (kb >> 2));
-                }
-                const uint64_t ad =
-                    tc::smem_desc(a0 + st * sizeof(s.a[0]) + uint32_t(kb & 3) * 256, 128, 2 * kStageKB * 128);
-                const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * 256, 128, kChunks * 128);
-                const uint32_t idesc = idesc0 | (uint32_t(kb & 3) << 4) | (uint32_t(kb & 3) << 29);
-                tc::mma(c.tbase + kColD + 8 * db, ad, bd, idesc, (c.tbase + kColSfa + 4 * st) | (uint32_t(kb & 3) << 30),
-                        sfb | (uint32_t(kb & 3) << 30), !first);
+            const uint32_t bbase = tc::smem_u32(&s.bgu[0][0]);
+            for (int kb = r.kb0; kb < r.kb0 + r.nkb; kb += 2) {
+                const uint32_t sel = uint32_t(kb & 3);
+                const uint32_t aoff = 32u * uint32_t((kb >> 1) & 3);
+                const uint32_t lc = uint32_t((kb >> 2) & 1);
+                const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * kBRowBytes, kBRowBytes, 128);
+                const uint32_t idesc = tc::instr_desc_f4(kN, sel);
+                const uint32_t sfb = (tbase + kColSfbG + 4 * uint32_t(kb >> 2)) | (sel << 30);
+                tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, idesc, (sfa_col + 4 * lc) | (sel << 30), sfb, !first);
+                tc::mma_f4(dcol + 16, tc::smem_desc_sw128(abase + 16384u + aoff), bd, idesc,
+                           (sfa_col + 4 * (2 + lc)) | (sel << 30), sfb, !first);
                 first = false;
             }
-            tc::mma_commit(&s.empty[st]);
-            ++pp.stage;
-            u += nkb;
+        } else {
+            for (int ch = c0; ch <= c1; ++ch) {
+                const uint32_t lc = uint32_t(ch & 3);
+                tc::sf_copy(sfa_col + 4 * lc, sfbase + kScaleBlockBytes * lc);
+            }
+            const int ds = s.dslot[r.q];
+            const uint32_t bbase = tc::smem_u32(&s.bdown[ds][0][0]);
+            const uint32_t sfb0 = tbase + kColSfbD + 4 * uint32_t(ds * kSfChunks);
+            for (int kb = r.kb0; kb < r.kb0 + r.nkb; kb += 2) {
+                const uint32_t sel = uint32_t(kb & 3);
+                const uint32_t aoff = 16384u * uint32_t((kb >> 3) & 1) + 32u * uint32_t((kb >> 1) & 3);
+                const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * kBRowBytes, kBRowBytes, 128);
+                tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, tc::instr_desc_f4(kN, sel),
+                           (sfa_col + 4 * uint32_t((kb >> 2) & 3)) | (sel << 30), (sfb0 + 4 * uint32_t(kb >> 2)) | (sel << 30),
+                           !first);
+                first = false;
+            }
         }
-        tc::mma_commit(&s.acc_full[db]);
-        ++pp.seg;
-    }
+        tc::mma_commit(&s.empty[st]);
+        ++pp.stage;
+        if (seg_last) {
+            tc::mma_commit(&s.acc_full[db]);
+            ++pp.seg;
+        }
+        return true;
+    });
 }
 
 // Number of contributors to tile t and the slot of this CTA.
@@ -422,23 +432,262 @@ __device__ __forceinline__ void tile_slots(const Phase &p, int tile, int &n, int
     slot = int(blockIdx.x) - c0;
 }
 
+// Sum over contributors in slot order (this CTA's own partial in `slot`);
+// the loads are issued together.
+__device__ __forceinline__ float ordered_sum(const float *base, size_t stride, int nslot, int slot, float mine) {
+    float v[kMaxSlots];
+#pragma unroll
+    for (int k = 0; k < kMaxSlots; ++k) {
+        v[k] = (k < nslot && k != slot) ? __ldcg(base + k * stride) : 0.0f;
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxSlots; ++k) {
+        if (k < nslot) {
+            sum += (k == slot) ? mine : v[k];
+        }
+    }
+    return sum;
+}
+
+// Sums v[0..15] over the warp's 32 lanes: afterwards lane l holds the total of
+// value 8*b4 + 4*b3 + 2*b2 + b1 (b = bits of l), identical in lanes l and l^1.
+__device__ __forceinline__ double transpose_sum16(double (&v)[16], int lane) {
+#pragma unroll
+    for (int lvl = 0; lvl < 4; ++lvl) {
+        const int off = 16 >> lvl;
+        const int half = 8 >> lvl;
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < half) {
+                const double send = upper ? v[j] : v[j + half];
+                const double keep = upper ? v[j + half] : v[j];
+                v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+        }
+    }
+    return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+__device__ __forceinline__ int transpose_index(int lane) {
+    return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+}
+
 // ---- epilogue warps (0-3): one thread per tile row ----
+// Every contributor to a tile but the last publishes its partial (store, then
+// a release-add on the tile's counter) and moves on; the last contributor --
+// the CTA holding the tile's last units -- reduces: it waits for the count,
+// sums the partials in slot order and finishes the tile.  A CTA first reads
+// all of its segments (so its partials for other tiles go out at once), then
+// reduces the tiles it owns.
+struct EpiTile {
+    int tile;
+    int nslot;
+    int slot;
+};
+
+// Operands of a tile's epilogue, loaded before the tile's accumulators are.
+struct TileOps {
+    float bias_g, bias_u;  // gate/up: biases of this row
+    float bsum;            // down: sum_q w_q b_q of this row
+    float resid;           // down: residual
+    float nw;              // down: next layer's RMSNorm weight
+    float xnext;           // down: next token's input (last layer)
+    float rw[kPreE];       // down: next layer's router weights of this row
+};
+
+__device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int tile, int t_token, int li, bool next_router,
+                                              TileOps &o) {
+    const Smem &s = *c.s;
+    const StackArgs &a = *c.a;
+    const StackLayer &L = *c.L;
+    const int i = threadIdx.x;
+    const int nl = a.layer_end - a.layer_begin;
+    const bool more_layers = (li + 1 < nl);
+    o.bias_g = o.bias_u = o.bsum = o.resid = o.nw = o.xnext = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kPreE; ++e) {
+        o.rw[e] = 0.0f;
+    }
+    if (p.kind == 0) {
+        const int q = tile / kTiles;
+        const int row = 128 * (tile - q * kTiles) + i;
+        if (row < kDim) {
+            const int le = s.local[s.slot_of[q]];
+            o.bias_g = __ldg(L.gate_b + size_t(le) * kDim + row);
+            o.bias_u = __ldg(L.up_b + size_t(le) * kDim + row);
+        }
+        return;
+    }
+    const int row = 128 * tile + i;
+    if (row >= kDim) {
+        return;
+    }
+    float b[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        b[k] = (k < s.n_local) ? __ldg(L.down_b + size_t(s.local[s.slot_of[k]]) * kDim + row) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        if (k < s.n_local) {
+            o.bsum = __fadd_rn(o.bsum, __fmul_rn(s.wts[s.slot_of[k]], b[k]));
+        }
+    }
+    if (a.mode == 1) {
+        const float *xcur = (li == 0) ? a.x + size_t(t_token) * kDim : a.y + size_t(t_token) * kDim;
+        o.resid = __ldcg(xcur + row);
+    }
+    if (next_router) {
+        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
+        const float *nrw = N.router_w;
+        o.nw = __ldg(N.norm_w + row);
+        if (!more_layers) {
+            o.xnext = __ldcg(a.x + size_t(t_token + 1) * kDim + row);
+        }
+#pragma unroll
+        for (int e = 0; e < kPreE; ++e) {
+            o.rw[e] = (e < a.experts) ? __ldg(nrw + size_t(e) * kDim + row) : 0.0f;
+        }
+    }
+}
+
+// The tile's epilogue proper (reducer only): gate/up -> SwiGLU, routing
+// weight and the digit terms of the down projection's input; down -> bias,
+// residual, output rows and the next layer's router sums.
+__device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, const TileOps &o, float pg, float pu,
+                            int t_token, int li, bool next_router) {
+    Smem &s = *c.s;
+    const StackArgs &a = *c.a;
+    const int i = threadIdx.x;
+    const int w = i >> 5;
+    const int lane = i & 31;
+    const int E = a.experts;
+    const int nl = a.layer_end - a.layer_begin;
+    const bool more_layers = (li + 1 < nl);
+    const int tile = et.tile;
+    if (et.nslot > 1) {
+        const size_t stride = (p.kind == 0) ? 256 : 128;
+        const float *base = (p.kind == 0 ? a.part_gu : a.part_dn) + size_t(tile) * kMaxSlots * stride;
+        unsigned *cnt = (p.kind == 0 ? a.cnt_gu : a.cnt_dn) + tile;
+        if (i == 0) {
+            const unsigned want = unsigned(et.nslot - 1);
+            const unsigned long long t0 = tc::now_ns();
+            unsigned cur = 0;
+            while (true) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(cnt) : "memory");
+                if (cur == want || aborted(s)) {
+                    break;
+                }
+                if (tc::now_ns() - t0 > kGridWaitNs) {
+                    fail_wait(s, a.status);
+                    break;
+                }
+            }
+            *cnt = 0u;  // the tile's next use is after a grid barrier
+        }
+        epi_sync();
+        if (aborted(s)) {
+            return;
+        }
+        pg = ordered_sum(base + i, stride, et.nslot, et.slot, pg);
+        if (p.kind == 0) {
+            pu = ordered_sum(base + 128 + i, stride, et.nslot, et.slot, pu);
+        }
+    }
+    if (p.kind == 0) {
+        const int q = tile / kTiles;
+        const int row = 128 * (tile - q * kTiles) + i;
+        // warp w holds K-block (row >> 5) of the down projection's input
+        if (row - lane < kDim) {
+            float h = 0.0f;
+            if (row < kDim) {
+                h = __fmul_rn(swiglu_ref(__fadd_rn(o.bias_g, pg), __fadd_rn(o.bias_u, pu)), s.wts[s.slot_of[q]]);
+            }
+            const int kb = row >> 5;
+            const uint32_t code = tc::digit_split_store(h, a.bdown + (size_t(q) * kBlocks + kb) * kBRowBytes, lane);
+            if (lane == 0) {
+                a.sfb_down[size_t(q) * kCodeBytes + kb] = uint8_t(code);
+            }
+        }
+        return;
+    }
+    const int row = 128 * tile + i;
+    float yv = 0.0f;
+    if (row < kDim) {
+        const float out = __fadd_rn(pg, o.bsum);
+        yv = (a.mode == 1) ? __fadd_rn(o.resid, out) : out;
+        a.y[size_t(t_token) * kDim + row] = yv;
+    }
+    if (next_router) {
+        // router sums of the next (token, layer) over these rows: per warp,
+        // products transposed-summed over the 32 rows
+        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
+        const float xr = more_layers ? yv : o.xnext;
+        const double xgd = double(__fmul_rn(xr, o.nw));  // 0 past the last row
+        for (int b = 0; 16 * b < E; ++b) {
+            double v[16];
+            if (b < kPreE / 16) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = double(b == 0 ? o.rw[j] : o.rw[16 + j]) * xgd;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int e = 16 * b + j;
+                    v[j] = (e < E && row < kDim) ? double(__ldg(N.router_w + size_t(e) * kDim + row)) * xgd : 0.0;
+                }
+            }
+            const double tot = transpose_sum16(v, lane);
+            const int e = 16 * b + transpose_index(lane);
+            if ((lane & 1) == 0 && e < E) {
+                s.rsum[w][e] = tot;
+            }
+        }
+        const double sq = warp_sum_d(row < kDim ? double(__fmul_rn(xr, xr)) : 0.0);
+        if (lane == 0) {
+            s.rsum[w][E] = sq;
+        }
+        epi_sync();
+        const int step = t_token * nl + li;
+        double *acc = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
+        for (int e = i; e < E + 1; e += 32 * kEpiWarps) {
+            double tot = 0.0;
+#pragma unroll
+            for (int k = 0; k < kEpiWarps; ++k) {
+                tot += s.rsum[k][e];
+            }
+            atomicAdd(acc + e, tot);
+        }
+        epi_sync();
+    }
+}
+
 __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token, int li, bool next_router) {
     Smem &s = *c.s;
     const StackArgs &a = *c.a;
-    const StackLayer &L = *c.L;
     const int i = threadIdx.x;  // 0..127: tile row
     const int w = i >> 5;
-    const int lane = i & 31;
     const int units = p.tiles * p.kunits;
     const int u0 = range_lo(blockIdx.x, gridDim.x, units);
     const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    int u = u0;
-    while (u < u1) {
+    // The first tile whose last unit lies in this CTA's range is reduced here;
+    // its operands are loaded now, while the MMAs run.
+    const int first_owned = (u0 + p.kunits) / p.kunits - 1;
+    TileOps ops;
+    if (u0 < u1 && (first_owned + 1) * p.kunits - 1 < u1) {
+        load_tile_ops(c, p, first_owned, t_token, li, next_router, ops);
+    }
+    EpiTile own[kOwnMax];
+    int nown = 0;
+    for (int u = u0; u < u1;) {
         const int tile = u / p.kunits;
-        const int seg_end = min(u1, (tile + 1) * p.kunits);
+        u = min(u1, (tile + 1) * p.kunits);
         const uint32_t db = pp.seg & 1;
         const uint32_t duse = pp.seg >> 1;
+        ++pp.seg;
         if (i == 0) {
             s.epi_go = wait_bar(s, &s.acc_full[db], duse & 1, a.status) ? 1 : 0;
         }
@@ -449,122 +698,65 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             return;
         }
         tc::fence_after_sync();
-        float d[8];
-        tc::tmem_ld8(c.tbase + (uint32_t(32 * w) << 16) + kColD + 8 * db, d);
+        float dg[16], du[16];
+        tc::tmem_ld16(c.tbase + (uint32_t(32 * w) << 16) + kColD + 32 * db, dg);
+        if (p.kind == 0) {
+            tc::tmem_ld16(c.tbase + (uint32_t(32 * w) << 16) + kColD + 32 * db + 16, du);
+        }
         tc::wait_ld();
         tc::fence_before_sync();
         mbar_arrive(&s.acc_empty[db]);
-        ++pp.seg;
-        u = seg_end;
-        float part = 0.0f;
+        // term partials, smallest digit first
+        float pg = 0.0f, pu = 0.0f;
 #pragma unroll
-        for (int n = 0; n < kTerms; ++n) {
-            part += d[n];
+        for (int n = 0; n < tc::kDigitTerms; ++n) {
+            pg += dg[n];
         }
-        int nslot, slot;
-        tile_slots(p, tile, nslot, slot);
-        if (nslot > kMaxSlots) {
+        if (p.kind == 0) {
+#pragma unroll
+            for (int n = 0; n < tc::kDigitTerms; ++n) {
+                pu += du[n];
+            }
+        }
+        EpiTile et;
+        et.tile = tile;
+        tile_slots(p, tile, et.nslot, et.slot);
+        if (et.nslot > kMaxSlots) {
             if (i == 0) {
                 set_status(a.status, kStatusBadShape);
             }
             continue;
         }
-        float *ws = (p.kind == 0 ? a.part_gu : a.part_dn) + (size_t(tile) * kMaxSlots + slot) * 128;
-        unsigned *cnt = (p.kind == 0 ? a.cnt_gu : a.cnt_dn) + tile;
-        if (nslot > 1) {
-            ws[i] = part;
-            __threadfence();
-            epi_sync();
-            if (i == 0) {
-                const unsigned prev = atomicAdd(cnt, 1u);
-                s.last = (prev == unsigned(nslot - 1));
-                if (s.last) {
-                    *cnt = 0u;
-                }
+        if (et.slot == et.nslot - 1) {
+            // this CTA reduces the tile: keep the partial for later
+            if (nown < kOwnMax) {
+                s.own_part[nown][0][i] = pg;
+                s.own_part[nown][1][i] = pu;
+                own[nown++] = et;
+            } else if (i == 0) {
+                set_status(a.status, kStatusBadShape);
             }
-            epi_sync();
-            if (!s.last) {
-                continue;
-            }
-            __threadfence();
-            float sum = 0.0f;
-            const float *base = (p.kind == 0 ? a.part_gu : a.part_dn) + size_t(tile) * kMaxSlots * 128;
-            for (int k = 0; k < nslot; ++k) {
-                sum += (k == slot) ? part : __ldcg(base + k * 128 + i);
-            }
-            part = sum;
+            continue;
         }
+        const size_t stride = (p.kind == 0) ? 256 : 128;
+        float *base = (p.kind == 0 ? a.part_gu : a.part_dn) + size_t(tile) * kMaxSlots * stride;
+        base[et.slot * stride + i] = pg;
         if (p.kind == 0) {
-            // gate rows 0..63 (warps 0, 1), up rows 64..127 (warps 2, 3)
-            const int q = tile / kGateTiles;
-            const int j = tile - q * kGateTiles;
-            const int le = s.local[s.slot_of[q]];
-            const int row = 64 * j + (i & 63);
-            if (i >= 64) {
-                s.xch[i - 64] = __fadd_rn(L.up_b[size_t(le) * kDim + row], part);
-            }
-            epi_sync();
-            if (i < 64) {
-                const float g = __fadd_rn(L.gate_b[size_t(le) * kDim + row], part);
-                const float h = __fmul_rn(swiglu_ref(g, s.xch[i]), s.wts[s.slot_of[q]]);
-                uint32_t sc;
-                const uint32_t tb = tc::split_terms<kTerms>(h, sc);
-                const int k = row;  // down-projection K index
-                uint8_t *bd = a.bdown + (size_t(q) * kChunks + (k >> 4)) * kN * 16;
-#pragma unroll
-                for (int n = 0; n < kTerms; ++n) {
-                    bd[n * 16 + (k & 15)] = uint8_t(tb >> (8 * n));
-                }
-                if (lane == 0) {
-                    const int kb = k >> 5;
-#pragma unroll
-                    for (int n = 0; n < kTerms; ++n) {
-                        a.sfb_down[(size_t(q) * kBlocks + kb) * kTerms + n] = uint8_t(sc >> (8 * n));
-                    }
-                }
-            }
-            epi_sync();
-        } else {
-            const int row = 128 * tile + i;
-            if (row < kDim) {
-                float bsum = 0.0f;
-                for (int k = 0; k < s.n_local; ++k) {
-                    const int rank = s.slot_of[k];
-                    bsum = __fadd_rn(bsum, __fmul_rn(s.wts[rank], L.down_b[size_t(s.local[rank]) * kDim + row]));
-                }
-                const float o = __fadd_rn(part, bsum);
-                const float *xcur = (li == 0) ? a.x + size_t(t_token) * kDim : a.y + size_t(t_token) * kDim;
-                float *ycur = a.y + size_t(t_token) * kDim;
-                const float yv = (a.mode == 1) ? __fadd_rn(__ldcg(xcur + row), o) : o;
-                ycur[row] = yv;
-                s.part[i] = yv;
-            }
-            if (next_router) {
-                // router sums of the next (token, layer) over these rows
-                epi_sync();
-                const bool more_layers = (li + 1 < a.layer_end - a.layer_begin);
-                const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
-                const int step = t_token * (a.layer_end - a.layer_begin) + li;
-                double *acc = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
-                for (int e = w; e < a.experts + 1; e += kEpiWarps) {
-                    double v = 0.0;
-#pragma unroll
-                    for (int r4 = 0; r4 < 4; ++r4) {
-                        const int rr = lane + 32 * r4;
-                        const int r = 128 * tile + rr;
-                        if (r < kDim) {
-                            const float xr = more_layers ? s.part[rr] : __ldcg(a.x + size_t(t_token + 1) * kDim + r);
-                            v += (e < a.experts)
-                                     ? double(__ldg(N.router_w + size_t(e) * kDim + r)) * double(__fmul_rn(xr, N.norm_w[r]))
-                                     : double(__fmul_rn(xr, xr));
-                        }
-                    }
-                    v = warp_sum_d(v);
-                    if (lane == 0) {
-                        atomicAdd(acc + e, v);
-                    }
-                }
-            }
+            base[et.slot * stride + 128 + i] = pu;
+        }
+        epi_sync();
+        if (i == 0) {
+            unsigned *cnt = (p.kind == 0 ? a.cnt_gu : a.cnt_dn) + tile;
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+        }
+    }
+    for (int k = 0; k < nown; ++k) {
+        if (own[k].tile != first_owned) {
+            load_tile_ops(c, p, own[k].tile, t_token, li, next_router, ops);
+        }
+        finish_tile(c, p, own[k], ops, s.own_part[k][0][i], s.own_part[k][1][i], t_token, li, next_router);
+        if (aborted(s)) {
+            return;
         }
     }
 }
@@ -658,26 +850,87 @@ __device__ void warp_top4(Smem &s, int experts, bool check_bounds) {
     }
 }
 
+// Softmax of the selected logits (src/model.cpp:310-321) and this rank's
+// experts; thread 0, then published to the load warp.
+__device__ void publish_selection(Smem &s, const StackArgs &a, bool export_top) {
+    float maximum = -INFINITY;
+    float v[4], wv[4];
+    for (int q = 0; q < kTopK; ++q) {
+        v[q] = s.val[s.sel[q]];
+        maximum = (maximum < v[q]) ? v[q] : maximum;
+    }
+    float sum = 0.0f;
+    for (int q = 0; q < kTopK; ++q) {
+        wv[q] = expf(__fsub_rn(v[q], maximum));
+        sum = __fadd_rn(sum, wv[q]);
+    }
+    int n = 0;
+    for (int q = 0; q < kTopK; ++q) {
+        s.wts[q] = __fdiv_rn(wv[q], sum);
+        const int le = s.sel[q] - a.expert_begin;
+        s.local[q] = (le >= 0 && le < a.expert_count) ? le : -1;
+        if (s.local[q] >= 0) {
+            s.slot_of[n++] = q;
+        }
+    }
+    s.n_local = n;
+    mbar_arrive(&s.sel_full);
+    if (export_top) {
+        for (int q = 0; q < kTopK; ++q) {
+            a.top_idx[q] = s.sel[q];
+            a.top_w[q] = s.wts[q];
+        }
+    }
+}
+
+// Load warp: every step's stages, following the published selections; at the
+// end it waits until every load it issued has landed.
+__device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps, int nl) {
+    Pipe pp;
+    for (int step = 0; step < steps; ++step) {
+        if (!wait_bar(s, &s.sel_full, uint32_t(step) & 1, a.status)) {
+            break;
+        }
+        int le[kTopK];
+        const int n = s.n_local;
+#pragma unroll
+        for (int q = 0; q < kTopK; ++q) {
+            le[q] = (q < n) ? s.local[s.slot_of[q]] : 0;
+        }
+        Ctx c = c0;
+        c.L = &a.layers[a.layer_begin + step % nl];
+        if (!produce_phase(c, gateup_phase(n), le, pp) || !produce_phase(c, down_phase(n), le, pp)) {
+            break;
+        }
+    }
+    for (uint32_t k = 0; k < kStages && k < pp.stage; ++k) {
+        const uint32_t last = pp.stage - 1 - k;
+        tc::mbar_wait(&s.full[last % kStages], (last / kStages) & 1);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    Smem &s = *reinterpret_cast<Smem *>(smem_raw);
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int E = a.experts;
     const int nl = a.layer_end - a.layer_begin;
+    const int steps = a.tokens * nl;
     unsigned gen = 0;
 
     if (threadIdx.x == 0) {
         s.abort = 0;
-        gen = *reinterpret_cast<volatile unsigned *>(a.barrier + 1);
         for (int i = 0; i < kStages; ++i) {
-            tc::mbar_init(&s.full[i], 32 * kLoadWarps);
+            tc::mbar_init(&s.full[i], 1);
             tc::mbar_init(&s.empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&s.acc_full[i], 1);
             tc::mbar_init(&s.acc_empty[i], 32 * kEpiWarps);
         }
+        tc::mbar_init(&s.sel_full, 1);
+        tc::mbar_init(&s.setup, 1);
         tc::mbar_init(&s.fin, 1);
         tc::fence_mbar_init();
     }
@@ -685,405 +938,313 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         tc::tmem_alloc(&s.tmem, kTmemCols);
         tc::tmem_relinquish();
     }
-    // zero the unused B rows (terms 4..7) once
-    for (int i = threadIdx.x; i < kChunks * kN * 16 / 16; i += kThreads) {
-        const int ch = i / kN, n = i % kN;
-        if (n >= kTerms) {
-            *reinterpret_cast<uint4 *>(&s.bgu[ch][n][0]) = make_uint4(0, 0, 0, 0);
-            for (int q = 0; q < kDownSlots; ++q) {
-                *reinterpret_cast<uint4 *>(&s.bdown[q][ch][n][0]) = make_uint4(0, 0, 0, 0);
-            }
-        }
+    // padding of the gate/up block codes (K-blocks 90..95)
+    if (threadIdx.x < kCodeBytes - kBlocks) {
+        s.gcode[kBlocks + threadIdx.x] = 127u;
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tbase = s.tmem;
-    Pipe pipe;
+    const Ctx c0{&a, &a.layers[a.layer_begin], &s, tbase};
 
-    // Router sums of (token 0, first layer) in stack mode.
-    if (a.mode == 1) {
-        const StackLayer &L = a.layers[a.layer_begin];
-        const int r0 = range_lo(blockIdx.x, gridDim.x, kDim);
-        const int r1 = range_lo(blockIdx.x + 1, gridDim.x, kDim);
-        for (int e = warp; e < E + 1; e += kThreads / 32) {
-            const int r = r0 + lane;
-            double v = 0.0;
-            if (r < r1) {
-                const float xr = a.x[r];
-                v = (e < E) ? double(__ldg(L.router_w + size_t(e) * kDim + r)) * double(__fmul_rn(xr, L.norm_w[r]))
-                            : double(__fmul_rn(xr, xr));
-            }
-            v = warp_sum_d(v);
-            if (lane == 0) {
-                atomicAdd(a.acc + e, v);
+    if (warp == kTmaWarp) {
+        if (lane == 0) {
+            run_loads(c0, s, a, steps, nl);
+        }
+    } else {
+        // ---------------- compute group: warps 0-8 ----------------
+        const int ct = threadIdx.x;  // 0..287
+        Pipe pipe;
+        // Router sums of (token 0, first layer) in stack mode.
+        if (a.mode == 1) {
+            const StackLayer &L = a.layers[a.layer_begin];
+            const int r0 = range_lo(blockIdx.x, gridDim.x, kDim);
+            const int r1 = range_lo(blockIdx.x + 1, gridDim.x, kDim);
+            for (int e = warp; e < E + 1; e += kComputeWarps) {
+                double v = 0.0;
+                for (int r = r0 + lane; r < r1; r += 32) {
+                    const float xr = a.x[r];
+                    v += (e < E) ? double(__ldg(L.router_w + size_t(e) * kDim + r)) * double(__fmul_rn(xr, L.norm_w[r]))
+                                 : double(__fmul_rn(xr, xr));
+                }
+                v = warp_sum_d(v);
+                if (lane == 0) {
+                    atomicAdd(a.acc + e, v);
+                }
             }
         }
-    }
-    bool ok = grid_barrier(a.barrier, gen, a.status, s);
+        bool ok = grid_barrier(a.barrier, gen, a.status, s);
 
-    for (int t = 0; ok && t < a.tokens; ++t) {
-        for (int li = 0; ok && li < nl; ++li) {
-            const int l = a.layer_begin + li;
-            const StackLayer &L = a.layers[l];
-            const int step = t * nl + li;
-            const float *xcur = (li == 0) ? a.x + size_t(t) * kDim : a.y + size_t(t) * kDim;
+        for (int t = 0; ok && t < a.tokens; ++t) {
+            for (int li = 0; ok && li < nl; ++li) {
+                const int l = a.layer_begin + li;
+                const StackLayer &L = a.layers[l];
+                const int step = t * nl + li;
+                const float *xcur = (li == 0) ? a.x + size_t(t) * kDim : a.y + size_t(t) * kDim;
+                const bool export_top = (blockIdx.x == 0 && t == a.tokens - 1 && li == nl - 1);
 
-            stamp(a, step, 0);
-            // ---------------- A: selection ----------------
-            if (a.mode == 1) {
-                const double *acc = a.acc + size_t(step & 1) * (kMaxExperts + 1);
-                if (threadIdx.x == 0) {
+                stamp(a, step, 0);
+                // x (and norm weight) loads of the B split, issued first:
+                // warp w takes K-blocks w + 9 i
+                constexpr int kPasses = kBlocks / kComputeWarps;  // 10
+                static_assert(kPasses * kComputeWarps == kBlocks, "split passes");
+                float xr[kPasses], gr[kPasses];
+#pragma unroll
+                for (int pi = 0; pi < kPasses; ++pi) {
+                    const int k = (warp + pi * kComputeWarps) * 32 + lane;
+                    xr[pi] = __ldcg(xcur + k);
+                    gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
+                }
+                float scale = 1.0f;
+                // ---------------- A: selection ----------------
+                if (a.mode == 1) {
+                    const double *acc = a.acc + size_t(step & 1) * (kMaxExperts + 1);
                     const float ss = float(__ldcg(acc + E));
-                    s.scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(kDim)), 1.0e-5f)));
-                }
-                __syncthreads();
-                for (int e = threadIdx.x; e < E; e += kThreads) {
-                    const double p = __ldcg(acc + e);
-                    const float lg = float(double(L.router_b[e]) + double(s.scale) * p);
-                    s.logit[e] = lg;
-                    s.val[e] = lg;
-                }
-                if (blockIdx.x == 0) {
-                    double *other = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
-                    for (int e = threadIdx.x; e < E + 1; e += kThreads) {
-                        other[e] = 0.0;
+                    scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(kDim)), 1.0e-5f)));
+                    for (int e = ct; e < E; e += kComputeThreads) {
+                        const double p = __ldcg(acc + e);
+                        const float lg = float(double(L.router_b[e]) + double(scale) * p);
+                        s.logit[e] = lg;
+                        s.val[e] = lg;
                     }
-                }
-                __syncthreads();
-                if (warp == 0) {
-                    warp_top4(s, E, false);
-                }
-                __syncthreads();
-            } else {
-                // CTA e < E: expert e's logit and the bound on the reference's f32 chain.
-                for (int e = blockIdx.x; e < E; e += gridDim.x) {
-                    const float *wr = L.router_w + size_t(e) * kDim;
-                    constexpr int kCols = kDim / (kThreads / 32);  // 320 per warp
-                    constexpr int kPer = (kCols + 31) / 32;        // 10 per lane
-                    const int c0 = warp * kCols;
-                    float p[kPer];
-                    double loc = 0.0;
-#pragma unroll
-                    for (int j = 0; j < kPer; ++j) {
-                        const int off = lane * kPer + j;
-                        p[j] = (off < kCols) ? __fmul_rn(__ldg(wr + c0 + off), __ldcg(xcur + c0 + off)) : 0.0f;
-                        loc += double(p[j]);
-                    }
-                    double inc = loc;
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const double tt = __shfl_up_sync(0xffffffffu, inc, o);
-                        if (lane >= o) {
-                            inc += tt;
+                    if (blockIdx.x == 0) {
+                        double *other = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
+                        for (int e = ct; e < E + 1; e += kComputeThreads) {
+                            other[e] = 0.0;
                         }
                     }
-                    __syncthreads();
-                    if (lane == 31) {
-                        s.red[warp] = inc;
-                    }
-                    __syncthreads();
-                    double base = double(L.router_b[e]);
-                    double total = 0.0;
-                    for (int k = 0; k < kThreads / 32; ++k) {
-                        if (k < warp) {
-                            base += s.red[k];
+                    compute_sync();
+                    if (warp == 0) {
+                        warp_top4(s, E, false);
+                        __syncwarp();
+                        if (lane == 0) {
+                            publish_selection(s, a, export_top);
                         }
-                        total += s.red[k];
+                        __syncwarp();
                     }
-                    double run = base + inc - loc;
-                    double abs_sum = 0.0;
+                } else {
+                    // CTA e < E: expert e's logit and the bound on the reference's f32 chain.
+                    for (int e = blockIdx.x; e < E; e += gridDim.x) {
+                        const float *wr = L.router_w + size_t(e) * kDim;
+                        constexpr int kCols = kDim / kComputeWarps;  // 320 per warp
+                        constexpr int kPer = (kCols + 31) / 32;      // 10 per lane
+                        const int c0 = warp * kCols;
+                        float p[kPer];
+                        double loc = 0.0;
 #pragma unroll
-                    for (int j = 0; j < kPer; ++j) {
-                        run += double(p[j]);
-                        abs_sum += fabs(run);
+                        for (int j = 0; j < kPer; ++j) {
+                            const int off = lane * kPer + j;
+                            p[j] = (off < kCols) ? __fmul_rn(__ldg(wr + c0 + off), __ldcg(xcur + c0 + off)) : 0.0f;
+                            loc += double(p[j]);
+                        }
+                        double inc = loc;
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const double tt = __shfl_up_sync(0xffffffffu, inc, o);
+                            if (lane >= o) {
+                                inc += tt;
+                            }
+                        }
+                        compute_sync();
+                        if (lane == 31) {
+                            s.red[warp] = inc;
+                        }
+                        compute_sync();
+                        double base = double(L.router_b[e]);
+                        double total = 0.0;
+                        for (int k = 0; k < kComputeWarps; ++k) {
+                            if (k < warp) {
+                                base += s.red[k];
+                            }
+                            total += s.red[k];
+                        }
+                        double run = base + inc - loc;
+                        double abs_sum = 0.0;
+#pragma unroll
+                        for (int j = 0; j < kPer; ++j) {
+                            run += double(p[j]);
+                            abs_sum += fabs(run);
+                        }
+                        abs_sum = warp_sum_d(abs_sum);
+                        compute_sync();
+                        if (lane == 0) {
+                            s.red[warp] = abs_sum;
+                        }
+                        compute_sync();
+                        if (threadIdx.x == 0) {
+                            double abs_total = 0.0;
+                            for (int k = 0; k < kComputeWarps; ++k) {
+                                abs_total += s.red[k];
+                            }
+                            const double logit = double(L.router_b[e]) + total;
+                            a.logits[e] = float(logit);
+                            a.bounds[e] = float((1.02 * 5.9604644775390625e-08 * abs_total +
+                                                 5.9604644775390625e-08 * fabs(logit) + 1e-30) *
+                                                1.0001);
+                        }
+                        compute_sync();
                     }
-                    abs_sum = warp_sum_d(abs_sum);
-                    __syncthreads();
-                    if (lane == 0) {
-                        s.red[warp] = abs_sum;
+                    ok = grid_barrier(a.barrier, gen, a.status, s);
+                    if (!ok) {
+                        break;
                     }
-                    __syncthreads();
+                    for (int e = ct; e < E; e += kComputeThreads) {
+                        s.logit[e] = __ldcg(a.logits + e);
+                        s.bound[e] = __ldcg(a.bounds + e);
+                        s.val[e] = s.logit[e];
+                    }
+                    compute_sync();
+                    if (warp == 0) {
+                        warp_top4(s, E, true);
+                    }
+                    compute_sync();
+                    if (s.amb) {
+                        float lower = INFINITY;
+                        for (int q = 0; q < kTopK; ++q) {
+                            lower = fminf(lower, s.logit[s.sel[q]] - s.bound[s.sel[q]]);
+                        }
+                        for (int e = ct; e < E; e += kComputeThreads) {
+                            if (!(s.logit[e] + s.bound[e] < lower)) {
+                                s.val[e] = exact_logit(L.router_w + size_t(e) * kDim, L.router_b[e], xcur);
+                            }
+                        }
+                        compute_sync();
+                        if (threadIdx.x == 0) {
+                            int idx[4];
+                            select_top4_ref(s.val, E, idx);
+                            for (int q = 0; q < kTopK; ++q) {
+                                s.sel[q] = idx[q];
+                            }
+                            if (blockIdx.x == 0) {
+                                atomicAdd(&a.counters[0], 1ull);
+                            }
+                        }
+                        compute_sync();
+                    }
                     if (threadIdx.x == 0) {
-                        double abs_total = 0.0;
-                        for (int k = 0; k < kThreads / 32; ++k) {
-                            abs_total += s.red[k];
-                        }
-                        const double logit = double(L.router_b[e]) + total;
-                        a.logits[e] = float(logit);
-                        a.bounds[e] = float((1.02 * 5.9604644775390625e-08 * abs_total +
-                                             5.9604644775390625e-08 * fabs(logit) + 1e-30) * 1.0001);
+                        publish_selection(s, a, export_top);
                     }
-                    __syncthreads();
                 }
+                stamp(a, step, 1);
+                // B for gate/up: h split into terms; SFB into tensor memory
+#pragma unroll
+                for (int pi = 0; pi < kPasses; ++pi) {
+                    const int kb = warp + pi * kComputeWarps;
+                    const float h = (a.mode == 1) ? __fmul_rn(__fmul_rn(xr[pi], scale), gr[pi]) : xr[pi];
+                    const uint32_t code = tc::digit_split_store(h, &s.bgu[kb][0], lane);
+                    if (lane == 0) {
+                        s.gcode[kb] = uint8_t(code);
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                compute_sync();
+                if (warp < kEpiWarps) {
+                    for (int g = 0; g < kSfChunks; ++g) {
+                        const uint32_t v = tc::digit_scales4(*reinterpret_cast<const uint32_t *>(&s.gcode[4 * g]), lane);
+                        tc::tmem_st4(tbase + (uint32_t(32 * warp) << 16) + kColSfbG + 4 * g, v, 0u, 0u, 0u);
+                    }
+                    tc::wait_st();
+                }
+                tc::fence_before_sync();
+                compute_sync();
+                tc::fence_after_sync();
+
+                stamp(a, step, 2);
+                // ---------------- B: gate/up ----------------
+                Ctx cx{&a, &L, &s, tbase};
+                const Phase pb = gateup_phase(s.n_local);
+                if (warp < kEpiWarps) {
+                    run_epilogue(cx, pb, pipe, t, li, false);
+                } else if (warp == kMmaWarp && lane == 0) {
+                    run_mma(cx, pb, pipe);
+                }
+                __syncwarp();
+                stamp(a, step, 3);
                 ok = grid_barrier(a.barrier, gen, a.status, s);
                 if (!ok) {
                     break;
                 }
-                for (int e = threadIdx.x; e < E; e += kThreads) {
-                    s.logit[e] = __ldcg(a.logits + e);
-                    s.bound[e] = __ldcg(a.bounds + e);
-                    s.val[e] = s.logit[e];
-                }
-                __syncthreads();
-                if (warp == 0) {
-                    warp_top4(s, E, true);
-                }
-                __syncthreads();
-                if (s.amb) {
-                    float lower = INFINITY;
+                stamp(a, step, 4);
+                // ---------------- C: down ----------------
+                // B for down: the w * hidden terms (written by phase B's reducers)
+                // of the experts this CTA's down units touch (at most kDownSlots),
+                // into shared memory; their scales into tensor memory.
+                if (threadIdx.x == 0) {
+                    // bdown slots of the experts this CTA's down units touch
+                    // (at most kDownSlots), fetched by bulk copies
+                    const int ku_tile = s.n_local * kPairs;
+                    const int units = kTiles * ku_tile;
+                    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
+                    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
                     for (int q = 0; q < kTopK; ++q) {
-                        lower = fminf(lower, s.logit[s.sel[q]] - s.bound[s.sel[q]]);
+                        s.dslot[q] = -1;
                     }
-                    for (int e = threadIdx.x; e < E; e += kThreads) {
-                        if (!(s.logit[e] + s.bound[e] < lower)) {
-                            s.val[e] = exact_logit(L.router_w + size_t(e) * kDim, L.router_b[e], xcur);
-                        }
-                    }
-                    __syncthreads();
-                    if (threadIdx.x == 0) {
-                        int idx[4];
-                        select_top4_ref(s.val, E, idx);
-                        for (int q = 0; q < kTopK; ++q) {
-                            s.sel[q] = idx[q];
-                        }
-                        if (blockIdx.x == 0) {
-                            atomicAdd(&a.counters[0], 1ull);
-                        }
-                    }
-                    __syncthreads();
-                }
-            }
-            stamp(a, step, 1);
-            // softmax (src/model.cpp:310-321) and ownership
-            if (threadIdx.x == 0) {
-                float maximum = -INFINITY;
-                float v[4], wv[4];
-                for (int q = 0; q < kTopK; ++q) {
-                    v[q] = s.val[s.sel[q]];
-                    maximum = (maximum < v[q]) ? v[q] : maximum;
-                }
-                float sum = 0.0f;
-                for (int q = 0; q < kTopK; ++q) {
-                    wv[q] = expf(__fsub_rn(v[q], maximum));
-                    sum = __fadd_rn(sum, wv[q]);
-                }
-                int n = 0;
-                for (int q = 0; q < kTopK; ++q) {
-                    s.wts[q] = __fdiv_rn(wv[q], sum);
-                    const int le = s.sel[q] - a.expert_begin;
-                    s.local[q] = (le >= 0 && le < a.expert_count) ? le : -1;
-                    if (s.local[q] >= 0) {
-                        s.slot_of[n++] = q;
-                    }
-                }
-                s.n_local = n;
-                if (blockIdx.x == 0 && t == a.tokens - 1 && li == nl - 1) {
-                    for (int q = 0; q < kTopK; ++q) {
-                        a.top_idx[q] = s.sel[q];
-                        a.top_w[q] = s.wts[q];
-                    }
-                }
-            }
-            __syncthreads();
-            // B for gate/up: h split into terms; SFB into tensor memory.
-            // this warp's K-blocks: kb2 = warp + 9 i, 5 passes of two blocks;
-            // all x (and norm weight) loads are issued up front
-            constexpr int kPasses = (kBlocks / 2 + kThreads / 32 - 1) / (kThreads / 32);
-            float xr[kPasses][2], gr[kPasses][2];
-#pragma unroll
-            for (int pi = 0; pi < kPasses; ++pi) {
-                const int kb2 = warp + pi * (kThreads / 32);
-#pragma unroll
-                for (int z = 0; z < 2; ++z) {
-                    const int k = (2 * kb2 + z) * 32 + lane;
-                    xr[pi][z] = kb2 < kBlocks / 2 ? __ldcg(xcur + k) : 0.0f;
-                    gr[pi][z] = (kb2 < kBlocks / 2 && a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
-                }
-            }
-#pragma unroll
-            for (int pi = 0; pi < kPasses; ++pi) {
-                const int kb2 = warp + pi * (kThreads / 32);
-                if (kb2 >= kBlocks / 2) {
-                    break;
-                }
-                // two independent K-blocks per pass (interleaved dependency chains)
-                float h[2];
-#pragma unroll
-                for (int z = 0; z < 2; ++z) {
-                    h[z] = (a.mode == 1) ? __fmul_rn(__fmul_rn(xr[pi][z], s.scale), gr[pi][z]) : xr[pi][z];
-                }
-                uint32_t sc[2], tb[2];
-#pragma unroll
-                for (int z = 0; z < 2; ++z) {
-                    tb[z] = tc::split_terms<kTerms>(h[z], sc[z]);
-                }
-#pragma unroll
-                for (int z = 0; z < 2; ++z) {
-                    const int kb = 2 * kb2 + z;
-                    const int k = kb * 32 + lane;
-#pragma unroll
-                    for (int n = 0; n < kTerms; ++n) {
-                        s.bgu[k >> 4][n][k & 15] = uint8_t(tb[z] >> (8 * n));
-                    }
-                    if (lane == 0) {
-#pragma unroll
-                        for (int n = 0; n < kTerms; ++n) {
-                            s.sfbg[kb][n] = uint8_t(sc[z] >> (8 * n));
-                        }
-                    }
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __threadfence_block();
-            __syncthreads();
-            if (warp >= kEpiWarps && warp < kEpiWarps + kLoadWarps) {
-                const int q4 = warp & 3;
-                for (int g = 0; g < kSfChunks; ++g) {
-                    uint32_t v = 0;
-                    if (lane < kTerms) {
-                        for (int k = 0; k < 4; ++k) {
-                            const int kb = 4 * g + k;
-                            v |= (kb < kBlocks ? uint32_t(s.sfbg[kb][lane]) : 127u) << (8 * k);
-                        }
-                    }
-                    tc::tmem_st4(tbase + (uint32_t(32 * q4) << 16) + kColSfbG + 4 * g, v, 0u, 0u, 0u);
-                }
-                tc::wait_st();
-            }
-            tc::fence_before_sync();
-            __syncthreads();
-            tc::fence_after_sync();
-
-            stamp(a, step, 2);
-            // ---------------- B: gate/up ----------------
-            Ctx cx{&a, &L, &s, tbase};
-            const Phase pb{0, s.n_local * kGateTiles, kBlocks};
-            if (warp < kEpiWarps) {
-                run_epilogue(cx, pb, pipe, t, li, false);
-            } else if (warp < kEpiWarps + kLoadWarps) {
-                run_loader(cx, pb, pipe);
-            } else if (lane == 0) {
-                run_mma(cx, pb, pipe);
-            } else {
-                prefetch_down(cx, s.n_local * kBlocks);
-            }
-            __syncthreads();
-            stamp(a, step, 3);
-            ok = grid_barrier(a.barrier, gen, a.status, s);
-            if (!ok) {
-                break;
-            }
-            stamp(a, step, 4);
-            // ---------------- C: down ----------------
-            // B for down: the w * hidden terms (written by phase B's reducers)
-            // of the experts this CTA's down units touch (at most kDownSlots),
-            // into shared memory; their scales into tensor memory.
-            if (threadIdx.x == 0) {
-                const int ku_tile = s.n_local * kBlocks;
-                const int units = kDownTiles * ku_tile;
-                const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-                const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-                for (int q = 0; q < kTopK; ++q) {
-                    s.dslot[q] = -1;
-                }
-                int nd = 0;
-                for (int u = u0; u < u1;) {
-                    const int ku = u % ku_tile;
-                    const int q = ku / kBlocks;
-                    if (s.dslot[q] < 0) {
-                        if (nd < kDownSlots) {
-                            s.dslot[q] = nd++;
-                        } else {
-                            set_status(a.status, kStatusBadShape);
-                            s.dslot[q] = 0;
-                        }
-                    }
-                    u += min(kBlocks - ku % kBlocks, u1 - u);
-                }
-            }
-            __syncthreads();
-            {
-                constexpr int kPer = (kDownSlots * kChunks * kTerms + kThreads - 1) / kThreads;
-                uint4 buf[kPer];
-                int dst[kPer];
-#pragma unroll
-                for (int k = 0; k < kPer; ++k) {
-                    const int i = threadIdx.x + k * kThreads;  // over (q in 0..3, chunk, term) of used experts
-                    dst[k] = -1;
-                    int seen = 0;
-                    for (int q = 0; q < kTopK; ++q) {
-                        if (s.dslot[q] >= 0 && q < s.n_local) {
-                            const int base = seen * kChunks * kTerms;
-                            if (i >= base && i < base + kChunks * kTerms) {
-                                const int r = i - base;
-                                const int ch = r / kTerms;
-                                const int n = r - ch * kTerms;
-                                buf[k] = __ldcg(reinterpret_cast<const uint4 *>(a.bdown + ((size_t(q) * kChunks + ch) * kN + n) * 16));
-                                dst[k] = (s.dslot[q] * kChunks + ch) * kN + n;
-                            }
-                            ++seen;
-                        }
-                    }
-                }
-#pragma unroll
-                for (int k = 0; k < kPer; ++k) {
-                    if (dst[k] >= 0) {
-                        *reinterpret_cast<uint4 *>(&s.bdown[0][0][0][0] + size_t(dst[k]) * 16) = buf[k];
-                    }
-                }
-            }
-            for (int i = threadIdx.x; i < kTopK * kBlocks; i += kThreads) {
-                const int q = i / kBlocks;
-                if (q < s.n_local && s.dslot[q] >= 0) {
-                    const uint32_t w4 = __ldcg(reinterpret_cast<const unsigned int *>(a.sfb_down) + i);
-                    *reinterpret_cast<uint32_t *>(&s.sfbd[s.dslot[q]][i % kBlocks][0]) = w4;
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncthreads();
-            if (warp >= kEpiWarps && warp < kEpiWarps + kLoadWarps) {
-                const int q4 = warp & 3;
-                for (int d = 0; d < kDownSlots; ++d) {
-                    for (int g = 0; g < kSfChunks; ++g) {
-                        uint32_t v = 0;
-                        if (lane < kTerms) {
-                            for (int k = 0; k < 4; ++k) {
-                                const int kb = 4 * g + k;
-                                v |= (kb < kBlocks ? uint32_t(s.sfbd[d][kb][lane]) : 127u) << (8 * k);
+                    int qs[kDownSlots];
+                    int nd = 0;
+                    for (int u = u0; u < u1;) {
+                        const int ku = u % ku_tile;
+                        const int q = ku / kPairs;
+                        if (s.dslot[q] < 0) {
+                            if (nd < kDownSlots) {
+                                qs[nd] = q;
+                                s.dslot[q] = nd++;
+                            } else {
+                                set_status(a.status, kStatusBadShape);
+                                s.dslot[q] = 0;
                             }
                         }
-                        tc::tmem_st4(tbase + (uint32_t(32 * q4) << 16) + kColSfbD + 4 * (d * kSfChunks + g), v, 0u, 0u,
-                                     0u);
+                        u += min(kPairs - ku % kPairs, u1 - u);
+                    }
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc::mbar_expect_tx(&s.setup, uint32_t(nd) * uint32_t(kBlocks * kBRowBytes + kCodeBytes));
+                    for (int d = 0; d < nd; ++d) {
+                        bulk_load(&s.bdown[d][0][0], a.bdown + size_t(qs[d]) * kBlocks * kBRowBytes, kBlocks * kBRowBytes,
+                                  &s.setup);
+                        bulk_load(&s.dcode[d][0], a.sfb_down + size_t(qs[d]) * kCodeBytes, kCodeBytes, &s.setup);
                     }
                 }
-                tc::wait_st();
+                if (!wait_bar(s, &s.setup, uint32_t(step) & 1, a.status)) {
+                    *reinterpret_cast<volatile int *>(&s.abort) = 1;
+                }
+                compute_sync();
+                if (warp < kEpiWarps) {
+                    for (int d = 0; d < kDownSlots; ++d) {
+                        for (int g = 0; g < kSfChunks; ++g) {
+                            const uint32_t v =
+                                tc::digit_scales4(*reinterpret_cast<const uint32_t *>(&s.dcode[d][4 * g]), lane);
+                            tc::tmem_st4(tbase + (uint32_t(32 * warp) << 16) + kColSfbD + 4 * (d * kSfChunks + g), v,
+                                         0u, 0u, 0u);
+                        }
+                    }
+                    tc::wait_st();
+                }
+                tc::fence_before_sync();
+                compute_sync();
+                tc::fence_after_sync();
+                stamp(a, step, 5);
+                const bool next_router = (a.mode == 1) && (li + 1 < nl || t + 1 < a.tokens);
+                const Phase pc = down_phase(s.n_local);
+                if (warp < kEpiWarps) {
+                    run_epilogue(cx, pc, pipe, t, li, next_router);
+                } else if (warp == kMmaWarp && lane == 0) {
+                    run_mma(cx, pc, pipe);
+                }
+                __syncwarp();
+                stamp(a, step, 6);
+                ok = grid_barrier(a.barrier, gen, a.status, s);
+                stamp(a, step, 7);
             }
-            tc::fence_before_sync();
-            __syncthreads();
-            tc::fence_after_sync();
-            stamp(a, step, 5);
-            const bool next_router =
-                (a.mode == 1) && (li + 1 < nl || t + 1 < a.tokens);
-            const Phase pc{1, kDownTiles, s.n_local * kBlocks};
-            if (warp < kEpiWarps) {
-                run_epilogue(cx, pc, pipe, t, li, next_router);
-            } else if (warp < kEpiWarps + kLoadWarps) {
-                run_loader(cx, pc, pipe);
-            } else if (lane == 0) {
-                run_mma(cx, pc, pipe);
-            }
-            __syncthreads();
-            stamp(a, step, 6);
-            ok = grid_barrier(a.barrier, gen, a.status, s);
-            stamp(a, step, 7);
         }
-    }
-    // drain: this thread's copies; the MMA thread waits for its MMAs; then
-    // tensor memory is freed
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    if (warp == kEpiWarps + kLoadWarps && lane == 0) {
-        tc::mma_commit(&s.fin);
-        tc::mbar_wait(&s.fin, 0);
+        if (!ok) {
+            *reinterpret_cast<volatile int *>(&s.abort) = 1;
+        }
+        // the MMA thread waits for its MMAs
+        if (warp == kMmaWarp && lane == 0) {
+            tc::mma_commit(&s.fin);
+            tc::mbar_wait(&s.fin, 0);
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -1096,18 +1257,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
 } // namespace
 
 size_t decode_tc_smem_bytes() {
-    return sizeof(Smem);
+    return sizeof(Smem) + 1024;
 }
 
 void configure_decode_tc() {
-    cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(Smem)));
+    cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(decode_tc_smem_bytes()));
 }
 
 cudaError_t launch_decode_tc(const StackArgs &args, int sms, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(unsigned(sms));
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sizeof(Smem);
+    cfg.dynamicSmemBytes = decode_tc_smem_bytes();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;

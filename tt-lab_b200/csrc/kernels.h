@@ -58,6 +58,21 @@ void launch_add(const float *residual, const float *moe, float *out, int n, cuda
 void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream);
 
 // ---- persistent decode (decode_stack.cu) ----
+// A CUtensorMap, kept opaque here (128 bytes, 64-byte aligned).
+struct alignas(64) TmaDesc {
+    unsigned long long w[16];
+};
+
+// Tensor maps of one layer's packed expert matrices: the nibble rows as bytes
+// (all local experts; box coordinates (byte of the row, row, expert); boxes
+// of 128 bytes x 128 rows, 128-byte swizzle; bytes past 1440 read as zero).
+enum TmaIndex {
+    kTmaGate,
+    kTmaUp,
+    kTmaDown,
+    kTmaCount
+};
+
 struct StackLayer {
     const float *router_w;
     const float *router_b;
@@ -68,6 +83,7 @@ struct StackLayer {
     const float *gate_b;
     const float *up_b;
     const float *down_b;
+    const TmaDesc *tma;  // [kTmaCount] in device memory (tensor-core decode)
 };
 
 struct StackArgs {
@@ -87,16 +103,16 @@ struct StackArgs {
     float *hidden;             // [4][2880]
     int32_t *top_idx;          // [4] selection of the last (token, layer)
     float *top_w;              // [4]
-    unsigned *barrier;         // [2] arrival count (zeroed by the host), generation
+    unsigned *barrier;         // [2] arrival count (zeroed by the host before a launch), generation
     uint32_t *status;
     unsigned long long *counters;
     // tensor-core decode workspace
-    float *part_gu;            // [4 * 45 tiles][16 slots][128] gate/up tile partials
+    float *part_gu;            // [4 * 23 tiles][16 slots][256] gate/up tile partials
     float *part_dn;            // [23 tiles][16 slots][128] down tile partials
-    unsigned *cnt_gu;          // [4 * 45] contributor counters (zeroed by the host)
+    unsigned *cnt_gu;          // [4 * 23] contributor counters (zeroed by the host)
     unsigned *cnt_dn;          // [23]
-    uint8_t *bdown;            // [4][180][8][16] down B operand: E4M3 terms of w * hidden
-    uint8_t *sfb_down;         // [4][90][4] their E8M0 scales
+    uint8_t *bdown;            // [4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
+    uint8_t *sfb_down;         // [4][96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
 };

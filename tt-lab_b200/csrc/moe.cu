@@ -6,6 +6,7 @@
 // ranks combine their partial outputs with NCCL over NVLink.  The router is
 // replicated (it is 0.7% of a layer's bytes) so every rank derives the same
 // top-4 without an exchange.
+#include <cuda.h>  // CUtensorMap types; the encoder is resolved through the runtime
 #include <cuda_runtime.h>
 #include <nccl.h>
 
@@ -95,6 +96,7 @@ struct ttl_moe {
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
     StackLayer *d_layers = nullptr;   // [layers]
+    TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     std::vector<StackLayer> host_layers;
     double *d_acc = nullptr;          // [2][kMaxExperts + 1]
     unsigned *d_barrier = nullptr;    // [2]
@@ -253,9 +255,68 @@ int enqueue_decode_layer(ttl_moe *h, int layer, const float *x, int mode, const 
     return TTL_OK;
 }
 
+static_assert(sizeof(CUtensorMap) == sizeof(TmaDesc) && alignof(TmaDesc) >= 64, "tensor map size");
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static const EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            p = nullptr;
+        }
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// Tensor maps of one layer's packed matrices (order of TmaIndex): the nibble
+// rows as bytes, 128-byte x 128-row boxes with 128-byte swizzle (the K-major
+// layout of the kind::mxf4 A operand).
+int build_layer_maps(ttl_moe *h, const LayerStore &st, TmaDesc *out) {
+    const EncodeTiledFn enc = encode_tiled();
+    if (!enc) {
+        return fail(h, TTL_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    }
+    const cuuint64_t experts = cuuint64_t(h->expert_count);
+    const cuuint32_t ones[3] = {1, 1, 1};
+    CUtensorMap maps[kTmaCount];
+    bool ok = true;
+    auto weights = [&](int idx, const uint8_t *base) {
+        const cuuint64_t dims[3] = {cuuint64_t(kNibbleRowBytes), cuuint64_t(kDim), experts};
+        const cuuint64_t strides[2] = {cuuint64_t(kNibbleRowBytes), cuuint64_t(kPackedMatrixBytes)};
+        const cuuint32_t box[3] = {128, 128, 1};
+        ok = ok && enc(&maps[idx], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides, box, ones,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    weights(kTmaGate, st.gate);
+    weights(kTmaUp, st.up);
+    weights(kTmaDown, st.down);
+    if (!ok) {
+        return fail(h, TTL_ERR_CUDA, "cuTensorMapEncodeTiled rejected a weight tensor map");
+    }
+    TTL_TRY_CUDA(h, cudaMemcpy(out, maps, sizeof(maps), cudaMemcpyHostToDevice));
+    return TTL_OK;
+}
+
 int push_layer_descriptor(ttl_moe *h, int layer) {
     const LayerDev L = layer_view(h, layer);
-    StackLayer d{L.router_w, L.router_b, L.norm_w, L.gate, L.up, L.down, L.gate_b, L.up_b, L.down_b};
+    StackLayer d{L.router_w, L.router_b, L.norm_w, L.gate, L.up, L.down, L.gate_b, L.up_b, L.down_b, nullptr};
+    const LayerStore &st = h->layers[size_t(layer)];
+    if (st.gate && st.up && st.down) {
+        TmaDesc *maps = h->d_tma + size_t(layer) * kTmaCount;
+        const int rc = build_layer_maps(h, st, maps);
+        if (rc) {
+            return rc;
+        }
+        d.tma = maps;
+    }
     h->host_layers[size_t(layer)] = d;
     TTL_TRY_CUDA(h, cudaMemcpy(h->d_layers + layer, &d, sizeof(d), cudaMemcpyHostToDevice));
     return TTL_OK;
@@ -302,6 +363,11 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
     }
     if (h->use_tc) {
+        for (int l = begin; l < end; ++l) {
+            if (!h->host_layers[size_t(l)].tma) {
+                return fail(h, TTL_ERR_STATE, "layer " + std::to_string(l) + " has no tensor maps");
+            }
+        }
         TTL_TRY_CUDA(h, launch_decode_tc(a, h->sms, h->stream));
     } else {
         TTL_TRY_CUDA(h, launch_decode_stack(a, h->sms, h->stream));
@@ -517,13 +583,14 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_x, T * kDim);
     rc = rc ? rc : alloc_n(h, &h->d_y, T * kDim);
     rc = rc ? rc : alloc_n(h, &h->d_layers, c.layers);
+    rc = rc ? rc : alloc_n(h, &h->d_tma, size_t(c.layers) * kTmaCount);
     rc = rc ? rc : alloc_n(h, &h->d_acc, 2 * (kMaxExperts + 1));
     rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
-    rc = rc ? rc : alloc_n(h, &h->d_part_gu, size_t(4 * 45) * 16 * 128);
+    rc = rc ? rc : alloc_n(h, &h->d_part_gu, size_t(4 * 23) * 16 * 256);
     rc = rc ? rc : alloc_n(h, &h->d_part_dn, size_t(23) * 16 * 128);
     rc = rc ? rc : alloc_n(h, &h->d_cnt, 4 * 45 + 23);
-    rc = rc ? rc : alloc_n(h, &h->d_bdown, size_t(4) * 180 * 8 * 16);
-    rc = rc ? rc : alloc_n(h, &h->d_sfb_down, size_t(4) * 90 * 4);
+    rc = rc ? rc : alloc_n(h, &h->d_bdown, size_t(4) * 90 * 256);
+    rc = rc ? rc : alloc_n(h, &h->d_sfb_down, size_t(4) * 96);
     if (rc) {
         return bail(rc);
     }
@@ -556,7 +623,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(h->d_bdown, 0, size_t(4) * 180 * 8 * 16) != cudaSuccess ||
+        cudaMemset(h->d_bdown, 0, size_t(4) * 90 * 256) != cudaSuccess ||
+        cudaMemset(h->d_sfb_down, 0x7f, size_t(4) * 96) != cudaSuccess ||
         cudaMemset(h->d_layers, 0, c.layers * sizeof(StackLayer)) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
     }

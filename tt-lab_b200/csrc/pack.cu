@@ -54,14 +54,7 @@ __global__ void pack_kernel(const uint8_t *__restrict__ gguf, uint8_t *__restric
         }
         uint8_t *base = packed + m * kPackedMatrixBytes;
         *reinterpret_cast<uint4 *>(base + r * kNibbleRowBytes + size_t(b) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-        uint8_t *scales = base + kNibbleBytes + r * kScaleRowBytes;
-        scales[b] = src[0];
-        if (b == kBlocks - 1) {
-#pragma unroll
-            for (int p = kBlocks; p < kScaleRowBytes; ++p) {
-                scales[p] = 0;
-            }
-        }
+        base[scale_offset(int(r), b)] = src[0];
     }
 }
 
@@ -82,7 +75,7 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ packed, uint8_t *__res
             e[2 * j + 1] = uint8_t(byte >> 4);
         }
         uint8_t *dst = gguf + i * 17;
-        dst[0] = base[kNibbleBytes + r * kScaleRowBytes + b];
+        dst[0] = base[scale_offset(int(r), b)];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
             dst[1 + j] = uint8_t(e[j] | (e[j + 16] << 4));
@@ -184,6 +177,8 @@ extern "C" int ttl_pack_mxfp4(const void *gguf, size_t matrices, void *packed, i
     const size_t gguf_bytes = size_t(kDim) * kGgufRowBytes;
     return run_repack(gguf, gguf_bytes, packed, kPackedMatrixBytes, matrices, device,
                       [](const uint8_t *s, uint8_t *d, size_t blocks) {
+                          cudaMemset2DAsync(d + kNibbleBytes, kPackedMatrixBytes, 0, kScaleBytes,
+                                            blocks / (size_t(kDim) * kBlocks), 0);
                           pack_kernel<<<grid_for(blocks), 256>>>(s, d, blocks);
                       });
 }
@@ -201,6 +196,8 @@ namespace ttl {
 void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream) {
     const size_t blocks = matrices * size_t(kDim) * kBlocks;
     if (blocks) {
+        // scale padding (K-blocks 90, 91; rows 2880..2943; the region's tail) is zero
+        cudaMemset2DAsync(packed_dev + kNibbleBytes, kPackedMatrixBytes, 0, kScaleBytes, matrices, stream);
         pack_kernel<<<grid_for(blocks), 256, 0, stream>>>(gguf_dev, packed_dev, blocks);
     }
 }

@@ -244,8 +244,8 @@ __global__ void __launch_bounds__(kProductThreads, 1)
                 if (kb < kBlocks) {
                     const uint4 gq = *reinterpret_cast<const uint4 *>(gm + size_t(row) * kNibbleRowBytes + kb * 16);
                     const uint4 uq = *reinterpret_cast<const uint4 *>(um + size_t(row) * kNibbleRowBytes + kb * 16);
-                    const float gs = e8m0_ref_scale(gm[kNibbleBytes + size_t(row) * kScaleRowBytes + kb]);
-                    const float us = e8m0_ref_scale(um[kNibbleBytes + size_t(row) * kScaleRowBytes + kb]);
+                    const float gs = e8m0_ref_scale(gm[scale_offset(row, kb)]);
+                    const float us = e8m0_ref_scale(um[scale_offset(row, kb)]);
                     float v[32];
                     decode_block(gq, v);
 #pragma unroll
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kProductThreads, 1) prefill_down_kernel(LayerD
                 const int kb = lane + 32 * j;
                 if (kb < kBlocks) {
                     const uint4 q = *reinterpret_cast<const uint4 *>(dm + size_t(row) * kNibbleRowBytes + kb * 16);
-                    const float sc = e8m0_ref_scale(dm[kNibbleBytes + size_t(row) * kScaleRowBytes + kb]);
+                    const float sc = e8m0_ref_scale(dm[scale_offset(row, kb)]);
                     float v[32];
                     decode_block(q, v);
 #pragma unroll

@@ -113,9 +113,10 @@ __global__ void __launch_bounds__(128, 1)
                 const int r = r0 + lane + 32 * m1;
                 v[m1] = 0;
                 if (r < kDim) {
-                    const uint8_t *sp = packed + kNibbleBytes + size_t(r) * kScaleRowBytes + kb0;
-                    v[m1] = uint32_t(sp[0]) | (uint32_t(sp[1]) << 8) | (uint32_t(sp[2]) << 16) |
-                            (uint32_t(sp[3]) << 24);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        v[m1] |= uint32_t(packed[scale_offset(r, kb0 + k)]) << (8 * k);
+                    }
                 }
             }
             tc::tmem_st4(tbase + lane_base + kColSfa, v[0], v[1], v[2], v[3]);
