@@ -284,12 +284,21 @@ def main():
     e2e_value = tokens * args.steps / e2e_s
     hbm_peak, peak_kind = peaks()
     if kms["persistent"]:
-        kernel = "decode_stack_kernel"
+        simt = os.environ.get("TTL_MOE_SIMT_DECODE") == "1"
+        kernel = "decode_stack_kernel" if simt else "decode_tc_kernel"
         bytes_launch = LAYER_BYTES_20B * kms["steps"]
     else:  # expert-parallel handles: the gate/up kernel of one layer
         kernel = "decode_gateup_kernel"
         bytes_launch = GATEUP_BYTES
     kernel_gbs = bytes_launch / (kms["ms"] * 1e-3) / 1e9
+    # DRAM traffic of the persistent kernel per token-layer, from the committed
+    # ncu capture of a smaller stack (traffic grows with the token-layers).
+    traffic = None
+    prof = ROOT / "profiles" / "decode_tc_small_6x8.md"
+    if kms["persistent"] and kernel == "decode_tc_kernel" and prof.exists():
+        for ln in prof.read_text().splitlines():
+            if ln.startswith("traffic_bytes_per_token_layer:"):
+                traffic = int(ln.split(":")[1]) * kms["steps"]
     # numerical spot check of this run against the oracle (first token, layer 0)
     ok_note = None
 
@@ -333,7 +342,8 @@ def main():
                 "unit": "GB/s",
                 "frac": kernel_gbs / hbm_peak,
                 "peak_kind": peak_kind,
-                "traffic": None,
+                "traffic": traffic,
+                "traffic_source": "profiles/decode_tc_small_6x8.md (ncu dram bytes per token-layer x token-layers)",
                 "bytes_per_launch": bytes_launch,
                 "bytes_per_token_layer": LAYER_BYTES_20B,
                 "launch_ms": kms["ms"],
