@@ -197,7 +197,7 @@ def main():
     import numpy as np
     import torch
     import ttl_moe
-    from ttl_moe import synth
+    from ttl_moe import parallel, synth
 
     torch.cuda.set_device(local)
     dist = None
@@ -211,11 +211,8 @@ def main():
     # NCCL id for the library's own communicator, broadcast over torch.distributed.
     nid = None
     if world > 1:
-        idt = torch.zeros(ttl_moe.NCCL_ID_BYTES, dtype=torch.uint8, device="cuda")
-        if rank == 0:
-            idt.copy_(torch.frombuffer(bytearray(ttl_moe.nccl_id()), dtype=torch.uint8))
-        dist.broadcast(idt, 0)
-        nid = bytes(idt.cpu().numpy().tobytes())
+        nid = parallel.share_bytes(dist, ttl_moe.nccl_id() if rank == 0 else None, ttl_moe.NCCL_ID_BYTES,
+                                   device="cuda")
 
     moe = ttl_moe.MoE(experts=experts, layers=layers, max_tokens=0, device=local, rank=rank, world=world,
                       nccl_id_bytes=nid)
@@ -275,9 +272,7 @@ def main():
     clk = clocks.stop()
 
     if dist:
-        tt = torch.tensor([ms, e2e_s], dtype=torch.float64, device="cuda")
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms, e2e_s = float(tt[0]), float(tt[1])
+        ms, e2e_s = parallel.max_over_ranks(dist, [ms, e2e_s], device="cuda")
 
     ms_step = ms / args.steps
     value = tokens / (ms_step / 1e3)
