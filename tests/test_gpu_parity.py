@@ -168,3 +168,18 @@ def test_errors_match_reference_behaviour(ttl, layer32):
             m.moe(2, np.zeros(D, np.float32))
         out, idx, w = m.moe(0, np.zeros(D, np.float32))  # handle still usable
         assert np.isfinite(out).all()
+
+
+def test_scale_byte_255_is_rejected_at_upload(ttl, layer32):
+    """tt-lab reads E8M0 byte 255 as 2^128 (src/tensor.cpp:36-44); the tensor
+    cores' E8M0 255 is NaN, so the upload refuses such weights loudly."""
+    t = dict(layer32)
+    bad = layer32["down_w"].copy()
+    bad[17 * 1000] = 255  # the scale byte of one block
+    t["down_w"] = bad
+    with ttl.MoE(experts=32, layers=1, device=0) as m:
+        with pytest.raises(RuntimeError, match="scale byte is 255"):
+            m.upload_layer(0, t)
+        m.upload_layer(0, layer32)  # the handle stays usable
+        out, idx, w = m.moe(0, np.zeros(D, np.float32))
+        assert np.isfinite(out).all()

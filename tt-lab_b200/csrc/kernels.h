@@ -54,8 +54,10 @@ void launch_decode_down(const LayerDev &L, const DecodeWork &w, const DecodeShap
 // out[i] = residual[i] + moe[i]
 void launch_add(const float *residual, const float *moe, float *out, int n, cudaStream_t stream);
 
-// GGUF -> packed layout on the device.
-void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream);
+// GGUF -> packed layout on the device; bit 0 of *flags (optional) is set when
+// a scale byte is 255.
+void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream,
+                 uint32_t *flags = nullptr);
 
 // ---- persistent decode (decode_stack.cu) ----
 // A CUtensorMap, kept opaque here (128 bytes, 64-byte aligned).

@@ -97,6 +97,7 @@ struct ttl_moe {
     uint8_t *d_sfb_down = nullptr;
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
+    uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
     std::vector<StackLayer> host_layers;
     double *d_acc = nullptr;          // [2][kMaxExperts + 1]
     unsigned *d_barrier = nullptr;    // [2]
@@ -584,6 +585,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_y, T * kDim);
     rc = rc ? rc : alloc_n(h, &h->d_layers, c.layers);
     rc = rc ? rc : alloc_n(h, &h->d_tma, size_t(c.layers) * kTmaCount);
+    rc = rc ? rc : alloc_n(h, &h->d_pack_flags, 1);
     rc = rc ? rc : alloc_n(h, &h->d_acc, 2 * (kMaxExperts + 1));
     rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
     rc = rc ? rc : alloc_n(h, &h->d_part_gu, size_t(4 * 23) * 16 * 256);
@@ -732,9 +734,18 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
             TTL_TRY_CUDA(h, cudaMemcpy(h->staging, src, El * expert_gguf, cudaMemcpyHostToDevice));
             src = h->staging;
         }
-        launch_pack(src, dsts[m], El, h->stream);
+        TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_pack_flags, 0, sizeof(uint32_t), h->stream));
+        launch_pack(src, dsts[m], El, h->stream, h->d_pack_flags);
         TTL_TRY_CUDA(h, cudaGetLastError());
+        uint32_t flags = 0;
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(&flags, h->d_pack_flags, sizeof(flags), cudaMemcpyDeviceToHost, h->stream));
         TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+        if (flags & 1u) {
+            return fail(h, TTL_ERR_UNSUPPORTED,
+                        "layer " + std::to_string(layer) +
+                            ": an MXFP4 scale byte is 255 (2^128 in tt-lab's convention), which the tensor cores' "
+                            "E8M0 scales cannot represent");
+        }
     }
     s.uploaded = true;
     return push_layer_descriptor(h, layer);

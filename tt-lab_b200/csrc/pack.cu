@@ -23,7 +23,10 @@ namespace ttl {
 namespace {
 
 // One thread per (matrix, row, block).
-__global__ void pack_kernel(const uint8_t *__restrict__ gguf, uint8_t *__restrict__ packed, size_t blocks) {
+// flags (optional): bit 0 is set when a scale byte is 255 -- tt-lab reads it as
+// 2^128 (src/tensor.cpp:36-44), which has no E8M0 encoding for the tensor cores.
+__global__ void pack_kernel(const uint8_t *__restrict__ gguf, uint8_t *__restrict__ packed, size_t blocks,
+                            uint32_t *flags = nullptr) {
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < blocks; i += size_t(gridDim.x) * blockDim.x) {
         const size_t row_all = i / kBlocks;
         const int b = int(i % kBlocks);
@@ -55,6 +58,9 @@ __global__ void pack_kernel(const uint8_t *__restrict__ gguf, uint8_t *__restric
         uint8_t *base = packed + m * kPackedMatrixBytes;
         *reinterpret_cast<uint4 *>(base + r * kNibbleRowBytes + size_t(b) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         base[scale_offset(int(r), b)] = src[0];
+        if (flags && src[0] == 255u) {
+            atomicOr(flags, 1u);
+        }
     }
 }
 
@@ -193,12 +199,13 @@ extern "C" int ttl_unpack_mxfp4(const void *packed, size_t matrices, void *gguf,
 
 // Device-side packing used by ttl_moe_upload_layer (stream-ordered, no sync).
 namespace ttl {
-void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream) {
+void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream,
+                 uint32_t *flags) {
     const size_t blocks = matrices * size_t(kDim) * kBlocks;
     if (blocks) {
         // scale padding (K-blocks 90, 91; rows 2880..2943; the region's tail) is zero
         cudaMemset2DAsync(packed_dev + kNibbleBytes, kPackedMatrixBytes, 0, kScaleBytes, matrices, stream);
-        pack_kernel<<<grid_for(blocks), 256, 0, stream>>>(gguf_dev, packed_dev, blocks);
+        pack_kernel<<<grid_for(blocks), 256, 0, stream>>>(gguf_dev, packed_dev, blocks, flags);
     }
 }
 } // namespace ttl
