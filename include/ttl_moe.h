@@ -165,6 +165,20 @@ int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
  * pointers on `device`; synchronous. */
 int ttl_matvec_mxfp4(const void *packed, const float *bias, const float *x, float *y, int device);
 
+/* ttl_matvec_mxfp4 for `matrices` consecutive problems (matrix m at
+ * packed + m * ttl_packed_bytes(1), its bias, x and y at + m * 2880 floats)
+ * that allocates no device memory: its per-matrix status words live in a
+ * fixed 1 KB static device array, so matrices must be 1..256 (more is refused
+ * with TTL_ERR_ARGUMENT before any GPU work).  For callers that cannot
+ * allocate (a fixed memory budget, a pool-owning host).  The first call on a
+ * device looks the array up (cudaGetSymbolAddress) with that device current;
+ * make it before any stream capture.  The array is shared by all calls on a
+ * device, so overlapping calls from several threads or streams race.
+ * Synchronous, on the device's legacy default stream.  No counterpart in
+ * tt-lab. */
+int ttl_matvec_mxfp4_noalloc(const void *packed, const float *bias, const float *x, float *y, size_t matrices,
+                             int device);
+
 /* ---- GPU weight-layout packer (requant) -------------------------------- */
 
 /* Bytes of the packed layout (TTQ format TTL_TTQ_FORMAT_MXFP4_GPU) of

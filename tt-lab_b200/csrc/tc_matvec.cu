@@ -9,6 +9,9 @@
 // and 90 MMAs of K = 32 accumulate the tile in tensor memory.
 #include <cuda_runtime.h>
 
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "internal.h"
 #include "tc.cuh"
@@ -213,6 +216,81 @@ extern "C" int ttl_matvec_mxfp4(const void *packed, const float *bias, const flo
     }
     if (st) {
         return fail(nullptr, TTL_ERR_DEVICE, "tc matvec: bounded wait gave up");
+    }
+    return TTL_OK;
+}
+
+// ---- allocation-free variant ----
+// Status words of ttl_matvec_mxfp4_noalloc live in this file-scope array
+// instead of a per-call cudaMalloc: one word per matrix of a call.
+namespace {
+constexpr size_t kNoAllocMaxMatrices = 256;  // 1 KB of scratch per device
+static __device__ __align__(256) uint32_t g_noalloc_status[kNoAllocMaxMatrices];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_addr[64] = {};  // per device ordinal, looked up once
+} // namespace
+
+extern "C" int ttl_matvec_mxfp4_noalloc(const void *packed, const float *bias, const float *x, float *y,
+                                        size_t matrices, int device) {
+    if (!packed || !bias || !x || !y) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null pointer");
+    }
+    if (matrices == 0 || matrices > kNoAllocMaxMatrices) {
+        return fail(nullptr, TTL_ERR_ARGUMENT,
+                    "ttl_matvec_mxfp4_noalloc takes 1.." + std::to_string(kNoAllocMaxMatrices) +
+                        " matrices per call (its scratch is a fixed static array); got " + std::to_string(matrices));
+    }
+    if (device >= 0 && cudaSetDevice(device) != cudaSuccess) {
+        return fail(nullptr, TTL_ERR_CUDA, "cannot select device");
+    }
+    int dev = 0;
+    TTL_TRY_CUDA(nullptr, cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) {
+        return fail(nullptr, TTL_ERR_UNSUPPORTED, "device ordinal above 63");
+    }
+    if (!is_device_pointer(packed) || !is_device_pointer(bias) || !is_device_pointer(x) || !is_device_pointer(y)) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "ttl_matvec_mxfp4_noalloc takes device pointers");
+    }
+    uint32_t *status = nullptr;
+    {
+        // first call on this device: look the scratch up (and set the kernel's
+        // shared-memory limit) with the device current
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if (!g_noalloc_addr[dev]) {
+            void *addr = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_status);
+            if (e != cudaSuccess || !addr) {
+                return fail(nullptr, TTL_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+            }
+            TTL_TRY_CUDA(nullptr, cudaFuncSetAttribute(tc_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       int(sizeof(MatvecSmem))));
+            g_noalloc_addr[dev] = addr;
+        }
+        status = static_cast<uint32_t *>(g_noalloc_addr[dev]);
+    }
+    // the status words start at zero
+    TTL_TRY_CUDA(nullptr, cudaMemsetAsync(status, 0, matrices * sizeof(uint32_t), 0));
+    for (size_t m = 0; m < matrices; ++m) {
+        tc_matvec_kernel<<<(kDim + 127) / 128, 128, int(sizeof(MatvecSmem))>>>(
+            static_cast<const uint8_t *>(packed) + m * kPackedMatrixBytes, bias + m * kDim, x + m * kDim, y + m * kDim,
+            status + m);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) {
+        e = cudaStreamSynchronize(0);
+    }
+    uint32_t st[kNoAllocMaxMatrices];
+    if (e == cudaSuccess) {
+        e = cudaMemcpy(st, status, matrices * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    }
+    if (e != cudaSuccess) {
+        return fail(nullptr, TTL_ERR_CUDA, std::string("tc matvec: ") + cudaGetErrorString(e));
+    }
+    for (size_t m = 0; m < matrices; ++m) {
+        if (st[m]) {
+            return fail(nullptr, TTL_ERR_DEVICE, "tc matvec: bounded wait gave up on matrix " + std::to_string(m));
+        }
     }
     return TTL_OK;
 }

@@ -88,6 +88,7 @@ def lib():
         "ttl_moe_trace": (i32, [vp, i32, ctypes.POINTER(u64)]),
         "ttl_moe_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float), sz]),
         "ttl_matvec_mxfp4": (i32, [vp, vp, vp, vp, i32]),
+        "ttl_matvec_mxfp4_noalloc": (i32, [vp, vp, vp, vp, sz, i32]),
         "ttl_packed_bytes": (sz, [sz]),
         "ttl_pack_mxfp4": (i32, [vp, sz, vp, i32]),
         "ttl_unpack_mxfp4": (i32, [vp, sz, vp, i32]),
@@ -266,6 +267,13 @@ def pack_mxfp4(gguf, matrices, packed=None, device=0):
 def matvec_mxfp4(packed, bias, x, y, device=0):
     """y = bias + W x on the tensor cores (device tensors)."""
     check(lib().ttl_matvec_mxfp4(_ptr(packed), _ptr(bias), _ptr(x), _ptr(y), device))
+    return y
+
+
+def matvec_mxfp4_noalloc(packed, bias, x, y, matrices=1, device=0):
+    """matvec_mxfp4 over `matrices` consecutive problems without allocating
+    device memory (at most 256 per call)."""
+    check(lib().ttl_matvec_mxfp4_noalloc(_ptr(packed), _ptr(bias), _ptr(x), _ptr(y), matrices, device))
     return y
 
 
