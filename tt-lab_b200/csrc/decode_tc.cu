@@ -53,6 +53,8 @@
 // drains its own copies and MMAs, frees its tensor memory and returns.
 #include <cuda_runtime.h>
 
+#include <cstddef>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc.cuh"
@@ -78,10 +80,12 @@ constexpr uint32_t kBoxTx = 128 * 128;        // bytes of one weight box (8 K-bl
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColD = 0;                                  // 2 buffers x (gate 16 + up 16) columns
 constexpr uint32_t kColSfa = 64;                               // kStages x 4 chunks x 4 columns
-constexpr uint32_t kColSfbG = kColSfa + 16 * kStages;          // 23 scale chunks x 4 columns
-constexpr uint32_t kColSfbD = kColSfbG + 4 * kSfChunks;        // kDownSlots x 23 x 4 columns
+constexpr uint32_t kSfbCols = 4 * 24;                          // B scales: 4 columns per chunk (the MMA's scale
+                                                               // address is 4-column aligned), 23 chunks + 1
+constexpr uint32_t kColSfbG = kColSfa + 16 * kStages;          // gate/up B scales
+constexpr uint32_t kColSfbD = kColSfbG + kSfbCols;             // kDownSlots x kSfbCols
 constexpr int kDownSlots = 2;                 // down-projection experts a CTA touches (checked)
-static_assert(kColSfbD + 4 * kDownSlots * kSfChunks <= kTmemCols, "tensor memory map");
+static_assert(kColSfbD + kSfbCols * kDownSlots <= kTmemCols, "tensor memory map");
 constexpr int kPreE = 32;                     // next-layer router weights the down epilogue loads early
 constexpr int kOwnMax = 3;                    // tiles a CTA reduces in one phase (checked)
 constexpr unsigned long long kGridWaitNs = 2000000000ull;
@@ -106,6 +110,7 @@ struct alignas(1024) Smem {
     uint64_t acc_empty[2];
     uint64_t sel_full;            // the step's selection is published
     uint64_t setup;               // the down B operands of the step landed
+    uint64_t bsetup;              // the gate/up B operand of the step landed (from the previous step)
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier verdict, written by thread 0 only
@@ -118,9 +123,16 @@ struct alignas(1024) Smem {
     int amb;
     int abort;
     int last;
+    float nscale;  // scalar the gate/up partials are multiplied by (the RMSNorm scale; 1 in mode 0)
 };
 
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory per CTA");
+// TMA boxes with 128-byte swizzle land on 1024-byte boundaries; bulk copies
+// and tcgen05 operand / copy sources need 16-byte alignment.
+static_assert(offsetof(Smem, a) % 1024 == 0 && sizeof(Smem::a[0][0]) % 1024 == 0, "A stage alignment");
+static_assert(offsetof(Smem, sfa) % 16 == 0 && offsetof(Smem, bgu) % 16 == 0 && offsetof(Smem, bdown) % 16 == 0 &&
+                  offsetof(Smem, gcode) % 16 == 0 && offsetof(Smem, dcode) % 16 == 0,
+              "bulk-copy destinations");
 
 // Role-local pipeline counters (each role walks the same stage sequence).
 struct Pipe {
@@ -402,7 +414,7 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
             }
             const int ds = s.dslot[r.q];
             const uint32_t bbase = tc::smem_u32(&s.bdown[ds][0][0]);
-            const uint32_t sfb0 = tbase + kColSfbD + 4 * uint32_t(ds * kSfChunks);
+            const uint32_t sfb0 = tbase + kColSfbD + kSfbCols * uint32_t(ds);
             for (int kb = r.kb0; kb < r.kb0 + r.nkb; kb += 2) {
                 const uint32_t sel = uint32_t(kb & 3);
                 const uint32_t aoff = 16384u * uint32_t((kb >> 3) & 1) + 32u * uint32_t((kb >> 1) & 3);
@@ -603,7 +615,9 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         if (row - lane < kDim) {
             float h = 0.0f;
             if (row < kDim) {
-                h = __fmul_rn(swiglu_ref(__fadd_rn(o.bias_g, pg), __fadd_rn(o.bias_u, pu)), s.wts[s.slot_of[q]]);
+                const float gv = __fadd_rn(o.bias_g, __fmul_rn(pg, s.nscale));
+                const float uv = __fadd_rn(o.bias_u, __fmul_rn(pu, s.nscale));
+                h = __fmul_rn(swiglu_ref(gv, uv), s.wts[s.slot_of[q]]);
             }
             const int kb = row >> 5;
             const uint32_t code = tc::digit_split_store(h, a.bdown + (size_t(q) * kBlocks + kb) * kBRowBytes, lane);
@@ -625,7 +639,17 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         // products transposed-summed over the 32 rows
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const float xr = more_layers ? yv : o.xnext;
-        const double xgd = double(__fmul_rn(xr, o.nw));  // 0 past the last row
+        const float xg = __fmul_rn(xr, o.nw);  // 0 past the last row
+        const double xgd = double(xg);
+        // the next step's gate/up B operand: digit terms of x * g (the RMSNorm
+        // scale is a scalar applied to the products)
+        if (row - lane < kDim) {
+            const int kb = row >> 5;
+            const uint32_t code = tc::digit_split_store(xg, a.bnext + size_t(kb) * kBRowBytes, lane);
+            if (lane == 0) {
+                a.bnext_code[kb] = uint8_t(code);
+            }
+        }
         for (int b = 0; 16 * b < E; ++b) {
             double v[16];
             if (b < kPreE / 16) {
@@ -850,6 +874,24 @@ __device__ void warp_top4(Smem &s, int experts, bool check_bounds) {
     }
 }
 
+// B-operand scales of one operand's 24 chunks into tensor memory: chunk c at
+// columns 4c..4c+3, of which the MMA reads column 4c (lane n = row n of B,
+// byte k = K-block 4c + k); four chunks per store.  Warp-collective, this
+// warp's lane quadrant.
+__device__ __forceinline__ void store_sfb(const uint8_t *codes, uint32_t taddr, int lane) {
+#pragma unroll
+    for (int g4 = 0; g4 < int(kSfbCols / 16); ++g4) {
+        uint32_t v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            v[k] = (k & 3) ? 0u
+                           : tc::digit_scales4(*reinterpret_cast<const uint32_t *>(codes + 16 * g4 + (k & ~3)), lane);
+        }
+        tc::tmem_st16(taddr + 16 * uint32_t(g4), v);
+    }
+    tc::wait_st();
+}
+
 // Softmax of the selected logits (src/model.cpp:310-321) and this rank's
 // experts; thread 0, then published to the load warp.
 __device__ void publish_selection(Smem &s, const StackArgs &a, bool export_top) {
@@ -931,6 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         }
         tc::mbar_init(&s.sel_full, 1);
         tc::mbar_init(&s.setup, 1);
+        tc::mbar_init(&s.bsetup, 1);
         tc::mbar_init(&s.fin, 1);
         tc::fence_mbar_init();
     }
@@ -957,6 +1000,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         // ---------------- compute group: warps 0-8 ----------------
         const int ct = threadIdx.x;  // 0..287
         Pipe pipe;
+        uint32_t bsetup_uses = 0;
         // Router sums of (token 0, first layer) in stack mode.
         if (a.mode == 1) {
             const StackLayer &L = a.layers[a.layer_begin];
@@ -986,16 +1030,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 const bool export_top = (blockIdx.x == 0 && t == a.tokens - 1 && li == nl - 1);
 
                 stamp(a, step, 0);
-                // x (and norm weight) loads of the B split, issued first:
-                // warp w takes K-blocks w + 9 i
+                // The gate/up B operand: digit terms of x * g (mode 1) or of h
+                // (mode 0).  From the second step of a stack on, the previous
+                // step's down epilogues have written it (a.bnext): one bulk
+                // copy.  Otherwise it is split here; its loads go out first
+                // (warp w takes K-blocks w + 9 i).
+                const bool split_here = (a.mode == 0) || (step == 0);
                 constexpr int kPasses = kBlocks / kComputeWarps;  // 10
                 static_assert(kPasses * kComputeWarps == kBlocks, "split passes");
                 float xr[kPasses], gr[kPasses];
+                if (split_here) {
 #pragma unroll
-                for (int pi = 0; pi < kPasses; ++pi) {
-                    const int k = (warp + pi * kComputeWarps) * 32 + lane;
-                    xr[pi] = __ldcg(xcur + k);
-                    gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
+                    for (int pi = 0; pi < kPasses; ++pi) {
+                        const int k = (warp + pi * kComputeWarps) * 32 + lane;
+                        xr[pi] = __ldcg(xcur + k);
+                        gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
+                    }
+                } else if (threadIdx.x == 0) {
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    tc::mbar_expect_tx(&s.bsetup, uint32_t(kBlocks * kBRowBytes + kCodeBytes));
+                    bulk_load(&s.bgu[0][0], a.bnext, kBlocks * kBRowBytes, &s.bsetup);
+                    bulk_load(&s.gcode[0], a.bnext_code, kCodeBytes, &s.bsetup);
                 }
                 float scale = 1.0f;
                 // ---------------- A: selection ----------------
@@ -1127,24 +1183,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     }
                 }
                 stamp(a, step, 1);
-                // B for gate/up: h split into terms; SFB into tensor memory
-#pragma unroll
-                for (int pi = 0; pi < kPasses; ++pi) {
-                    const int kb = warp + pi * kComputeWarps;
-                    const float h = (a.mode == 1) ? __fmul_rn(__fmul_rn(xr[pi], scale), gr[pi]) : xr[pi];
-                    const uint32_t code = tc::digit_split_store(h, &s.bgu[kb][0], lane);
-                    if (lane == 0) {
-                        s.gcode[kb] = uint8_t(code);
-                    }
+                if (threadIdx.x == 0) {
+                    s.nscale = scale;
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if (split_here) {
+#pragma unroll
+                    for (int pi = 0; pi < kPasses; ++pi) {
+                        const int kb = warp + pi * kComputeWarps;
+                        const float h = (a.mode == 1) ? __fmul_rn(xr[pi], gr[pi]) : xr[pi];
+                        const uint32_t code = tc::digit_split_store(h, &s.bgu[kb][0], lane);
+                        if (lane == 0) {
+                            s.gcode[kb] = uint8_t(code);
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                } else {
+                    if (!wait_bar(s, &s.bsetup, bsetup_uses & 1u, a.status)) {
+                        *reinterpret_cast<volatile int *>(&s.abort) = 1;
+                    }
+                    ++bsetup_uses;
+                }
                 compute_sync();
                 if (warp < kEpiWarps) {
-                    for (int g = 0; g < kSfChunks; ++g) {
-                        const uint32_t v = tc::digit_scales4(*reinterpret_cast<const uint32_t *>(&s.gcode[4 * g]), lane);
-                        tc::tmem_st4(tbase + (uint32_t(32 * warp) << 16) + kColSfbG + 4 * g, v, 0u, 0u, 0u);
-                    }
-                    tc::wait_st();
+                    store_sfb(s.gcode, tbase + (uint32_t(32 * warp) << 16) + kColSfbG, lane);
                 }
                 tc::fence_before_sync();
                 compute_sync();
@@ -1211,14 +1272,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 compute_sync();
                 if (warp < kEpiWarps) {
                     for (int d = 0; d < kDownSlots; ++d) {
-                        for (int g = 0; g < kSfChunks; ++g) {
-                            const uint32_t v =
-                                tc::digit_scales4(*reinterpret_cast<const uint32_t *>(&s.dcode[d][4 * g]), lane);
-                            tc::tmem_st4(tbase + (uint32_t(32 * warp) << 16) + kColSfbD + 4 * (d * kSfChunks + g), v,
-                                         0u, 0u, 0u);
-                        }
+                        store_sfb(s.dcode[d], tbase + (uint32_t(32 * warp) << 16) + kColSfbD + kSfbCols * d, lane);
                     }
-                    tc::wait_st();
                 }
                 tc::fence_before_sync();
                 compute_sync();

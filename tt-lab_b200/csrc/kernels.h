@@ -115,6 +115,8 @@ struct StackArgs {
     unsigned *cnt_dn;          // [23]
     uint8_t *bdown;            // [4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
     uint8_t *sfb_down;         // [4][96] their block codes (90 + padding, 127)
+    uint8_t *bnext;            // [90 K-blocks][2][8][16] next step's gate/up B operand: digit terms of x * g
+    uint8_t *bnext_code;       // [96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
 };

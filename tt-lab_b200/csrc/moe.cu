@@ -95,6 +95,8 @@ struct ttl_moe {
     unsigned *d_cnt = nullptr;        // [4 * 45 + 23]
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
+    uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
+    uint8_t *d_bnext_code = nullptr;
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
@@ -351,6 +353,8 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.cnt_dn = h->d_cnt + 4 * 45;
     a.bdown = h->d_bdown;
     a.sfb_down = h->d_sfb_down;
+    a.bnext = h->d_bnext;
+    a.bnext_code = h->d_bnext_code;
     a.trace = h->d_trace;
     a.trace_steps = h->trace_steps;
     if (h->d_trace) {
@@ -593,6 +597,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_cnt, 4 * 45 + 23);
     rc = rc ? rc : alloc_n(h, &h->d_bdown, size_t(4) * 90 * 256);
     rc = rc ? rc : alloc_n(h, &h->d_sfb_down, size_t(4) * 96);
+    rc = rc ? rc : alloc_n(h, &h->d_bnext, size_t(90) * 256);
+    rc = rc ? rc : alloc_n(h, &h->d_bnext_code, size_t(96));
     if (rc) {
         return bail(rc);
     }
@@ -627,6 +633,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(h->d_bdown, 0, size_t(4) * 90 * 256) != cudaSuccess ||
         cudaMemset(h->d_sfb_down, 0x7f, size_t(4) * 96) != cudaSuccess ||
+        cudaMemset(h->d_bnext, 0, size_t(90) * 256) != cudaSuccess ||
+        cudaMemset(h->d_bnext_code, 0x7f, size_t(96)) != cudaSuccess ||
         cudaMemset(h->d_layers, 0, c.layers * sizeof(StackLayer)) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
     }
