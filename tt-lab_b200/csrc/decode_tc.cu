@@ -8,8 +8,11 @@
 // Roles (10 warps):
 //   warps 0-8  the compute group: selection, B-operand preparation and the
 //              grid barriers; warps 0-3 also run the epilogues (one thread
-//              per tile row, TMEM lane quadrant = warp) and lane 0 of warp 8
-//              issues the block-scaled MMAs
+//              per tile row, TMEM lane quadrant = warp); lane 0 of each of
+//              warps 4-7 issues the block-scaled MMAs of one scale chunk of
+//              every stage into its own accumulator (one issuing thread
+//              sustains about one MMA per 150 cycles, four about one per 40);
+//              lane 0 of warp 8 issues the operand bulk copies
 //   warp 9     lane 0 issues the loads into the stage ring: per stage 32 KB
 //              of packed E2M1 weights as two 128-byte x 128-row TMA boxes
 //              (128-byte swizzle: the K-major layout of the MMA's A operand)
@@ -70,7 +73,9 @@ constexpr int kSfChunks = kScaleChunks;       // 23 scale chunks of 4 K-blocks
 constexpr int kTiles = kScaleTiles;           // 23 tiles of 128 rows
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 4;                  // warps 0-3
-constexpr int kMmaWarp = 8;
+constexpr int kIssuers = 4;                   // MMA issuers: lane 0 of warps 4-7
+constexpr int kIssuerWarp0 = 4;
+constexpr int kMmaWarp = 8;                   // lane 0 issues the operand bulk copies
 constexpr int kTmaWarp = 9;
 constexpr int kThreads = 32 * (kTmaWarp + 1);
 constexpr int kComputeWarps = kTmaWarp;       // warps 0-8
@@ -78,8 +83,8 @@ constexpr int kComputeThreads = 32 * kComputeWarps;
 constexpr int kMaxSlots = 16;                 // contributors per tile (checked)
 constexpr uint32_t kBoxTx = 128 * 128;        // bytes of one weight box (8 K-blocks of 128 rows)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD = 0;                                  // 2 buffers x (gate 16 + up 16) columns
-constexpr uint32_t kColSfa = 64;                               // kStages x 4 chunks x 4 columns
+constexpr uint32_t kColD = 0;                                  // 2 buffers x kIssuers x 16 columns
+constexpr uint32_t kColSfa = 128;                              // kStages x 4 chunks x 4 columns
 constexpr uint32_t kSfbCols = 4 * 24;                          // B scales: 4 columns per chunk (the MMA's scale
                                                                // address is 4-column aligned), 23 chunks + 1
 constexpr uint32_t kColSfbG = kColSfa + 16 * kStages;          // gate/up B scales
@@ -359,8 +364,24 @@ __device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTop
     });
 }
 
-// ---- MMA issuer (warp 8, lane 0) ----
-__device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
+// Issuers that have K-blocks in a segment of phase p: issuer k owns, in each
+// stage, scale chunk k & 1 of the gate (k < 2) or up (k >= 2) box, or chunk k
+// of the four of a down stage.  units [u_lo, u_hi) of tile `tile`.
+__device__ __forceinline__ uint32_t segment_issuers(const Phase &p, int tile, int u_lo, int u_hi) {
+    uint32_t mask = 0;
+    for (int u = u_lo; u < u_hi; ++u) {
+        const int pr = (u - tile * p.kunits) % kPairs;
+        if (p.kind == 0) {
+            mask |= ((pr >> 1) & 1) ? 0xAu : 0x5u;
+        } else {
+            mask |= 1u << ((pr >> 1) & 3);
+        }
+    }
+    return mask;
+}
+
+// ---- MMA issuers (warps 4-7, lane 0; issuer k = warp - 4) ----
+__device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp, int k) {
     Smem &s = *c.s;
     const uint32_t a0 = tc::smem_u32(&s.a[0][0][0][0]);
     const uint32_t sf0 = tc::smem_u32(&s.sfa[0][0][0]);
@@ -382,46 +403,32 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp) {
             return false;
         }
         tc::fence_after_sync();
-        const uint32_t abase = a0 + st * uint32_t(sizeof(s.a[0]));
-        const uint32_t sfbase = sf0 + st * uint32_t(sizeof(s.sfa[0]));
-        const uint32_t sfa_col = tbase + kColSfa + 16 * st;
-        const uint32_t dcol = tbase + kColD + 32 * db;
-        const int c0 = r.kb0 >> 2;
-        const int c1 = (r.kb0 + r.nkb - 1) >> 2;
-        if (r.kind == 0) {
-            for (int ch = c0; ch <= c1; ++ch) {
-                const uint32_t lc = uint32_t(ch & 1);
-                tc::sf_copy(sfa_col + 4 * lc, sfbase + kScaleBlockBytes * lc);
-                tc::sf_copy(sfa_col + 4 * (2 + lc), sfbase + kScaleBlockBytes * (2 + lc));
+        // this issuer's scale chunk of the stage and its K-blocks in it
+        const int m = (r.kind == 0) ? (k >> 1) : 0;
+        const int chunk = (r.kind == 0) ? ((r.kb0 & ~7) >> 2) + (k & 1) : ((r.kb0 & ~15) >> 2) + k;
+        const int lo = max(r.kb0, 4 * chunk);
+        const int hi = min(r.kb0 + r.nkb, 4 * chunk + 4);
+        if (lo < hi) {
+            const uint32_t abase = a0 + st * uint32_t(sizeof(s.a[0]));
+            const uint32_t sfa = tbase + kColSfa + 16 * st + 4 * uint32_t(k);
+            tc::sf_copy(sfa, sf0 + st * uint32_t(sizeof(s.sfa[0])) + kScaleBlockBytes * uint32_t(k));
+            const uint32_t dcol = tbase + kColD + 64 * db + 16 * uint32_t(k);
+            uint32_t bbase, sfb0;
+            if (r.kind == 0) {
+                bbase = tc::smem_u32(&s.bgu[0][0]);
+                sfb0 = tbase + kColSfbG;
+            } else {
+                const int ds = s.dslot[r.q];
+                bbase = tc::smem_u32(&s.bdown[ds][0][0]);
+                sfb0 = tbase + kColSfbD + kSfbCols * uint32_t(ds);
             }
-            const uint32_t bbase = tc::smem_u32(&s.bgu[0][0]);
-            for (int kb = r.kb0; kb < r.kb0 + r.nkb; kb += 2) {
+            for (int kb = lo; kb < hi; kb += 2) {
                 const uint32_t sel = uint32_t(kb & 3);
-                const uint32_t aoff = 32u * uint32_t((kb >> 1) & 3);
-                const uint32_t lc = uint32_t((kb >> 2) & 1);
+                const uint32_t box = (r.kind == 0) ? uint32_t(m) : uint32_t((kb >> 3) & 1);
+                const uint32_t aoff = 16384u * box + 32u * uint32_t((kb >> 1) & 3);
                 const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * kBRowBytes, kBRowBytes, 128);
-                const uint32_t idesc = tc::instr_desc_f4(kN, sel);
-                const uint32_t sfb = (tbase + kColSfbG + 4 * uint32_t(kb >> 2)) | (sel << 30);
-                tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, idesc, (sfa_col + 4 * lc) | (sel << 30), sfb, !first);
-                tc::mma_f4(dcol + 16, tc::smem_desc_sw128(abase + 16384u + aoff), bd, idesc,
-                           (sfa_col + 4 * (2 + lc)) | (sel << 30), sfb, !first);
-                first = false;
-            }
-        } else {
-            for (int ch = c0; ch <= c1; ++ch) {
-                const uint32_t lc = uint32_t(ch & 3);
-                tc::sf_copy(sfa_col + 4 * lc, sfbase + kScaleBlockBytes * lc);
-            }
-            const int ds = s.dslot[r.q];
-            const uint32_t bbase = tc::smem_u32(&s.bdown[ds][0][0]);
-            const uint32_t sfb0 = tbase + kColSfbD + kSfbCols * uint32_t(ds);
-            for (int kb = r.kb0; kb < r.kb0 + r.nkb; kb += 2) {
-                const uint32_t sel = uint32_t(kb & 3);
-                const uint32_t aoff = 16384u * uint32_t((kb >> 3) & 1) + 32u * uint32_t((kb >> 1) & 3);
-                const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * kBRowBytes, kBRowBytes, 128);
-                tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, tc::instr_desc_f4(kN, sel),
-                           (sfa_col + 4 * uint32_t((kb >> 2) & 3)) | (sel << 30), (sfb0 + 4 * uint32_t(kb >> 2)) | (sel << 30),
-                           !first);
+                tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, tc::instr_desc_f4(kN, sel), sfa | (sel << 30),
+                           (sfb0 + 4 * uint32_t(kb >> 2)) | (sel << 30), !first);
                 first = false;
             }
         }
@@ -708,7 +715,9 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
     int nown = 0;
     for (int u = u0; u < u1;) {
         const int tile = u / p.kunits;
+        const int seg_lo = u;
         u = min(u1, (tile + 1) * p.kunits);
+        const uint32_t mask = segment_issuers(p, tile, seg_lo, u);
         const uint32_t db = pp.seg & 1;
         const uint32_t duse = pp.seg >> 1;
         ++pp.seg;
@@ -722,26 +731,29 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             return;
         }
         tc::fence_after_sync();
-        float dg[16], du[16];
-        tc::tmem_ld16(c.tbase + (uint32_t(32 * w) << 16) + kColD + 32 * db, dg);
-        if (p.kind == 0) {
-            tc::tmem_ld16(c.tbase + (uint32_t(32 * w) << 16) + kColD + 32 * db + 16, du);
-        }
-        tc::wait_ld();
-        tc::fence_before_sync();
-        mbar_arrive(&s.acc_empty[db]);
-        // term partials, smallest digit first
+        // the issuers' accumulators (gate/up: issuers 0-1 gate, 2-3 up), term
+        // partials smallest digit first, issuers in order
         float pg = 0.0f, pu = 0.0f;
+#pragma unroll 1
+        for (int k = 0; k < kIssuers; ++k) {
+            if (mask & (1u << k)) {
+                float d[16];
+                tc::tmem_ld16(c.tbase + (uint32_t(32 * w) << 16) + kColD + 64 * db + 16 * k, d);
+                tc::wait_ld();
+                float part = 0.0f;
 #pragma unroll
-        for (int n = 0; n < tc::kDigitTerms; ++n) {
-            pg += dg[n];
-        }
-        if (p.kind == 0) {
-#pragma unroll
-            for (int n = 0; n < tc::kDigitTerms; ++n) {
-                pu += du[n];
+                for (int n = 0; n < tc::kDigitTerms; ++n) {
+                    part += d[n];
+                }
+                if (p.kind == 0 && k >= 2) {
+                    pu += part;
+                } else {
+                    pg += part;
+                }
             }
         }
+        tc::fence_before_sync();
+        mbar_arrive(&s.acc_empty[db]);
         EpiTile et;
         et.tile = tile;
         tile_slots(p, tile, et.nslot, et.slot);
@@ -965,16 +977,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         s.abort = 0;
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(&s.full[i], 1);
-            tc::mbar_init(&s.empty[i], 1);
+            tc::mbar_init(&s.empty[i], kIssuers);
         }
         for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&s.acc_full[i], 1);
+            tc::mbar_init(&s.acc_full[i], kIssuers);
             tc::mbar_init(&s.acc_empty[i], 32 * kEpiWarps);
         }
         tc::mbar_init(&s.sel_full, 1);
         tc::mbar_init(&s.setup, 1);
         tc::mbar_init(&s.bsetup, 1);
-        tc::mbar_init(&s.fin, 1);
+        tc::mbar_init(&s.fin, kIssuers);
         tc::fence_mbar_init();
     }
     if (warp == 0) {
@@ -1046,7 +1058,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         xr[pi] = __ldcg(xcur + k);
                         gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
                     }
-                } else if (threadIdx.x == 0) {
+                } else if (warp == kMmaWarp && lane == 0) {  // off the selection's warp
                     asm volatile("fence.proxy.async.global;" ::: "memory");
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     tc::mbar_expect_tx(&s.bsetup, uint32_t(kBlocks * kBRowBytes + kCodeBytes));
@@ -1198,9 +1210,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 } else {
-                    if (!wait_bar(s, &s.bsetup, bsetup_uses & 1u, a.status)) {
+                    // only the warps that read the copied codes wait, one lane
+                    // each (the rest park at the barrier below instead of
+                    // polling beside the selection's warp)
+                    if (warp < kEpiWarps && lane == 0 && !wait_bar(s, &s.bsetup, bsetup_uses & 1u, a.status)) {
                         *reinterpret_cast<volatile int *>(&s.abort) = 1;
                     }
+                    __syncwarp();
                     ++bsetup_uses;
                 }
                 compute_sync();
@@ -1217,8 +1233,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 const Phase pb = gateup_phase(s.n_local);
                 if (warp < kEpiWarps) {
                     run_epilogue(cx, pb, pipe, t, li, false);
-                } else if (warp == kMmaWarp && lane == 0) {
-                    run_mma(cx, pb, pipe);
+                } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
+                    run_mma(cx, pb, pipe, warp - kIssuerWarp0);
                 }
                 __syncwarp();
                 stamp(a, step, 3);
@@ -1231,7 +1247,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 // B for down: the w * hidden terms (written by phase B's reducers)
                 // of the experts this CTA's down units touch (at most kDownSlots),
                 // into shared memory; their scales into tensor memory.
-                if (threadIdx.x == 0) {
+                if (warp == kMmaWarp && lane == 0) {
                     // bdown slots of the experts this CTA's down units touch
                     // (at most kDownSlots), fetched by bulk copies
                     const int ku_tile = s.n_local * kPairs;
@@ -1266,9 +1282,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         bulk_load(&s.dcode[d][0], a.sfb_down + size_t(qs[d]) * kCodeBytes, kCodeBytes, &s.setup);
                     }
                 }
-                if (!wait_bar(s, &s.setup, uint32_t(step) & 1, a.status)) {
+                if (warp < kEpiWarps && lane == 0 && !wait_bar(s, &s.setup, uint32_t(step) & 1, a.status)) {
                     *reinterpret_cast<volatile int *>(&s.abort) = 1;
                 }
+                __syncwarp();
                 compute_sync();
                 if (warp < kEpiWarps) {
                     for (int d = 0; d < kDownSlots; ++d) {
@@ -1283,8 +1300,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 const Phase pc = down_phase(s.n_local);
                 if (warp < kEpiWarps) {
                     run_epilogue(cx, pc, pipe, t, li, next_router);
-                } else if (warp == kMmaWarp && lane == 0) {
-                    run_mma(cx, pc, pipe);
+                } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
+                    run_mma(cx, pc, pipe, warp - kIssuerWarp0);
                 }
                 __syncwarp();
                 stamp(a, step, 6);
@@ -1295,8 +1312,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         if (!ok) {
             *reinterpret_cast<volatile int *>(&s.abort) = 1;
         }
-        // the MMA thread waits for its MMAs
-        if (warp == kMmaWarp && lane == 0) {
+        // the MMA issuers wait for their MMAs
+        if (warp >= kIssuerWarp0 && warp < kIssuerWarp0 + kIssuers && lane == 0) {
             tc::mma_commit(&s.fin);
             tc::mbar_wait(&s.fin, 0);
         }
