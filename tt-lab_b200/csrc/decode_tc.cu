@@ -324,20 +324,31 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
                  : "memory");
 }
 
+__device__ __forceinline__ void bulk_load_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            tc::smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(tc::smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // ---- loads (warp 9, lane 0) ----
+// Expert weights are read once per token: they go through L2 as evict-first,
+// so they do not push out the partials, operands and code the step reuses.
 __device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTopK], Pipe &pp) {
     Smem &s = *c.s;
     const TmaDesc *tm = c.L->tma;
     const uint8_t *gate = c.L->gate;
     const uint8_t *up = c.L->up;
     const uint8_t *down = c.L->down;
+    const uint64_t pol = tc::policy_evict_first();
     return for_each_stage(p, [&](const StageRef &r, bool, bool) {
         const uint32_t st = pp.stage % kStages;
         const uint32_t use = pp.stage / kStages;
         if (use > 0 && !wait_bar(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
             return false;
         }
-        const int e = le[r.q];
+        const int e = (r.q == 0) ? le[0] : (r.q == 1) ? le[1] : (r.q == 2) ? le[2] : le[3];
         const int c0 = r.kb0 >> 2;
         const int c1 = (r.kb0 + r.nkb - 1) >> 2;
         const uint32_t nc = uint32_t(c1 - c0 + 1);
@@ -346,18 +357,18 @@ __device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTop
         if (r.kind == 0) {
             const int x = 16 * (r.kb0 & ~7);  // byte offset of the stage's box in a row
             tc::mbar_expect_tx(&s.full[st], 2 * kBoxTx + 2 * nc * uint32_t(kScaleBlockBytes));
-            tc::tma_load_3d(&s.a[st][0][0][0], tm + kTmaGate, x, row0, e, &s.full[st]);
-            tc::tma_load_3d(&s.a[st][1][0][0], tm + kTmaUp, x, row0, e, &s.full[st]);
-            bulk_load(&s.sfa[st][c0 & 1][0], gate + so, nc * kScaleBlockBytes, &s.full[st]);
-            bulk_load(&s.sfa[st][2 + (c0 & 1)][0], up + so, nc * kScaleBlockBytes, &s.full[st]);
+            tc::tma_load_3d_hint(&s.a[st][0][0][0], tm + kTmaGate, x, row0, e, &s.full[st], pol);
+            tc::tma_load_3d_hint(&s.a[st][1][0][0], tm + kTmaUp, x, row0, e, &s.full[st], pol);
+            bulk_load_hint(&s.sfa[st][c0 & 1][0], gate + so, nc * kScaleBlockBytes, &s.full[st], pol);
+            bulk_load_hint(&s.sfa[st][2 + (c0 & 1)][0], up + so, nc * kScaleBlockBytes, &s.full[st], pol);
         } else {
             const int b0 = r.kb0 >> 3;
             const int b1 = (r.kb0 + r.nkb - 1) >> 3;
             tc::mbar_expect_tx(&s.full[st], uint32_t(b1 - b0 + 1) * kBoxTx + nc * uint32_t(kScaleBlockBytes));
             for (int b = b0; b <= b1; ++b) {
-                tc::tma_load_3d(&s.a[st][b & 1][0][0], tm + kTmaDown, 128 * b, row0, e, &s.full[st]);
+                tc::tma_load_3d_hint(&s.a[st][b & 1][0][0], tm + kTmaDown, 128 * b, row0, e, &s.full[st], pol);
             }
-            bulk_load(&s.sfa[st][c0 & 3][0], down + so, nc * kScaleBlockBytes, &s.full[st]);
+            bulk_load_hint(&s.sfa[st][c0 & 3][0], down + so, nc * kScaleBlockBytes, &s.full[st], pol);
         }
         ++pp.stage;
         return true;
@@ -768,7 +779,13 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             if (nown < kOwnMax) {
                 s.own_part[nown][0][i] = pg;
                 s.own_part[nown][1][i] = pu;
-                own[nown++] = et;
+#pragma unroll
+                for (int k = 0; k < kOwnMax; ++k) {
+                    if (k == nown) {
+                        own[k] = et;
+                    }
+                }
+                ++nown;
             } else if (i == 0) {
                 set_status(a.status, kStatusBadShape);
             }
@@ -786,7 +803,11 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         }
     }
-    for (int k = 0; k < nown; ++k) {
+#pragma unroll
+    for (int k = 0; k < kOwnMax; ++k) {
+        if (k >= nown) {
+            break;
+        }
         if (own[k].tile != first_owned) {
             load_tile_ops(c, p, own[k].tile, t_token, li, next_router, ops);
         }
@@ -832,57 +853,84 @@ __device__ float exact_logit(const float *__restrict__ wrow, float bias, const f
     return acc;
 }
 
-// Warp 0: top 4 of s.logit (lowest index on exact ties); with bounds, flags
-// an interval of a selected expert touching another expert's.
-__device__ void warp_top4(Smem &s, int experts, bool check_bounds) {
+// Order key of expert e: larger logits first, the lower index first among
+// equal logits, NaN after every number (-0 and +0 compare equal).  Keys of
+// different experts differ; an absent expert's key (kAbsentKey) is below all.
+constexpr long long kAbsentKey = static_cast<long long>(0x8000000000000000ull);
+__device__ __forceinline__ long long order_key(float v, int e) {
+    int b = __float_as_int(v + 0.0f);
+    b = (b >= 0) ? b : (b ^ 0x7fffffff);
+    b = (v == v) ? b : int(0x80000000u);
+    return static_cast<long long>((static_cast<unsigned long long>(unsigned(b)) << 32) | unsigned(kMaxExperts - e));
+}
+
+// Ranks of this lane's NPER experts against all 32 * NPER keys, through
+// register shuffles and without branches.
+template <int NPER>
+__device__ __forceinline__ void rank_keys(const long long (&key)[4], int (&rank)[4]) {
+#pragma unroll
+    for (int c = 0; c < NPER; ++c) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const long long kj = __shfl_sync(0xffffffffu, key[c], j);
+#pragma unroll
+            for (int k = 0; k < NPER; ++k) {
+                rank[k] += (kj > key[k]) ? 1 : 0;
+            }
+        }
+    }
+}
+
+// Top-4 of s.logit, by warp 0: lane l ranks experts l, l + 32, ... against
+// all of them, and the experts of rank 0-3 land in s.sel (the keys are a
+// total order, so s.sel is always filled).  Selection sort with a strict
+// ">" (src/model.cpp:296-309) gives the same order whenever the logits are
+// distinct; equal logits are the ambiguous case the callers resolve.
+__device__ __forceinline__ void warp_top4(Smem &s, int experts) {
     const int lane = threadIdx.x & 31;
-    int chosen[4];
-    bool invalid = false;
-    for (int r = 0; r < kTopK; ++r) {
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int i = lane; i < experts; i += 32) {
-            bool taken = false;
-            for (int q = 0; q < r; ++q) {
-                taken |= (chosen[q] == i);
-            }
-            const float v = s.logit[i];
-            if (!taken && (bi == 0x7fffffff || v > bv || (v == bv && i < bi))) {
-                bv = v;
-                bi = i;
-            }
-        }
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi == 0x7fffffff || !(bv == bv)) {
-            invalid = true;
-            bi = r;
-        }
-        chosen[r] = bi;
+    long long key[4];
+    int rank[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k;
+        key[k] = (e < experts) ? order_key(s.logit[e], e) : kAbsentKey;
+        rank[k] = 0;
     }
-    bool amb = invalid;
-    if (check_bounds) {
-        for (int i = lane; i < experts; i += 32) {
-            for (int q = 0; q < kTopK; ++q) {
-                const int a = chosen[q];
-                if (a != i && !(fabsf(s.logit[a] - s.logit[i]) > s.bound[a] + s.bound[i])) {
-                    amb = true;
-                }
-            }
+    static_assert(kMaxExperts == 128, "four keys per lane");
+    if (experts <= 32) {
+        rank_keys<1>(key, rank);
+    } else if (experts <= 64) {
+        rank_keys<2>(key, rank);
+    } else if (experts <= 96) {
+        rank_keys<3>(key, rank);
+    } else {
+        rank_keys<4>(key, rank);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k;
+        if (e < experts && rank[k] < kTopK) {
+            s.sel[rank[k]] = e;
         }
     }
-    amb = __any_sync(0xffffffffu, amb);
-    if (lane == 0) {
-        s.amb = amb ? 1 : 0;
+}
+
+// After warp_top4 and a compute_sync: whether a selected logit is NaN or a
+// selected and another expert's logits are closer than their bounds (the f32
+// order of the reference may differ); sets s.amb, which the caller zeroed
+// before the last compute_sync.
+__device__ __forceinline__ void check_top4(Smem &s, int experts) {
+    bool amb = false;
+    for (int e = threadIdx.x; e < experts; e += kComputeThreads) {
+#pragma unroll
         for (int q = 0; q < kTopK; ++q) {
-            s.sel[q] = chosen[q];
+            const int a = s.sel[q];
+            const float la = s.logit[a];
+            amb = amb | !(la == la) | ((a != e) & !(fabsf(la - s.logit[e]) > s.bound[a] + s.bound[e]));
         }
+    }
+    if (amb) {
+        s.amb = 1;
     }
 }
 
@@ -905,35 +953,50 @@ __device__ __forceinline__ void store_sfb(const uint8_t *codes, uint32_t taddr, 
 }
 
 // Softmax of the selected logits (src/model.cpp:310-321) and this rank's
-// experts; thread 0, then published to the load warp.
-__device__ void publish_selection(Smem &s, const StackArgs &a, bool export_top) {
+// experts, by warp 0 (lane q handles selection q; the maximum and the sum
+// run in rank order as in the reference), then published to the load warp.
+// Called by all 32 lanes of warp 0 after s.sel is visible to them.
+__device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, bool export_top) {
+    const int lane = threadIdx.x & 31;
+    const int q = lane & 3;
+    const int e = s.sel[q];
+    const float v = s.val[e];
+    float v4[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        v4[k] = __shfl_sync(0xffffffffu, v, k);
+    }
     float maximum = -INFINITY;
-    float v[4], wv[4];
-    for (int q = 0; q < kTopK; ++q) {
-        v[q] = s.val[s.sel[q]];
-        maximum = (maximum < v[q]) ? v[q] : maximum;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        maximum = (maximum < v4[k]) ? v4[k] : maximum;
     }
+    const float wq = expf(__fsub_rn(v, maximum));
     float sum = 0.0f;
-    for (int q = 0; q < kTopK; ++q) {
-        wv[q] = expf(__fsub_rn(v[q], maximum));
-        sum = __fadd_rn(sum, wv[q]);
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, wq, k));
     }
-    int n = 0;
-    for (int q = 0; q < kTopK; ++q) {
-        s.wts[q] = __fdiv_rn(wv[q], sum);
-        const int le = s.sel[q] - a.expert_begin;
-        s.local[q] = (le >= 0 && le < a.expert_count) ? le : -1;
-        if (s.local[q] >= 0) {
-            s.slot_of[n++] = q;
+    const int le = e - a.expert_begin;
+    const bool mine = (le >= 0) & (le < a.expert_count) & (lane < kTopK);
+    const unsigned owned = __ballot_sync(0xffffffffu, mine);
+    if (lane < kTopK) {
+        s.wts[q] = __fdiv_rn(wq, sum);
+        s.local[q] = mine ? le : -1;
+        if (mine) {
+            s.slot_of[__popc(owned & ((1u << lane) - 1u))] = q;
+        }
+        if (export_top) {
+            a.top_idx[q] = e;
+            a.top_w[q] = __fdiv_rn(wq, sum);
         }
     }
-    s.n_local = n;
-    mbar_arrive(&s.sel_full);
-    if (export_top) {
-        for (int q = 0; q < kTopK; ++q) {
-            a.top_idx[q] = s.sel[q];
-            a.top_w[q] = s.wts[q];
-        }
+    if (lane == 0) {
+        s.n_local = __popc(owned);
+    }
+    __syncwarp();
+    if (lane == 0) {
+        mbar_arrive(&s.sel_full);
     }
 }
 
@@ -965,6 +1028,9 @@ __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps,
 
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // aligned by offsetting the shared array itself, so that accesses through
+    // s stay shared-memory accesses (a detour through an integer address
+    // would make every one of them a generic access)
     Smem &s = *reinterpret_cast<Smem *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1085,12 +1151,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     }
                     compute_sync();
                     if (warp == 0) {
-                        warp_top4(s, E, false);
+                        warp_top4(s, E);
                         __syncwarp();
-                        if (lane == 0) {
-                            publish_selection(s, a, export_top);
-                        }
-                        __syncwarp();
+                        publish_selection(s, a, export_top);
                     }
                 } else {
                     // CTA e < E: expert e's logit and the bound on the reference's f32 chain.
@@ -1162,10 +1225,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         s.bound[e] = __ldcg(a.bounds + e);
                         s.val[e] = s.logit[e];
                     }
+                    if (threadIdx.x == 0) {
+                        s.amb = 0;
+                    }
                     compute_sync();
                     if (warp == 0) {
-                        warp_top4(s, E, true);
+                        warp_top4(s, E);
                     }
+                    compute_sync();
+                    check_top4(s, E);
                     compute_sync();
                     if (s.amb) {
                         float lower = INFINITY;
@@ -1190,7 +1258,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         }
                         compute_sync();
                     }
-                    if (threadIdx.x == 0) {
+                    if (warp == 0) {
                         publish_selection(s, a, export_top);
                     }
                 }
@@ -1257,14 +1325,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     for (int q = 0; q < kTopK; ++q) {
                         s.dslot[q] = -1;
                     }
-                    int qs[kDownSlots];
+                    static_assert(kDownSlots == 2, "two down slots");
+                    int qs0 = 0, qs1 = 0;
                     int nd = 0;
                     for (int u = u0; u < u1;) {
                         const int ku = u % ku_tile;
                         const int q = ku / kPairs;
                         if (s.dslot[q] < 0) {
                             if (nd < kDownSlots) {
-                                qs[nd] = q;
+                                if (nd == 0) {
+                                    qs0 = q;
+                                } else {
+                                    qs1 = q;
+                                }
                                 s.dslot[q] = nd++;
                             } else {
                                 set_status(a.status, kStatusBadShape);
@@ -1277,9 +1350,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     tc::mbar_expect_tx(&s.setup, uint32_t(nd) * uint32_t(kBlocks * kBRowBytes + kCodeBytes));
                     for (int d = 0; d < nd; ++d) {
-                        bulk_load(&s.bdown[d][0][0], a.bdown + size_t(qs[d]) * kBlocks * kBRowBytes, kBlocks * kBRowBytes,
+                        const int q = (d == 0) ? qs0 : qs1;
+                        bulk_load(&s.bdown[d][0][0], a.bdown + size_t(q) * kBlocks * kBRowBytes, kBlocks * kBRowBytes,
                                   &s.setup);
-                        bulk_load(&s.dcode[d][0], a.sfb_down + size_t(qs[d]) * kCodeBytes, kCodeBytes, &s.setup);
+                        bulk_load(&s.dcode[d][0], a.sfb_down + size_t(q) * kCodeBytes, kCodeBytes, &s.setup);
                     }
                 }
                 if (warp < kEpiWarps && lane == 0 && !wait_bar(s, &s.setup, uint32_t(step) & 1, a.status)) {

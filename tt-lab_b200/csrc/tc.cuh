@@ -174,6 +174,23 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, 
         : "memory");
 }
 
+// L2 policy for data read once: its lines are the first to be evicted.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// tma_load_3d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const void *tmap, int x, int y, int z, uint64_t *bar,
+                                                 uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+        "{%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 // Instruction descriptor: kind::mxf8f6f4, A = E2M1, B = E4M3, scales E8M0,
 // K-major A and B, M = 128, N = n.  sfa_id / sfb_id select the scale byte.
 __device__ __forceinline__ uint32_t instr_desc(uint32_t n, uint32_t sfa_id, uint32_t sfb_id) {
