@@ -115,7 +115,6 @@ struct alignas(1024) Smem {
     uint64_t acc_empty[2];
     uint64_t sel_full;            // the step's selection is published
     uint64_t setup;               // the down B operands of the step landed
-    uint64_t bsetup;              // the gate/up B operand of the step landed (from the previous step)
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier verdict, written by thread 0 only
@@ -154,6 +153,25 @@ __device__ __forceinline__ void fail_wait(Smem &s, uint32_t *status) {
     *reinterpret_cast<volatile int *>(&s.abort) = 1;
 }
 
+// ---- tagged words ----
+// An f32 in the low half and, in the high half, the tag seq + step + 1 of the
+// step that wrote it: one 8-byte access carries both, so a reader that sees
+// the tag has the value, and words of other steps or launches never match.
+__device__ __forceinline__ uint32_t step_tag(const StackArgs &a, int step) {
+    return a.seq + uint32_t(step) + 1u;
+}
+__device__ __forceinline__ unsigned long long tagged(uint32_t tag, float v) {
+    return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void st_tagged(unsigned long long *p, unsigned long long w) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
 // Bounded wait; a phase that already completed costs one try_wait.
 __device__ __forceinline__ bool wait_bar(Smem &s, uint64_t *bar, uint32_t parity, uint32_t *status) {
     if (tc::mbar_try_wait(bar, parity)) {
@@ -167,6 +185,46 @@ __device__ __forceinline__ bool wait_bar(Smem &s, uint64_t *bar, uint32_t parity
         return false;
     }
     return true;
+}
+
+// The value of the tagged word at p once it carries `tag` (w: a first load of
+// it).  Bounded: after a timeout or an abort it returns 0 with the status set.
+__device__ __forceinline__ float wait_tagged_slow(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status) {
+    const unsigned long long t0 = tc::now_ns();
+    while (true) {
+        const unsigned long long w = ld_tagged(p);
+        if (uint32_t(w >> 32) == tag) {
+            return __uint_as_float(uint32_t(w));
+        }
+        if (aborted(s)) {
+            return 0.0f;
+        }
+        if (tc::now_ns() - t0 > 2000000000ull) {
+            fail_wait(s, status);
+            return 0.0f;
+        }
+        __nanosleep(32);  // the reducer's 128 threads poll the same few lines
+    }
+}
+__device__ __forceinline__ float wait_tagged(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status,
+                                             unsigned long long w) {
+    return (uint32_t(w >> 32) == tag) ? __uint_as_float(uint32_t(w)) : wait_tagged_slow(s, p, tag, status);
+}
+
+// Waits (bounded) until the counter at p reaches `want`; acquire.
+__device__ __forceinline__ void wait_count(Smem &s, const unsigned *p, unsigned want, uint32_t *status) {
+    const unsigned long long t0 = tc::now_ns();
+    while (true) {
+        unsigned cur;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(p) : "memory");
+        if (int(cur - want) >= 0 || aborted(s)) {
+            return;
+        }
+        if (tc::now_ns() - t0 > 2000000000ull) {
+            fail_wait(s, status);
+            return;
+        }
+    }
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -281,17 +339,22 @@ struct StageRef {
     int nkb;   // K-blocks in the stage (even)
 };
 
-// Visits this CTA's stages of phase p in order; f(ref, seg_first, seg_last)
-// returns false to stop.
+// Visits this CTA's stages of phase p; f(ref, seg_first, seg_last) returns
+// false to stop.  Segments (one per tile the CTA's unit range touches) go
+// from the last to the first: the last one is the head of a tile a later CTA
+// reduces, so its partial is published first, and the first one -- the tail
+// of a tile this CTA reduces -- comes last, when the earlier CTA's partial of
+// that tile (its first segment) is already out.  Stages within a segment go
+// in K order.  Every role walks the same order.
 template <class F>
 __device__ __forceinline__ bool for_each_stage(const Phase &p, F &&f) {
     const int units = p.tiles * p.kunits;
-    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    int u = range_lo(blockIdx.x, gridDim.x, units);
+    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
     const int span = (p.kind == 0) ? 4 : 8;  // pairs
-    while (u < u1) {
-        const int tile = u / p.kunits;
-        const int seg_end = min(u1, (tile + 1) * p.kunits);
+    for (int seg_end = range_lo(blockIdx.x + 1, gridDim.x, units); seg_end > u0;) {
+        const int tile = (seg_end - 1) / p.kunits;
+        const int seg_lo = max(u0, tile * p.kunits);
+        int u = seg_lo;
         bool first = true;
         while (u < seg_end) {
             const int ku0 = u - tile * p.kunits;
@@ -313,6 +376,7 @@ __device__ __forceinline__ bool for_each_stage(const Phase &p, F &&f) {
             }
             first = false;
         }
+        seg_end = seg_lo;
     }
     return true;
 }
@@ -462,22 +526,26 @@ __device__ __forceinline__ void tile_slots(const Phase &p, int tile, int &n, int
     slot = int(blockIdx.x) - c0;
 }
 
-// Sum over contributors in slot order (this CTA's own partial in `slot`);
-// the loads are issued together.
-__device__ __forceinline__ float ordered_sum(const float *base, size_t stride, int nslot, int slot, float mine) {
-    float v[kMaxSlots];
-#pragma unroll
-    for (int k = 0; k < kMaxSlots; ++k) {
-        v[k] = (k < nslot && k != slot) ? __ldcg(base + k * stride) : 0.0f;
-    }
+// Tagged partials of tile `tile` in phase p of `step`: [slot][256 or 128].
+__device__ __forceinline__ size_t part_stride(const Phase &p) {
+    return (p.kind == 0) ? 256 : 128;
+}
+__device__ __forceinline__ unsigned long long *part_base(const StackArgs &a, const Phase &p, int step, int tile) {
+    return (p.kind == 0 ? a.part_gu + size_t(step & 1) * (kPartGuWords / 2)
+                        : a.part_dn + size_t(step & 1) * (kPartDnWords / 2)) +
+           size_t(tile) * kMaxSlots * part_stride(p);
+}
+
+// Sum over the contributors in slot order; this CTA reduces the tile, so its
+// own partial `mine` is the last one.  p: this row's word of slot 0.
+__device__ __forceinline__ float tagged_sum(Smem &s, const unsigned long long *p, size_t stride, int nslot, float mine,
+                                            uint32_t tag, uint32_t *status) {
     float sum = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kMaxSlots; ++k) {
-        if (k < nslot) {
-            sum += (k == slot) ? mine : v[k];
-        }
+    for (int k = 0; k + 1 < nslot; ++k) {
+        const unsigned long long *pk = p + size_t(k) * stride;
+        sum += wait_tagged(s, pk, tag, status, ld_tagged(pk));
     }
-    return sum;
+    return sum + mine;
 }
 
 // Sums v[0..15] over the warp's 32 lanes: afterwards lane l holds the total of
@@ -597,33 +665,15 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const int nl = a.layer_end - a.layer_begin;
     const bool more_layers = (li + 1 < nl);
     const int tile = et.tile;
+    const int step = t_token * nl + li;
+    const uint32_t tag = step_tag(a, step);
     if (et.nslot > 1) {
-        const size_t stride = (p.kind == 0) ? 256 : 128;
-        const float *base = (p.kind == 0 ? a.part_gu : a.part_dn) + size_t(tile) * kMaxSlots * stride;
-        unsigned *cnt = (p.kind == 0 ? a.cnt_gu : a.cnt_dn) + tile;
-        if (i == 0) {
-            const unsigned want = unsigned(et.nslot - 1);
-            const unsigned long long t0 = tc::now_ns();
-            unsigned cur = 0;
-            while (true) {
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(cnt) : "memory");
-                if (cur == want || aborted(s)) {
-                    break;
-                }
-                if (tc::now_ns() - t0 > kGridWaitNs) {
-                    fail_wait(s, a.status);
-                    break;
-                }
-            }
-            *cnt = 0u;  // the tile's next use is after a grid barrier
-        }
-        epi_sync();
-        if (aborted(s)) {
-            return;
-        }
-        pg = ordered_sum(base + i, stride, et.nslot, et.slot, pg);
+        // the other contributors' tagged partials (after an abort the sums
+        // are garbage; every later wait returns at once)
+        const unsigned long long *base = part_base(a, p, step, tile) + i;
+        pg = tagged_sum(s, base, part_stride(p), et.nslot, pg, tag, a.status);
         if (p.kind == 0) {
-            pu = ordered_sum(base + 128 + i, stride, et.nslot, et.slot, pu);
+            pu = tagged_sum(s, base + 128, part_stride(p), et.nslot, pu, tag, a.status);
         }
     }
     if (p.kind == 0) {
@@ -638,10 +688,16 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
                 h = __fmul_rn(swiglu_ref(gv, uv), s.wts[s.slot_of[q]]);
             }
             const int kb = row >> 5;
-            const uint32_t code = tc::digit_split_store(h, a.bdown + (size_t(q) * kBlocks + kb) * kBRowBytes, lane);
+            uint8_t *bd = a.bdown + size_t(step & 1) * (kBdownBytes / 2);
+            const uint32_t code = tc::digit_split_store(h, bd + (size_t(q) * kBlocks + kb) * kBRowBytes, lane);
             if (lane == 0) {
-                a.sfb_down[size_t(q) * kCodeBytes + kb] = uint8_t(code);
+                a.sfb_down[size_t(step & 1) * (kSfbDownBytes / 2) + size_t(q) * kCodeBytes + kb] = uint8_t(code);
             }
+        }
+        // this tile of expert slot q is in place for the down phase
+        epi_sync();
+        if (i == 0) {
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_b + q) : "memory");
         }
         return;
     }
@@ -663,9 +719,10 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         // scale is a scalar applied to the products)
         if (row - lane < kDim) {
             const int kb = row >> 5;
-            const uint32_t code = tc::digit_split_store(xg, a.bnext + size_t(kb) * kBRowBytes, lane);
+            uint8_t *bn = a.bnext + size_t(step & 1) * (kBnextBytes / 2);
+            const uint32_t code = tc::digit_split_store(xg, bn + size_t(kb) * kBRowBytes, lane);
             if (lane == 0) {
-                a.bnext_code[kb] = uint8_t(code);
+                a.bnext_code[size_t(step & 1) * (kBnextCodeBytes / 2) + kb] = uint8_t(code);
             }
         }
         for (int b = 0; 16 * b < E; ++b) {
@@ -693,17 +750,21 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             s.rsum[w][E] = sq;
         }
         epi_sync();
-        const int step = t_token * nl + li;
-        double *acc = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
+        // this tile's router sums for the next step; the count released
+        // after them also covers this tile's y and next B-operand rows
+        double *rp = a.rp + (size_t(step & 1) * kTiles + tile) * (kMaxExperts + 1);
         for (int e = i; e < E + 1; e += 32 * kEpiWarps) {
             double tot = 0.0;
 #pragma unroll
             for (int k = 0; k < kEpiWarps; ++k) {
                 tot += s.rsum[k][e];
             }
-            atomicAdd(acc + e, tot);
+            rp[e] = tot;
         }
         epi_sync();
+        if (i == 0) {
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_r) : "memory");
+        }
     }
 }
 
@@ -718,17 +779,20 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
     // The first tile whose last unit lies in this CTA's range is reduced here;
     // its operands are loaded now, while the MMAs run.
     const int first_owned = (u0 + p.kunits) / p.kunits - 1;
+    const int step = t_token * (a.layer_end - a.layer_begin) + li;
+    const uint32_t tag = step_tag(a, step);
     TileOps ops;
     if (u0 < u1 && (first_owned + 1) * p.kunits - 1 < u1) {
         load_tile_ops(c, p, first_owned, t_token, li, next_router, ops);
     }
     EpiTile own[kOwnMax];
     int nown = 0;
-    for (int u = u0; u < u1;) {
-        const int tile = u / p.kunits;
-        const int seg_lo = u;
-        u = min(u1, (tile + 1) * p.kunits);
-        const uint32_t mask = segment_issuers(p, tile, seg_lo, u);
+    // segments in the order for_each_stage visits them
+    for (int seg_end = u1; seg_end > u0;) {
+        const int tile = (seg_end - 1) / p.kunits;
+        const int seg_lo = max(u0, tile * p.kunits);
+        const uint32_t mask = segment_issuers(p, tile, seg_lo, seg_end);
+        seg_end = seg_lo;
         const uint32_t db = pp.seg & 1;
         const uint32_t duse = pp.seg >> 1;
         ++pp.seg;
@@ -791,16 +855,10 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             }
             continue;
         }
-        const size_t stride = (p.kind == 0) ? 256 : 128;
-        float *base = (p.kind == 0 ? a.part_gu : a.part_dn) + size_t(tile) * kMaxSlots * stride;
-        base[et.slot * stride + i] = pg;
+        unsigned long long *base = part_base(a, p, step, tile) + size_t(et.slot) * part_stride(p);
+        st_tagged(base + i, tagged(tag, pg));
         if (p.kind == 0) {
-            base[et.slot * stride + 128 + i] = pu;
-        }
-        epi_sync();
-        if (i == 0) {
-            unsigned *cnt = (p.kind == 0 ? a.cnt_gu : a.cnt_dn) + tile;
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+            st_tagged(base + 128 + i, tagged(tag, pu));
         }
     }
 #pragma unroll
@@ -816,6 +874,59 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
             return;
         }
     }
+}
+
+// Stack mode, step > 0: the router sums of `step` and its gate/up B
+// operand, both written by the down reducers of the previous step.  Every
+// reducer counts its tile in a.cnt_r after writing them; thread 0 waits for
+// the count, then all loads go out together: the B operand (bytes and block
+// codes) into s.bgu / s.gcode, and thread e <= E sums expert e's 23 tile
+// partials in tile order (every CTA gets the same sums) into s.rsum[0][e].
+// Needs a compute_sync before any of it is read.
+__device__ __forceinline__ void gather_step_inputs(Smem &s, const StackArgs &a, int step, int E) {
+    const int ct = threadIdx.x;
+    if (ct == 0) {
+        wait_count(s, a.cnt_r, unsigned(kTiles) * unsigned(step), a.status);
+    }
+    compute_sync();
+    const size_t par = size_t((step - 1) & 1);
+    constexpr int kVec = kBlocks * kBRowBytes / 16;
+    constexpr int kVecPer = (kVec + kComputeThreads - 1) / kComputeThreads;
+    const uint4 *bn = reinterpret_cast<const uint4 *>(a.bnext + par * (kBnextBytes / 2));
+    uint4 bv[kVecPer];
+#pragma unroll
+    for (int k = 0; k < kVecPer; ++k) {
+        const int idx = ct + k * kComputeThreads;
+        bv[k] = (idx < kVec) ? __ldcg(bn + idx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    const uint32_t *bc = reinterpret_cast<const uint32_t *>(a.bnext_code + par * (kBnextCodeBytes / 2));
+    const uint32_t code4 = (ct < kCodeBytes / 4) ? __ldcg(bc + ct) : 0u;
+    if (ct <= E) {
+        const double *rp = a.rp + par * kTiles * (kMaxExperts + 1) + ct;
+        double v[kTiles];
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t) {
+            v[t] = __ldcg(rp + t * (kMaxExperts + 1));
+        }
+        double sum = 0.0;
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t) {
+            sum += v[t];
+        }
+        s.rsum[0][ct] = sum;
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(&s.bgu[0][0]);
+#pragma unroll
+    for (int k = 0; k < kVecPer; ++k) {
+        const int idx = ct + k * kComputeThreads;
+        if (idx < kVec) {
+            dst[idx] = bv[k];
+        }
+    }
+    if (ct < kCodeBytes / 4) {
+        reinterpret_cast<uint32_t *>(s.gcode)[ct] = code4;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // s.bgu is read by the MMAs
 }
 
 __device__ void select_top4_ref(const float *vals, int experts, int idx[4]) {
@@ -1051,7 +1162,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         }
         tc::mbar_init(&s.sel_full, 1);
         tc::mbar_init(&s.setup, 1);
-        tc::mbar_init(&s.bsetup, 1);
         tc::mbar_init(&s.fin, kIssuers);
         tc::fence_mbar_init();
     }
@@ -1078,7 +1188,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         // ---------------- compute group: warps 0-8 ----------------
         const int ct = threadIdx.x;  // 0..287
         Pipe pipe;
-        uint32_t bsetup_uses = 0;
+        unsigned want_b0 = 0, want_b1 = 0, want_b2 = 0, want_b3 = 0;  // warp 8, lane 0
         // Router sums of (token 0, first layer) in stack mode.
         if (a.mode == 1) {
             const StackLayer &L = a.layers[a.layer_begin];
@@ -1124,30 +1234,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         xr[pi] = __ldcg(xcur + k);
                         gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
                     }
-                } else if (warp == kMmaWarp && lane == 0) {  // off the selection's warp
-                    asm volatile("fence.proxy.async.global;" ::: "memory");
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    tc::mbar_expect_tx(&s.bsetup, uint32_t(kBlocks * kBRowBytes + kCodeBytes));
-                    bulk_load(&s.bgu[0][0], a.bnext, kBlocks * kBRowBytes, &s.bsetup);
-                    bulk_load(&s.gcode[0], a.bnext_code, kCodeBytes, &s.bsetup);
                 }
                 float scale = 1.0f;
                 // ---------------- A: selection ----------------
                 if (a.mode == 1) {
-                    const double *acc = a.acc + size_t(step & 1) * (kMaxExperts + 1);
-                    const float ss = float(__ldcg(acc + E));
+                    // router sums: the kernel's opening pass (step 0) or the
+                    // previous step's down reducers
+                    if (step > 0) {
+                        gather_step_inputs(s, a, step, E);
+                    }
+                    compute_sync();
+                    stamp(a, step, 4);
+                    const double *sums = (step > 0) ? &s.rsum[0][0] : a.acc;
+                    const float ss = float(sums[E]);
                     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(kDim)), 1.0e-5f)));
                     for (int e = ct; e < E; e += kComputeThreads) {
-                        const double p = __ldcg(acc + e);
-                        const float lg = float(double(L.router_b[e]) + double(scale) * p);
+                        const float lg = float(double(L.router_b[e]) + double(scale) * sums[e]);
                         s.logit[e] = lg;
                         s.val[e] = lg;
-                    }
-                    if (blockIdx.x == 0) {
-                        double *other = a.acc + size_t((step + 1) & 1) * (kMaxExperts + 1);
-                        for (int e = ct; e < E + 1; e += kComputeThreads) {
-                            other[e] = 0.0;
-                        }
                     }
                     compute_sync();
                     if (warp == 0) {
@@ -1209,8 +1313,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                                 abs_total += s.red[k];
                             }
                             const double logit = double(L.router_b[e]) + total;
-                            a.logits[e] = float(logit);
-                            a.bounds[e] = float((1.02 * 5.9604644775390625e-08 * abs_total +
+                            a.logits[(step & 1) * kMaxExperts + e] = float(logit);
+                            a.bounds[(step & 1) * kMaxExperts + e] = float((1.02 * 5.9604644775390625e-08 * abs_total +
                                                  5.9604644775390625e-08 * fabs(logit) + 1e-30) *
                                                 1.0001);
                         }
@@ -1221,8 +1325,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         break;
                     }
                     for (int e = ct; e < E; e += kComputeThreads) {
-                        s.logit[e] = __ldcg(a.logits + e);
-                        s.bound[e] = __ldcg(a.bounds + e);
+                        s.logit[e] = __ldcg(a.logits + (step & 1) * kMaxExperts + e);
+                        s.bound[e] = __ldcg(a.bounds + (step & 1) * kMaxExperts + e);
                         s.val[e] = s.logit[e];
                     }
                     if (threadIdx.x == 0) {
@@ -1277,15 +1381,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         }
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                } else {
-                    // only the warps that read the copied codes wait, one lane
-                    // each (the rest park at the barrier below instead of
-                    // polling beside the selection's warp)
-                    if (warp < kEpiWarps && lane == 0 && !wait_bar(s, &s.bsetup, bsetup_uses & 1u, a.status)) {
-                        *reinterpret_cast<volatile int *>(&s.abort) = 1;
-                    }
-                    __syncwarp();
-                    ++bsetup_uses;
                 }
                 compute_sync();
                 if (warp < kEpiWarps) {
@@ -1306,11 +1401,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 }
                 __syncwarp();
                 stamp(a, step, 3);
-                ok = grid_barrier(a.barrier, gen, a.status, s);
-                if (!ok) {
-                    break;
-                }
-                stamp(a, step, 4);
                 // ---------------- C: down ----------------
                 // B for down: the w * hidden terms (written by phase B's reducers)
                 // of the experts this CTA's down units touch (at most kDownSlots),
@@ -1325,6 +1415,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     for (int q = 0; q < kTopK; ++q) {
                         s.dslot[q] = -1;
                     }
+                    // gate/up tiles each expert slot has had reduced through this step
+                    const int nloc = s.n_local;
+                    want_b0 += (nloc > 0) ? unsigned(kTiles) : 0u;
+                    want_b1 += (nloc > 1) ? unsigned(kTiles) : 0u;
+                    want_b2 += (nloc > 2) ? unsigned(kTiles) : 0u;
+                    want_b3 += (nloc > 3) ? unsigned(kTiles) : 0u;
                     static_assert(kDownSlots == 2, "two down slots");
                     int qs0 = 0, qs1 = 0;
                     int nd = 0;
@@ -1346,14 +1442,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         }
                         u += min(kPairs - ku % kPairs, u1 - u);
                     }
+                    // the down B operand of these slots is complete once all their
+                    // gate/up tiles of this step are reduced
+                    for (int d = 0; d < nd; ++d) {
+                        const int q = (d == 0) ? qs0 : qs1;
+                        const unsigned want = (q == 0) ? want_b0 : (q == 1) ? want_b1 : (q == 2) ? want_b2 : want_b3;
+                        wait_count(s, a.cnt_b + q, want, a.status);
+                    }
                     asm volatile("fence.proxy.async.global;" ::: "memory");
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     tc::mbar_expect_tx(&s.setup, uint32_t(nd) * uint32_t(kBlocks * kBRowBytes + kCodeBytes));
+                    const uint8_t *bd = a.bdown + size_t(step & 1) * (kBdownBytes / 2);
+                    const uint8_t *sd = a.sfb_down + size_t(step & 1) * (kSfbDownBytes / 2);
                     for (int d = 0; d < nd; ++d) {
                         const int q = (d == 0) ? qs0 : qs1;
-                        bulk_load(&s.bdown[d][0][0], a.bdown + size_t(q) * kBlocks * kBRowBytes, kBlocks * kBRowBytes,
-                                  &s.setup);
-                        bulk_load(&s.dcode[d][0], a.sfb_down + size_t(q) * kCodeBytes, kCodeBytes, &s.setup);
+                        bulk_load(&s.bdown[d][0][0], bd + size_t(q) * kBlocks * kBRowBytes, kBlocks * kBRowBytes, &s.setup);
+                        bulk_load(&s.dcode[d][0], sd + size_t(q) * kCodeBytes, kCodeBytes, &s.setup);
                     }
                 }
                 if (warp < kEpiWarps && lane == 0 && !wait_bar(s, &s.setup, uint32_t(step) & 1, a.status)) {
@@ -1379,7 +1483,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 }
                 __syncwarp();
                 stamp(a, step, 6);
-                ok = grid_barrier(a.barrier, gen, a.status, s);
+                // every compute thread leaves or stays together
+                compute_sync();
+                if (threadIdx.x == 0) {
+                    s.go = aborted(s) ? 0 : 1;
+                }
+                compute_sync();
+                ok = s.go != 0;
                 stamp(a, step, 7);
             }
         }

@@ -100,28 +100,41 @@ struct StackArgs {
     int expert_begin;
     int expert_count;
     double *acc;               // [2][129] router sums (f64), zeroed by the host before a launch
-    float *logits;             // [E] mode 0
-    float *bounds;             // [E] mode 0
+    float *logits;             // [2][128] mode 0 (steps of even and odd index in turn)
+    float *bounds;             // [2][128] mode 0
     float *hidden;             // [4][2880]
     int32_t *top_idx;          // [4] selection of the last (token, layer)
     float *top_w;              // [4]
     unsigned *barrier;         // [2] arrival count (zeroed by the host before a launch), generation
     uint32_t *status;
     unsigned long long *counters;
-    // tensor-core decode workspace
-    float *part_gu;            // [4 * 23 tiles][16 slots][256] gate/up tile partials
-    float *part_dn;            // [23 tiles][16 slots][128] down tile partials
-    unsigned *cnt_gu;          // [4 * 23] contributor counters (zeroed by the host)
-    unsigned *cnt_dn;          // [23]
-    uint8_t *bdown;            // [4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
-    uint8_t *sfb_down;         // [4][96] their block codes (90 + padding, 127)
-    uint8_t *bnext;            // [90 K-blocks][2][8][16] next step's gate/up B operand: digit terms of x * g
-    uint8_t *bnext_code;       // [96] their block codes (90 + padding, 127)
+    // tensor-core decode workspace.  Buffers marked [2] are used by steps of
+    // even and odd index in turn; "tagged" words hold an f32 in the low half
+    // and, in the high half, the tag seq + step + 1 of the step that wrote it.
+    uint32_t seq;                  // tag base of this launch (the host advances it by the launch's steps)
+    unsigned long long *part_gu;   // [2][4 * 23 tiles][16 slots][256] gate/up tile partials, tagged
+    unsigned long long *part_dn;   // [2][23 tiles][16 slots][128] down tile partials, tagged
+    double *rp;                    // [2][23 tiles][129] next step's router sums per down tile
+    unsigned *cnt_b;               // [4] gate/up tiles reduced per expert slot (zeroed by the host)
+    unsigned *cnt_r;               // [1] down tiles whose router sums are written (zeroed by the host)
+    uint8_t *bdown;                // [2][4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
+    uint8_t *sfb_down;             // [2][4][96] their block codes (90 + padding, 127)
+    uint8_t *bnext;                // [2][90 K-blocks][2][8][16] next step's gate/up B operand: digit terms of x * g
+    uint8_t *bnext_code;           // [2][96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
 };
 
 constexpr int kTracePoints = 10;
+
+// Sizes of the tensor-core decode workspace (StackArgs), in elements.
+constexpr size_t kPartGuWords = size_t(2) * 4 * 23 * 16 * 256;
+constexpr size_t kPartDnWords = size_t(2) * 23 * 16 * 128;
+constexpr size_t kRpWords = size_t(2) * 23 * 129;
+constexpr size_t kBdownBytes = size_t(2) * 4 * 90 * 256;
+constexpr size_t kSfbDownBytes = size_t(2) * 4 * 96;
+constexpr size_t kBnextBytes = size_t(2) * 90 * 256;
+constexpr size_t kBnextCodeBytes = size_t(2) * 96;
 
 size_t decode_tc_smem_bytes();
 void configure_decode_tc();

@@ -90,13 +90,15 @@ struct ttl_moe {
     // persistent decode kernel
     bool use_stack = true;
     bool use_tc = true;               // tensor-core persistent kernel (else the CUDA-core one)
-    float *d_part_gu = nullptr;
-    float *d_part_dn = nullptr;
-    unsigned *d_cnt = nullptr;        // [4 * 45 + 23]
+    unsigned long long *d_part_gu = nullptr;  // tagged tile partials, [2] x gate/up and down
+    unsigned long long *d_part_dn = nullptr;
+    double *d_rp = nullptr;           // router sums per down tile
+    unsigned *d_cnt = nullptr;        // [5] gate/up tiles reduced per expert slot, down tiles with router sums
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
     uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
     uint8_t *d_bnext_code = nullptr;
+    uint32_t seq = 0;                 // tag base of the next launch
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
@@ -347,10 +349,13 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.barrier = h->d_barrier;
     a.status = h->d_status;
     a.counters = h->d_counters;
+    a.seq = h->seq;
+    h->seq += uint32_t(tokens) * uint32_t(end - begin);
     a.part_gu = h->d_part_gu;
     a.part_dn = h->d_part_dn;
-    a.cnt_gu = h->d_cnt;
-    a.cnt_dn = h->d_cnt + 4 * 45;
+    a.rp = h->d_rp;
+    a.cnt_b = h->d_cnt;
+    a.cnt_r = h->d_cnt + 4;
     a.bdown = h->d_bdown;
     a.sfb_down = h->d_sfb_down;
     a.bnext = h->d_bnext;
@@ -362,7 +367,7 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     }
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
-    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned), h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, 5 * sizeof(unsigned), h->stream));
     const bool prof = h->profile && mode == 1;
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
@@ -578,8 +583,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_counters, 4);
     rc = rc ? rc : alloc_n(h, &h->d_ones, kDim);
     rc = rc ? rc : alloc_n(h, &h->dw.h, kDim);
-    rc = rc ? rc : alloc_n(h, &h->dw.logits, E);
-    rc = rc ? rc : alloc_n(h, &h->dw.bounds, E);
+    rc = rc ? rc : alloc_n(h, &h->dw.logits, 2 * size_t(kMaxExperts));
+    rc = rc ? rc : alloc_n(h, &h->dw.bounds, 2 * size_t(kMaxExperts));
     rc = rc ? rc : alloc_n(h, &h->dw.top_idx, 4);
     rc = rc ? rc : alloc_n(h, &h->dw.top_w, 4);
     rc = rc ? rc : alloc_n(h, &h->dw.hidden, 4 * size_t(kDim));
@@ -592,13 +597,14 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_pack_flags, 1);
     rc = rc ? rc : alloc_n(h, &h->d_acc, 2 * (kMaxExperts + 1));
     rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
-    rc = rc ? rc : alloc_n(h, &h->d_part_gu, size_t(4 * 23) * 16 * 256);
-    rc = rc ? rc : alloc_n(h, &h->d_part_dn, size_t(23) * 16 * 128);
-    rc = rc ? rc : alloc_n(h, &h->d_cnt, 4 * 45 + 23);
-    rc = rc ? rc : alloc_n(h, &h->d_bdown, size_t(4) * 90 * 256);
-    rc = rc ? rc : alloc_n(h, &h->d_sfb_down, size_t(4) * 96);
-    rc = rc ? rc : alloc_n(h, &h->d_bnext, size_t(90) * 256);
-    rc = rc ? rc : alloc_n(h, &h->d_bnext_code, size_t(96));
+    rc = rc ? rc : alloc_n(h, &h->d_part_gu, kPartGuWords);
+    rc = rc ? rc : alloc_n(h, &h->d_part_dn, kPartDnWords);
+    rc = rc ? rc : alloc_n(h, &h->d_rp, kRpWords);
+    rc = rc ? rc : alloc_n(h, &h->d_cnt, 5);
+    rc = rc ? rc : alloc_n(h, &h->d_bdown, kBdownBytes);
+    rc = rc ? rc : alloc_n(h, &h->d_sfb_down, kSfbDownBytes);
+    rc = rc ? rc : alloc_n(h, &h->d_bnext, kBnextBytes);
+    rc = rc ? rc : alloc_n(h, &h->d_bnext_code, kBnextCodeBytes);
     if (rc) {
         return bail(rc);
     }
@@ -630,11 +636,14 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(h->d_cnt, 0, (4 * 45 + 23) * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(h->d_bdown, 0, size_t(4) * 90 * 256) != cudaSuccess ||
-        cudaMemset(h->d_sfb_down, 0x7f, size_t(4) * 96) != cudaSuccess ||
-        cudaMemset(h->d_bnext, 0, size_t(90) * 256) != cudaSuccess ||
-        cudaMemset(h->d_bnext_code, 0x7f, size_t(96)) != cudaSuccess ||
+        cudaMemset(h->d_cnt, 0, 5 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_part_gu, 0, kPartGuWords * 8) != cudaSuccess ||
+        cudaMemset(h->d_part_dn, 0, kPartDnWords * 8) != cudaSuccess ||
+        cudaMemset(h->d_rp, 0, kRpWords * 8) != cudaSuccess ||
+        cudaMemset(h->d_bdown, 0, kBdownBytes) != cudaSuccess ||
+        cudaMemset(h->d_sfb_down, 0x7f, kSfbDownBytes) != cudaSuccess ||
+        cudaMemset(h->d_bnext, 0, kBnextBytes) != cudaSuccess ||
+        cudaMemset(h->d_bnext_code, 0x7f, kBnextCodeBytes) != cudaSuccess ||
         cudaMemset(h->d_layers, 0, c.layers * sizeof(StackLayer)) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "device initialisation failed"));
     }
