@@ -95,6 +95,35 @@ constexpr int kPreE = 32;                     // next-layer router weights the d
 constexpr int kOwnMax = 3;                    // tiles a CTA reduces in one phase (checked)
 constexpr unsigned long long kGridWaitNs = 2000000000ull;
 
+// ---- per-CTA work plans ----
+// The stages and segments of one phase for one number of local experts,
+// walked in the order every role uses (computed once per launch, so the
+// per-stage loops do no unit arithmetic).
+constexpr int kPlanStages = 24;  // stages of one phase (checked)
+constexpr int kPlanSegs = 6;     // segments of one phase (checked)
+struct PlanStage {
+    uint8_t tile;   // 128-row tile of the expert's matrix (0..22)
+    uint8_t q;      // expert slot
+    uint8_t kb0;    // first K-block (even)
+    uint8_t nkb;    // K-blocks (even)
+    uint8_t flags;  // kFirst: first stage of a segment, kLast: last
+    uint8_t pad[3];
+};
+constexpr uint8_t kFirst = 1;
+constexpr uint8_t kLast = 2;
+struct PlanSeg {
+    uint8_t tile;   // tile of the phase (gate/up: slot * 23 + tile)
+    uint8_t mask;   // MMA issuers with K-blocks in the segment
+    uint8_t nslot;  // contributors to the tile
+    uint8_t slot;   // this CTA's slot; nslot - 1: this CTA reduces the tile
+};
+struct Plan {
+    PlanStage st[kPlanStages];
+    PlanSeg seg[kPlanSegs];
+    int nst;
+    int nseg;
+};
+
 struct alignas(1024) Smem {
     uint8_t a[kStages][2][128][128];              // A stages: two boxes of 128 rows x 256 E2M1, swizzled
     uint8_t sfa[kStages][4][kScaleBlockBytes];    // their scale blocks (gate/up: gate 0-1, up 2-3; down: 0-3)
@@ -104,6 +133,7 @@ struct alignas(1024) Smem {
     alignas(16) uint8_t dcode[kDownSlots][kCodeBytes];  // down B block codes
     double rsum[kEpiWarps][kMaxExperts + 1];      // next-layer router sums per epilogue warp
     float own_part[kOwnMax][2][128];              // partials of the tiles this CTA reduces (gate, up)
+    Plan plan[kTopK + 1][2];                      // [local experts][phase]
     int dslot[kTopK];                             // expert slot -> bdown slot, -1 if unused
     float logit[kMaxExperts];
     float bound[kMaxExperts];
@@ -331,55 +361,6 @@ struct Ctx {
 // What one stage holds.  Gate/up: K-blocks of one aligned group of 8 (one
 // weight box), gate rows in box 0 and up rows in box 1.  Down: K-blocks of
 // one aligned group of 16, K-blocks 8b..8b+7 in box b & 1.
-struct StageRef {
-    int kind;
-    int tile;
-    int q;     // expert slot (index into slot_of)
-    int kb0;   // first K-block (even)
-    int nkb;   // K-blocks in the stage (even)
-};
-
-// Visits this CTA's stages of phase p; f(ref, seg_first, seg_last) returns
-// false to stop.  Segments (one per tile the CTA's unit range touches) go
-// from the last to the first: the last one is the head of a tile a later CTA
-// reduces, so its partial is published first, and the first one -- the tail
-// of a tile this CTA reduces -- comes last, when the earlier CTA's partial of
-// that tile (its first segment) is already out.  Stages within a segment go
-// in K order.  Every role walks the same order.
-template <class F>
-__device__ __forceinline__ bool for_each_stage(const Phase &p, F &&f) {
-    const int units = p.tiles * p.kunits;
-    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-    const int span = (p.kind == 0) ? 4 : 8;  // pairs
-    for (int seg_end = range_lo(blockIdx.x + 1, gridDim.x, units); seg_end > u0;) {
-        const int tile = (seg_end - 1) / p.kunits;
-        const int seg_lo = max(u0, tile * p.kunits);
-        int u = seg_lo;
-        bool first = true;
-        while (u < seg_end) {
-            const int ku0 = u - tile * p.kunits;
-            StageRef r;
-            r.kind = p.kind;
-            r.q = ku0 / kPairs;
-            const int pr = ku0 - r.q * kPairs;
-            r.tile = tile;
-            if (p.kind == 0) {
-                r.q = tile / kTiles;
-                r.tile = tile - r.q * kTiles;
-            }
-            const int np = min(min((pr & ~(span - 1)) + span, kPairs) - pr, seg_end - u);
-            r.kb0 = 2 * pr;
-            r.nkb = 2 * np;
-            u += np;
-            if (!f(r, first, u == seg_end)) {
-                return false;
-            }
-            first = false;
-        }
-        seg_end = seg_lo;
-    }
-    return true;
-}
 
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -399,14 +380,15 @@ __device__ __forceinline__ void bulk_load_hint(void *dst, const void *src, uint3
 // ---- loads (warp 9, lane 0) ----
 // Expert weights are read once per token: they go through L2 as evict-first,
 // so they do not push out the partials, operands and code the step reuses.
-__device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTopK], Pipe &pp) {
+__device__ bool produce_phase(const Ctx &c, const Plan &pl, int kind, const int (&le)[kTopK], Pipe &pp) {
     Smem &s = *c.s;
     const TmaDesc *tm = c.L->tma;
     const uint8_t *gate = c.L->gate;
     const uint8_t *up = c.L->up;
     const uint8_t *down = c.L->down;
     const uint64_t pol = tc::policy_evict_first();
-    return for_each_stage(p, [&](const StageRef &r, bool, bool) {
+    for (int si = 0; si < pl.nst; ++si) {
+        const PlanStage r = pl.st[si];
         const uint32_t st = pp.stage % kStages;
         const uint32_t use = pp.stage / kStages;
         if (use > 0 && !wait_bar(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
@@ -418,7 +400,7 @@ __device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTop
         const uint32_t nc = uint32_t(c1 - c0 + 1);
         const int row0 = 128 * r.tile;
         const size_t so = size_t(e) * kPackedMatrixBytes + scale_block_offset(r.tile, c0);
-        if (r.kind == 0) {
+        if (kind == 0) {
             const int x = 16 * (r.kb0 & ~7);  // byte offset of the stage's box in a row
             tc::mbar_expect_tx(&s.full[st], 2 * kBoxTx + 2 * nc * uint32_t(kScaleBlockBytes));
             tc::tma_load_3d_hint(&s.a[st][0][0][0], tm + kTmaGate, x, row0, e, &s.full[st], pol);
@@ -435,8 +417,8 @@ __device__ bool produce_phase(const Ctx &c, const Phase &p, const int (&le)[kTop
             bulk_load_hint(&s.sfa[st][c0 & 3][0], down + so, nc * kScaleBlockBytes, &s.full[st], pol);
         }
         ++pp.stage;
-        return true;
-    });
+    }
+    return true;
 }
 
 // Issuers that have K-blocks in a segment of phase p: issuer k owns, in each
@@ -456,31 +438,32 @@ __device__ __forceinline__ uint32_t segment_issuers(const Phase &p, int tile, in
 }
 
 // ---- MMA issuers (warps 4-7, lane 0; issuer k = warp - 4) ----
-__device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp, int k) {
+__device__ void run_mma(const Ctx &c, const Plan &pl, int kind, Pipe &pp, int k) {
     Smem &s = *c.s;
     const uint32_t a0 = tc::smem_u32(&s.a[0][0][0][0]);
     const uint32_t sf0 = tc::smem_u32(&s.sfa[0][0][0]);
     const uint32_t tbase = c.tbase;
     uint32_t db = 0;
     bool first = true;
-    for_each_stage(p, [&](const StageRef &r, bool seg_first, bool seg_last) {
-        if (seg_first) {
+    for (int si = 0; si < pl.nst; ++si) {
+        const PlanStage r = pl.st[si];
+        if (r.flags & kFirst) {
             db = pp.seg & 1;
             const uint32_t duse = pp.seg >> 1;
             if (duse > 0 && !wait_bar(s, &s.acc_empty[db], (duse - 1) & 1, c.a->status)) {
-                return false;
+                return;
             }
             tc::fence_after_sync();
             first = true;
         }
         const uint32_t st = pp.stage % kStages;
         if (!wait_bar(s, &s.full[st], (pp.stage / kStages) & 1, c.a->status)) {
-            return false;
+            return;
         }
         tc::fence_after_sync();
         // this issuer's scale chunk of the stage and its K-blocks in it
-        const int m = (r.kind == 0) ? (k >> 1) : 0;
-        const int chunk = (r.kind == 0) ? ((r.kb0 & ~7) >> 2) + (k & 1) : ((r.kb0 & ~15) >> 2) + k;
+        const int m = (kind == 0) ? (k >> 1) : 0;
+        const int chunk = (kind == 0) ? ((r.kb0 & ~7) >> 2) + (k & 1) : ((r.kb0 & ~15) >> 2) + k;
         const int lo = max(r.kb0, 4 * chunk);
         const int hi = min(r.kb0 + r.nkb, 4 * chunk + 4);
         if (lo < hi) {
@@ -489,7 +472,7 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp, int k) {
             tc::sf_copy(sfa, sf0 + st * uint32_t(sizeof(s.sfa[0])) + kScaleBlockBytes * uint32_t(k));
             const uint32_t dcol = tbase + kColD + 64 * db + 16 * uint32_t(k);
             uint32_t bbase, sfb0;
-            if (r.kind == 0) {
+            if (kind == 0) {
                 bbase = tc::smem_u32(&s.bgu[0][0]);
                 sfb0 = tbase + kColSfbG;
             } else {
@@ -499,7 +482,7 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp, int k) {
             }
             for (int kb = lo; kb < hi; kb += 2) {
                 const uint32_t sel = uint32_t(kb & 3);
-                const uint32_t box = (r.kind == 0) ? uint32_t(m) : uint32_t((kb >> 3) & 1);
+                const uint32_t box = (kind == 0) ? uint32_t(m) : uint32_t((kb >> 3) & 1);
                 const uint32_t aoff = 16384u * box + 32u * uint32_t((kb >> 1) & 3);
                 const uint64_t bd = tc::smem_desc(bbase + uint32_t(kb) * kBRowBytes, kBRowBytes, 128);
                 tc::mma_f4(dcol, tc::smem_desc_sw128(abase + aoff), bd, tc::instr_desc_f4(kN, sel), sfa | (sel << 30),
@@ -509,12 +492,11 @@ __device__ void run_mma(const Ctx &c, const Phase &p, Pipe &pp, int k) {
         }
         tc::mma_commit(&s.empty[st]);
         ++pp.stage;
-        if (seg_last) {
+        if (r.flags & kLast) {
             tc::mma_commit(&s.acc_full[db]);
             ++pp.seg;
         }
-        return true;
-    });
+    }
 }
 
 // Number of contributors to tile t and the slot of this CTA.
@@ -524,6 +506,63 @@ __device__ __forceinline__ void tile_slots(const Phase &p, int tile, int &n, int
     const int c1 = cta_of((tile + 1) * p.kunits - 1, gridDim.x, units);
     n = c1 - c0 + 1;
     slot = int(blockIdx.x) - c0;
+}
+
+// The plan of phase p for this CTA (one thread).  Segments (one per tile the
+// CTA's unit range touches) go from the last to the first: the last one is
+// the head of a tile a later CTA reduces, so its partial is published first,
+// and the first one -- the tail of a tile this CTA reduces -- comes last,
+// when the earlier CTA's partial of that tile (its first segment) is already
+// out.  Stages within a segment go in K order; a stage spans one aligned
+// group of 4 (gate/up) or 8 (down) K-block pairs.
+__device__ void build_plan(Plan &pl, const Phase &p, uint32_t *status) {
+    const int units = p.tiles * p.kunits;
+    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
+    const int span = (p.kind == 0) ? 4 : 8;  // pairs
+    int nst = 0, nseg = 0;
+    for (int seg_end = range_lo(blockIdx.x + 1, gridDim.x, units); seg_end > u0;) {
+        const int tile = (seg_end - 1) / p.kunits;
+        const int seg_lo = max(u0, tile * p.kunits);
+        if (nseg < kPlanSegs) {
+            int n, slot;
+            tile_slots(p, tile, n, slot);
+            PlanSeg &g = pl.seg[nseg];
+            g.tile = uint8_t(tile);
+            g.mask = uint8_t(segment_issuers(p, tile, seg_lo, seg_end));
+            g.nslot = uint8_t(min(n, 255));
+            g.slot = uint8_t(slot);
+        }
+        ++nseg;
+        uint8_t flags = kFirst;
+        for (int u = seg_lo; u < seg_end;) {
+            const int ku0 = u - tile * p.kunits;
+            int q = ku0 / kPairs;
+            const int pr = ku0 - q * kPairs;
+            int t = tile;
+            if (p.kind == 0) {
+                q = tile / kTiles;
+                t = tile - q * kTiles;
+            }
+            const int np = min(min((pr & ~(span - 1)) + span, kPairs) - pr, seg_end - u);
+            u += np;
+            if (nst < kPlanStages) {
+                PlanStage &r = pl.st[nst];
+                r.tile = uint8_t(t);
+                r.q = uint8_t(q);
+                r.kb0 = uint8_t(2 * pr);
+                r.nkb = uint8_t(2 * np);
+                r.flags = uint8_t(flags | (u == seg_end ? kLast : 0));
+            }
+            ++nst;
+            flags = 0;
+        }
+        seg_end = seg_lo;
+    }
+    if (nst > kPlanStages || nseg > kPlanSegs) {
+        set_status(status, kStatusBadShape);
+    }
+    pl.nst = min(nst, kPlanStages);
+    pl.nseg = min(nseg, kPlanSegs);
 }
 
 // Tagged partials of tile `tile` in phase p of `step`: [slot][256 or 128].
@@ -538,19 +577,30 @@ __device__ __forceinline__ unsigned long long *part_base(const StackArgs &a, con
 
 // Sum over the contributors in slot order; this CTA reduces the tile, so its
 // own partial `mine` is the last one.  p: this row's word of slot 0.
+// The loads of up to eight contributors go out together.
 __device__ __forceinline__ float tagged_sum(Smem &s, const unsigned long long *p, size_t stride, int nslot, float mine,
                                             uint32_t tag, uint32_t *status) {
+    constexpr int kBatch = 8;
     float sum = 0.0f;
-    for (int k = 0; k + 1 < nslot; ++k) {
-        const unsigned long long *pk = p + size_t(k) * stride;
-        sum += wait_tagged(s, pk, tag, status, ld_tagged(pk));
+    for (int k0 = 0; k0 + 1 < nslot; k0 += kBatch) {
+        unsigned long long w[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            w[j] = (k0 + j + 1 < nslot) ? ld_tagged(p + size_t(k0 + j) * stride) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (k0 + j + 1 < nslot) {
+                sum += wait_tagged(s, p + size_t(k0 + j) * stride, tag, status, w[j]);
+            }
+        }
     }
     return sum + mine;
 }
 
 // Sums v[0..15] over the warp's 32 lanes: afterwards lane l holds the total of
 // value 8*b4 + 4*b3 + 2*b2 + b1 (b = bits of l), identical in lanes l and l^1.
-__device__ __forceinline__ double transpose_sum16(double (&v)[16], int lane) {
+__device__ __forceinline__ float transpose_sum16(float (&v)[16], int lane) {
 #pragma unroll
     for (int lvl = 0; lvl < 4; ++lvl) {
         const int off = 16 >> lvl;
@@ -559,8 +609,8 @@ __device__ __forceinline__ double transpose_sum16(double (&v)[16], int lane) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             if (j < half) {
-                const double send = upper ? v[j] : v[j + half];
-                const double keep = upper ? v[j + half] : v[j];
+                const float send = upper ? v[j] : v[j + half];
+                const float keep = upper ? v[j + half] : v[j];
                 v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
             }
         }
@@ -710,11 +760,10 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     }
     if (next_router) {
         // router sums of the next (token, layer) over these rows: per warp,
-        // products transposed-summed over the 32 rows
+        // f32 products transposed-summed over the 32 rows (f64 from there on)
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const float xr = more_layers ? yv : o.xnext;
         const float xg = __fmul_rn(xr, o.nw);  // 0 past the last row
-        const double xgd = double(xg);
         // the next step's gate/up B operand: digit terms of x * g (the RMSNorm
         // scale is a scalar applied to the products)
         if (row - lane < kDim) {
@@ -726,23 +775,23 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             }
         }
         for (int b = 0; 16 * b < E; ++b) {
-            double v[16];
+            float v[16];
             if (b < kPreE / 16) {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    v[j] = double(b == 0 ? o.rw[j] : o.rw[16 + j]) * xgd;
+                    v[j] = __fmul_rn(b == 0 ? o.rw[j] : o.rw[16 + j], xg);
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int e = 16 * b + j;
-                    v[j] = (e < E && row < kDim) ? double(__ldg(N.router_w + size_t(e) * kDim + row)) * xgd : 0.0;
+                    v[j] = (e < E && row < kDim) ? __fmul_rn(__ldg(N.router_w + size_t(e) * kDim + row), xg) : 0.0f;
                 }
             }
-            const double tot = transpose_sum16(v, lane);
+            const float tot = transpose_sum16(v, lane);
             const int e = 16 * b + transpose_index(lane);
             if ((lane & 1) == 0 && e < E) {
-                s.rsum[w][e] = tot;
+                s.rsum[w][e] = double(tot);
             }
         }
         const double sq = warp_sum_d(row < kDim ? double(__fmul_rn(xr, xr)) : 0.0);
@@ -768,31 +817,32 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     }
 }
 
-__device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token, int li, bool next_router) {
+__device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe &pp, int t_token, int li,
+                             bool next_router) {
     Smem &s = *c.s;
     const StackArgs &a = *c.a;
     const int i = threadIdx.x;  // 0..127: tile row
     const int w = i >> 5;
-    const int units = p.tiles * p.kunits;
-    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
-    // The first tile whose last unit lies in this CTA's range is reduced here;
-    // its operands are loaded now, while the MMAs run.
-    const int first_owned = (u0 + p.kunits) / p.kunits - 1;
+    // The first tile this CTA reduces (in plan order) has its operands loaded
+    // now, while the MMAs run.
+    int first_owned = -1;
+    for (int g = pl.nseg - 1; g >= 0; --g) {
+        if (pl.seg[g].slot + 1 == pl.seg[g].nslot) {
+            first_owned = pl.seg[g].tile;
+        }
+    }
     const int step = t_token * (a.layer_end - a.layer_begin) + li;
     const uint32_t tag = step_tag(a, step);
     TileOps ops;
-    if (u0 < u1 && (first_owned + 1) * p.kunits - 1 < u1) {
+    if (first_owned >= 0) {
         load_tile_ops(c, p, first_owned, t_token, li, next_router, ops);
     }
     EpiTile own[kOwnMax];
     int nown = 0;
-    // segments in the order for_each_stage visits them
-    for (int seg_end = u1; seg_end > u0;) {
-        const int tile = (seg_end - 1) / p.kunits;
-        const int seg_lo = max(u0, tile * p.kunits);
-        const uint32_t mask = segment_issuers(p, tile, seg_lo, seg_end);
-        seg_end = seg_lo;
+    for (int g = 0; g < pl.nseg; ++g) {
+        const PlanSeg sg = pl.seg[g];
+        const int tile = sg.tile;
+        const uint32_t mask = sg.mask;
         const uint32_t db = pp.seg & 1;
         const uint32_t duse = pp.seg >> 1;
         ++pp.seg;
@@ -831,7 +881,8 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, Pipe &pp, int t_token
         mbar_arrive(&s.acc_empty[db]);
         EpiTile et;
         et.tile = tile;
-        tile_slots(p, tile, et.nslot, et.slot);
+        et.nslot = sg.nslot;
+        et.slot = sg.slot;
         if (et.nslot > kMaxSlots) {
             if (i == 0) {
                 set_status(a.status, kStatusBadShape);
@@ -1127,7 +1178,7 @@ __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps,
         }
         Ctx c = c0;
         c.L = &a.layers[a.layer_begin + step % nl];
-        if (!produce_phase(c, gateup_phase(n), le, pp) || !produce_phase(c, down_phase(n), le, pp)) {
+        if (!produce_phase(c, s.plan[n][0], 0, le, pp) || !produce_phase(c, s.plan[n][1], 1, le, pp)) {
             break;
         }
     }
@@ -1172,6 +1223,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     // padding of the gate/up block codes (K-blocks 90..95)
     if (threadIdx.x < kCodeBytes - kBlocks) {
         s.gcode[kBlocks + threadIdx.x] = 127u;
+    }
+    // work plans for 0..4 local experts: lane 0 of warp w builds (w / 2, w % 2)
+    if (lane == 0 && warp < 2 * (kTopK + 1)) {
+        const int n = warp >> 1;
+        build_plan(s.plan[n][warp & 1], (warp & 1) ? down_phase(n) : gateup_phase(n), a.status);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc::fence_before_sync();
@@ -1394,10 +1450,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 // ---------------- B: gate/up ----------------
                 Ctx cx{&a, &L, &s, tbase};
                 const Phase pb = gateup_phase(s.n_local);
+                const Plan &plb = s.plan[s.n_local][0];
                 if (warp < kEpiWarps) {
-                    run_epilogue(cx, pb, pipe, t, li, false);
+                    run_epilogue(cx, pb, plb, pipe, t, li, false);
                 } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
-                    run_mma(cx, pb, pipe, warp - kIssuerWarp0);
+                    run_mma(cx, plb, 0, pipe, warp - kIssuerWarp0);
                 }
                 __syncwarp();
                 stamp(a, step, 3);
@@ -1408,10 +1465,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 if (warp == kMmaWarp && lane == 0) {
                     // bdown slots of the experts this CTA's down units touch
                     // (at most kDownSlots), fetched by bulk copies
-                    const int ku_tile = s.n_local * kPairs;
-                    const int units = kTiles * ku_tile;
-                    const int u0 = range_lo(blockIdx.x, gridDim.x, units);
-                    const int u1 = range_lo(blockIdx.x + 1, gridDim.x, units);
+                    const Plan &pd = s.plan[s.n_local][1];
                     for (int q = 0; q < kTopK; ++q) {
                         s.dslot[q] = -1;
                     }
@@ -1424,9 +1478,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     static_assert(kDownSlots == 2, "two down slots");
                     int qs0 = 0, qs1 = 0;
                     int nd = 0;
-                    for (int u = u0; u < u1;) {
-                        const int ku = u % ku_tile;
-                        const int q = ku / kPairs;
+                    for (int si = 0; si < pd.nst; ++si) {
+                        const int q = pd.st[si].q;
                         if (s.dslot[q] < 0) {
                             if (nd < kDownSlots) {
                                 if (nd == 0) {
@@ -1440,7 +1493,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                                 s.dslot[q] = 0;
                             }
                         }
-                        u += min(kPairs - ku % kPairs, u1 - u);
                     }
                     // the down B operand of these slots is complete once all their
                     // gate/up tiles of this step are reduced
@@ -1476,10 +1528,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 stamp(a, step, 5);
                 const bool next_router = (a.mode == 1) && (li + 1 < nl || t + 1 < a.tokens);
                 const Phase pc = down_phase(s.n_local);
+                const Plan &plc = s.plan[s.n_local][1];
                 if (warp < kEpiWarps) {
-                    run_epilogue(cx, pc, pipe, t, li, next_router);
+                    run_epilogue(cx, pc, plc, pipe, t, li, next_router);
                 } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
-                    run_mma(cx, pc, pipe, warp - kIssuerWarp0);
+                    run_mma(cx, plc, 1, pipe, warp - kIssuerWarp0);
                 }
                 __syncwarp();
                 stamp(a, step, 6);
