@@ -261,11 +261,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
+// Named barriers of whole warps: bar.sync needs every lane of a warp to
+// execute it together, and a warp whose lanes diverged before (one lane
+// polling, publishing, ...) would otherwise arrive twice and let the others
+// through early, so each warp reconverges first.
 __device__ __forceinline__ void epi_sync() {
+    __syncwarp();
     asm volatile("bar.sync 2, 128;" ::: "memory");
 }
 
 __device__ __forceinline__ void compute_sync() {
+    __syncwarp();
     asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory");
 }
 
@@ -1231,6 +1237,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc::fence_before_sync();
+    __syncwarp();  // warps reconverge before the block barrier (see compute_sync)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tbase = s.tmem;
@@ -1517,10 +1524,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 }
                 __syncwarp();
                 compute_sync();
-                if (warp < kEpiWarps) {
-                    for (int d = 0; d < kDownSlots; ++d) {
-                        store_sfb(s.dcode[d], tbase + (uint32_t(32 * warp) << 16) + kColSfbD + kSfbCols * d, lane);
-                    }
+                // slot d's scales by warps 4d .. 4d + 3 (warp w reaches lanes 32 (w % 4) ..)
+                static_assert(kDownSlots * 4 <= kComputeWarps, "one warp quadrant set per down slot");
+                if (warp < 4 * kDownSlots) {
+                    const int d = warp >> 2;
+                    store_sfb(s.dcode[d], tbase + (uint32_t(32 * (warp & 3)) << 16) + kColSfbD + kSfbCols * d, lane);
                 }
                 tc::fence_before_sync();
                 compute_sync();
@@ -1556,6 +1564,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         }
     }
     tc::fence_before_sync();
+    __syncwarp();
     __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
