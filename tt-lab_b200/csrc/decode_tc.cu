@@ -571,6 +571,32 @@ __device__ void build_plan(Plan &pl, const Phase &p, uint32_t *status) {
     pl.nseg = min(nseg, kPlanSegs);
 }
 
+// tagged_sum of the gate (p) and up (p + 128) partials together: the loads
+// of both go out at once, four contributors at a time.
+__device__ __forceinline__ void tagged_sum2(Smem &s, const unsigned long long *p, size_t stride, int nslot, float &g,
+                                            float &u, uint32_t tag, uint32_t *status) {
+    constexpr int kBatch = 4;
+    float sg = 0.0f, su = 0.0f;
+    for (int k0 = 0; k0 + 1 < nslot; k0 += kBatch) {
+        unsigned long long wg[kBatch], wu[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            const bool in = k0 + j + 1 < nslot;
+            wg[j] = in ? ld_tagged(p + size_t(k0 + j) * stride) : 0ull;
+            wu[j] = in ? ld_tagged(p + 128 + size_t(k0 + j) * stride) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+            if (k0 + j + 1 < nslot) {
+                sg += wait_tagged(s, p + size_t(k0 + j) * stride, tag, status, wg[j]);
+                su += wait_tagged(s, p + 128 + size_t(k0 + j) * stride, tag, status, wu[j]);
+            }
+        }
+    }
+    g = sg + g;
+    u = su + u;
+}
+
 // Tagged partials of tile `tile` in phase p of `step`: [slot][256 or 128].
 __device__ __forceinline__ size_t part_stride(const Phase &p) {
     return (p.kind == 0) ? 256 : 128;
@@ -727,9 +753,10 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         // the other contributors' tagged partials (after an abort the sums
         // are garbage; every later wait returns at once)
         const unsigned long long *base = part_base(a, p, step, tile) + i;
-        pg = tagged_sum(s, base, part_stride(p), et.nslot, pg, tag, a.status);
         if (p.kind == 0) {
-            pu = tagged_sum(s, base + 128, part_stride(p), et.nslot, pu, tag, a.status);
+            tagged_sum2(s, base, part_stride(p), et.nslot, pg, pu, tag, a.status);
+        } else {
+            pg = tagged_sum(s, base, part_stride(p), et.nslot, pg, tag, a.status);
         }
     }
     if (p.kind == 0) {
@@ -1301,6 +1328,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 float scale = 1.0f;
                 // ---------------- A: selection ----------------
                 if (a.mode == 1) {
+                    // the router bias is loaded before the wait for the sums
+                    static_assert(kMaxExperts <= kComputeThreads, "one expert per compute thread");
+                    const float rb = (ct < E) ? __ldg(L.router_b + ct) : 0.0f;
                     // router sums: the kernel's opening pass (step 0) or the
                     // previous step's down reducers
                     if (step > 0) {
@@ -1311,10 +1341,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     const double *sums = (step > 0) ? &s.rsum[0][0] : a.acc;
                     const float ss = float(sums[E]);
                     scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(kDim)), 1.0e-5f)));
-                    for (int e = ct; e < E; e += kComputeThreads) {
-                        const float lg = float(double(L.router_b[e]) + double(scale) * sums[e]);
-                        s.logit[e] = lg;
-                        s.val[e] = lg;
+                    if (ct < E) {
+                        const float lg = float(double(rb) + double(scale) * sums[ct]);
+                        s.logit[ct] = lg;
+                        s.val[ct] = lg;
                     }
                     compute_sync();
                     if (warp == 0) {
