@@ -6,13 +6,13 @@
 // a decode call; one CTA per SM.
 //
 // Roles (10 warps):
-//   warps 0-8  the compute group: selection, B-operand preparation and the
-//              grid barriers; warps 0-3 also run the epilogues (one thread
+//   warps 0-8  the compute group: selection and B-operand preparation;
+//              warps 0-3 also run the epilogues (one thread
 //              per tile row, TMEM lane quadrant = warp); lane 0 of each of
 //              warps 4-7 issues the block-scaled MMAs of one scale chunk of
 //              every stage into its own accumulator (one issuing thread
 //              sustains about one MMA per 150 cycles, four about one per 40);
-//              lane 0 of warp 8 issues the operand bulk copies
+//              lane 0 of warp 8 waits for and copies the down operand
 //   warp 9     lane 0 issues the loads into the stage ring: per stage 32 KB
 //              of packed E2M1 weights as two 128-byte x 128-row TMA boxes
 //              (128-byte swizzle: the K-major layout of the MMA's A operand)
@@ -20,6 +20,8 @@
 //              tile blocks (already in tcgen05.cp order).  It follows the
 //              published selection only, so the down-projection weights stream
 //              in while the grid is still finishing the gate/up phase.
+// Each CTA builds its work plans (stages and segments of both phases for 0..4
+// local experts) once per launch; the roles walk them.
 //
 // Products are kind::mxf4 block-scaled MMAs (A = the weights' E2M1 nibbles
 // with their E8M0 scales, untouched; K = 64 per instruction).  The B operand
@@ -28,12 +30,14 @@
 // exact to 2^-24 of each K-block's largest value; the accumulator's 16
 // columns are the per-term partial products, summed in the epilogue.
 //
-// Per layer:
-//   A  select   Every CTA reads the layer's router sums (f64, accumulated by
-//               the previous layer's epilogues -- the RMSNorm scale is a
-//               scalar, so logit_e = b_e + s * sum_c W_ec g_c x_c splits over
-//               row slices), picks the same top 4 and, meanwhile, splits
-//               h = RMSNorm(x)*g into its digit terms (the B operand).
+// Per step (token x layer), with no grid barrier:
+//   A  select   Every CTA waits for the previous step's 23 down tiles to
+//               count their router sums out, adds them in tile order (so all
+//               CTAs get the same sums -- the RMSNorm scale is a scalar, so
+//               logit_e = b_e + s * sum_c W_ec g_c x_c splits over row slices),
+//               loads the B operand those tiles wrote (digit terms of x*g) and
+//               picks the same top 4.  The first step of a launch splits
+//               h = RMSNorm(x)*g itself.
 //               Mode 0 (one plain MoE, h given) computes the logits in a
 //               router phase with an error bound instead and re-evaluates
 //               near-ties exactly in the reference's order, so its indices
@@ -43,15 +47,20 @@
 //               accumulators).  Each CTA takes an equal contiguous range of
 //               units (stream-K).  The last contributor to a tile sums the
 //               partials in order, adds the biases, applies SwiGLU and the
-//               routing weight, and writes the tile's 128 hidden values as
-//               digit terms -- the B operand of the down projection.
-//   -- grid barrier --
+//               routing weight, writes the tile's 128 hidden values as digit
+//               terms -- the B operand of the down projection -- and counts
+//               the tile on its expert slot.
 //   C  down     Units are (128-row tile, expert x K-block pair): the four experts'
 //               down projections accumulate into one tensor (the routing
-//               weights are already in B).  The last contributor adds
-//               sum_q w_q b_q, the residual, writes the output rows and (stack
-//               mode) accumulates the next layer's router sums for them.
-//   -- grid barrier --
+//               weights are already in B).  A CTA starts once the gate/up tiles
+//               of the expert slots it reads are all counted.  The last
+//               contributor adds sum_q w_q b_q, the residual, writes the output
+//               rows and (stack mode) the next step's B operand and router
+//               sums for them, then counts the tile.
+// Split-K partials travel as tagged words (value + step tag in one 8-byte
+// store), so a reducer polls the data itself.  Buffers alternate between
+// even and odd steps: a CTA starts step s + 2 only after every CTA has
+// contributed to step s + 1, so nothing of step s is still being read.
 // Every wait is bounded; on timeout the kernel records kStatusWaitTimeout,
 // drains its own copies and MMAs, frees its tensor memory and returns.
 #include <cuda_runtime.h>
@@ -147,7 +156,7 @@ struct alignas(1024) Smem {
     uint64_t setup;               // the down B operands of the step landed
     uint64_t fin;
     uint32_t tmem;
-    int go;      // grid-barrier verdict, written by thread 0 only
+    int go;      // grid-barrier / end-of-step verdict, written by thread 0 only
     int epi_go;  // epilogue verdict, written by thread 0 only
     int sel[kTopK];
     int local[kTopK];
@@ -655,12 +664,11 @@ __device__ __forceinline__ int transpose_index(int lane) {
 }
 
 // ---- epilogue warps (0-3): one thread per tile row ----
-// Every contributor to a tile but the last publishes its partial (store, then
-// a release-add on the tile's counter) and moves on; the last contributor --
-// the CTA holding the tile's last units -- reduces: it waits for the count,
-// sums the partials in slot order and finishes the tile.  A CTA first reads
-// all of its segments (so its partials for other tiles go out at once), then
-// reduces the tiles it owns.
+// Every contributor to a tile but the last publishes its partial as tagged
+// words and moves on; the last contributor -- the CTA holding the tile's last
+// units -- reduces: it polls the words, sums the partials in slot order and
+// finishes the tile.  A CTA first reads all of its segments (so its partials
+// for other tiles go out at once), then reduces the tiles it owns.
 struct EpiTile {
     int tile;
     int nslot;
