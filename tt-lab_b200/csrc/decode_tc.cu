@@ -242,7 +242,6 @@ __device__ __forceinline__ float wait_tagged_slow(Smem &s, const unsigned long l
             fail_wait(s, status);
             return 0.0f;
         }
-        __nanosleep(32);  // the reducer's 128 threads poll the same few lines
     }
 }
 __device__ __forceinline__ float wait_tagged(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status,
@@ -1221,6 +1220,14 @@ __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps,
         c.L = &a.layers[a.layer_begin + step % nl];
         if (!produce_phase(c, s.plan[n][0], 0, le, pp) || !produce_phase(c, s.plan[n][1], 1, le, pp)) {
             break;
+        }
+        // the next step's tensor maps, while this step's loads are in flight
+        if (step + 1 < steps) {
+            const TmaDesc *nt = a.layers[a.layer_begin + (step + 1) % nl].tma;
+#pragma unroll
+            for (int m = 0; m < kTmaCount; ++m) {
+                asm volatile("prefetch.tensormap [%0];" ::"l"(nt + m) : "memory");
+            }
         }
     }
     for (uint32_t k = 0; k < kStages && k < pp.stage; ++k) {
