@@ -408,6 +408,14 @@ __device__ bool produce_phase(const Ctx &c, const Plan &pl, int kind, const int 
         if (use > 0 && !wait_bar(s, &s.empty[st], (use - 1) & 1, c.a->status)) {
             return false;
         }
+        // the step's first gate/up stages go out two at a time: later ones
+        // wait until the one two before has landed
+        if (kind == 0 && si >= 2 && si < kStages) {
+            const uint32_t prev = pp.stage - 2;
+            if (!wait_bar(s, &s.full[prev % kStages], (prev / kStages) & 1, c.a->status)) {
+                return false;
+            }
+        }
         const int e = (r.q == 0) ? le[0] : (r.q == 1) ? le[1] : (r.q == 2) ? le[2] : le[3];
         const int c0 = r.kb0 >> 2;
         const int c1 = (r.kb0 + r.nkb - 1) >> 2;
@@ -796,6 +804,8 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     if (row < kDim) {
         const float out = __fadd_rn(pg, o.bsum);
         yv = (a.mode == 1) ? __fadd_rn(o.resid, out) : out;
+    }
+    if (!next_router && row < kDim) {
         a.y[size_t(t_token) * kDim + row] = yv;
     }
     if (next_router) {
@@ -804,16 +814,6 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const float xr = more_layers ? yv : o.xnext;
         const float xg = __fmul_rn(xr, o.nw);  // 0 past the last row
-        // the next step's gate/up B operand: digit terms of x * g (the RMSNorm
-        // scale is a scalar applied to the products)
-        if (row - lane < kDim) {
-            const int kb = row >> 5;
-            uint8_t *bn = a.bnext + size_t(step & 1) * (kBnextBytes / 2);
-            const uint32_t code = tc::digit_split_store(xg, bn + size_t(kb) * kBRowBytes, lane);
-            if (lane == 0) {
-                a.bnext_code[size_t(step & 1) * (kBnextCodeBytes / 2) + kb] = uint8_t(code);
-            }
-        }
         for (int b = 0; 16 * b < E; ++b) {
             float v[16];
             if (b < kPreE / 16) {
@@ -839,8 +839,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             s.rsum[w][E] = sq;
         }
         epi_sync();
-        // this tile's router sums for the next step; the count released
-        // after them also covers this tile's y and next B-operand rows
+        // this tile's router sums for the next step, counted first
         double *rp = a.rp + (size_t(step & 1) * kTiles + tile) * (kMaxExperts + 1);
         for (int e = i; e < E + 1; e += 32 * kEpiWarps) {
             double tot = 0.0;
@@ -853,6 +852,26 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         epi_sync();
         if (i == 0) {
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_r) : "memory");
+        }
+        // then this tile's output rows and the next step's gate/up B operand
+        // (digit terms of x * g; the RMSNorm scale is a scalar applied to the
+        // products), counted on their own
+        if (row < kDim) {
+            a.y[size_t(t_token) * kDim + row] = yv;
+        }
+        // the next step's gate/up B operand: digit terms of x * g (the RMSNorm
+        // scale is a scalar applied to the products)
+        if (row - lane < kDim) {
+            const int kb = row >> 5;
+            uint8_t *bn = a.bnext + size_t(step & 1) * (kBnextBytes / 2);
+            const uint32_t code = tc::digit_split_store(xg, bn + size_t(kb) * kBRowBytes, lane);
+            if (lane == 0) {
+                a.bnext_code[size_t(step & 1) * (kBnextCodeBytes / 2) + kb] = uint8_t(code);
+            }
+        }
+        epi_sync();
+        if (i == 0) {
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_r + 1) : "memory");
         }
     }
 }
@@ -974,24 +993,13 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
 // codes) into s.bgu / s.gcode, and thread e <= E sums expert e's 23 tile
 // partials in tile order (every CTA gets the same sums) into s.rsum[0][e].
 // Needs a compute_sync before any of it is read.
-__device__ __forceinline__ void gather_step_inputs(Smem &s, const StackArgs &a, int step, int E) {
+__device__ __forceinline__ void gather_router_sums(Smem &s, const StackArgs &a, int step, int E) {
     const int ct = threadIdx.x;
     if (ct == 0) {
         wait_count(s, a.cnt_r, unsigned(kTiles) * unsigned(step), a.status);
     }
     compute_sync();
     const size_t par = size_t((step - 1) & 1);
-    constexpr int kVec = kBlocks * kBRowBytes / 16;
-    constexpr int kVecPer = (kVec + kComputeThreads - 1) / kComputeThreads;
-    const uint4 *bn = reinterpret_cast<const uint4 *>(a.bnext + par * (kBnextBytes / 2));
-    uint4 bv[kVecPer];
-#pragma unroll
-    for (int k = 0; k < kVecPer; ++k) {
-        const int idx = ct + k * kComputeThreads;
-        bv[k] = (idx < kVec) ? __ldcg(bn + idx) : make_uint4(0u, 0u, 0u, 0u);
-    }
-    const uint32_t *bc = reinterpret_cast<const uint32_t *>(a.bnext_code + par * (kBnextCodeBytes / 2));
-    const uint32_t code4 = (ct < kCodeBytes / 4) ? __ldcg(bc + ct) : 0u;
     if (ct <= E) {
         const double *rp = a.rp + par * kTiles * (kMaxExperts + 1) + ct;
         double v[kTiles];
@@ -1006,6 +1014,26 @@ __device__ __forceinline__ void gather_step_inputs(Smem &s, const StackArgs &a, 
         }
         s.rsum[0][ct] = sum;
     }
+}
+
+__device__ __forceinline__ void gather_next_operand(Smem &s, const StackArgs &a, int step) {
+    const int ct = threadIdx.x;
+    if (ct == 0) {
+        wait_count(s, a.cnt_r + 1, unsigned(kTiles) * unsigned(step), a.status);
+    }
+    compute_sync();
+    const size_t par = size_t((step - 1) & 1);
+    constexpr int kVec = kBlocks * kBRowBytes / 16;
+    constexpr int kVecPer = (kVec + kComputeThreads - 1) / kComputeThreads;
+    const uint4 *bn = reinterpret_cast<const uint4 *>(a.bnext + par * (kBnextBytes / 2));
+    uint4 bv[kVecPer];
+#pragma unroll
+    for (int k = 0; k < kVecPer; ++k) {
+        const int idx = ct + k * kComputeThreads;
+        bv[k] = (idx < kVec) ? __ldcg(bn + idx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    const uint32_t *bc = reinterpret_cast<const uint32_t *>(a.bnext_code + par * (kBnextCodeBytes / 2));
+    const uint32_t code4 = (ct < kCodeBytes / 4) ? __ldcg(bc + ct) : 0u;
     uint4 *dst = reinterpret_cast<uint4 *>(&s.bgu[0][0]);
 #pragma unroll
     for (int k = 0; k < kVecPer; ++k) {
@@ -1349,7 +1377,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     // router sums: the kernel's opening pass (step 0) or the
                     // previous step's down reducers
                     if (step > 0) {
-                        gather_step_inputs(s, a, step, E);
+                        gather_router_sums(s, a, step, E);
                     }
                     compute_sync();
                     stamp(a, step, 4);
@@ -1489,6 +1517,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         }
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                } else {
+                    gather_next_operand(s, a, step);
                 }
                 compute_sync();
                 if (warp < kEpiWarps) {

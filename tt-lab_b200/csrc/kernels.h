@@ -116,7 +116,8 @@ struct StackArgs {
     unsigned long long *part_dn;   // [2][23 tiles][16 slots][128] down tile partials, tagged
     double *rp;                    // [2][23 tiles][129] next step's router sums per down tile
     unsigned *cnt_b;               // [4] gate/up tiles reduced per expert slot (zeroed by the host)
-    unsigned *cnt_r;               // [1] down tiles whose router sums are written (zeroed by the host)
+    unsigned *cnt_r;               // [2] down tiles whose router sums are written, and whose output rows and
+                                   // next B operand are (zeroed by the host)
     uint8_t *bdown;                // [2][4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
     uint8_t *sfb_down;             // [2][4][96] their block codes (90 + padding, 127)
     uint8_t *bnext;                // [2][90 K-blocks][2][8][16] next step's gate/up B operand: digit terms of x * g

@@ -93,7 +93,7 @@ struct ttl_moe {
     unsigned long long *d_part_gu = nullptr;  // tagged tile partials, [2] x gate/up and down
     unsigned long long *d_part_dn = nullptr;
     double *d_rp = nullptr;           // router sums per down tile
-    unsigned *d_cnt = nullptr;        // [5] gate/up tiles reduced per expert slot, down tiles with router sums
+    unsigned *d_cnt = nullptr;        // [6] gate/up tiles reduced per expert slot, down tiles with router sums, and with y
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
     uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
@@ -367,7 +367,7 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     }
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
-    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, 5 * sizeof(unsigned), h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, 6 * sizeof(unsigned), h->stream));
     const bool prof = h->profile && mode == 1;
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
@@ -600,7 +600,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_part_gu, kPartGuWords);
     rc = rc ? rc : alloc_n(h, &h->d_part_dn, kPartDnWords);
     rc = rc ? rc : alloc_n(h, &h->d_rp, kRpWords);
-    rc = rc ? rc : alloc_n(h, &h->d_cnt, 5);
+    rc = rc ? rc : alloc_n(h, &h->d_cnt, 6);
     rc = rc ? rc : alloc_n(h, &h->d_bdown, kBdownBytes);
     rc = rc ? rc : alloc_n(h, &h->d_sfb_down, kSfbDownBytes);
     rc = rc ? rc : alloc_n(h, &h->d_bnext, kBnextBytes);
@@ -636,7 +636,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(h->d_cnt, 0, 5 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_cnt, 0, 6 * sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(h->d_part_gu, 0, kPartGuWords * 8) != cudaSuccess ||
         cudaMemset(h->d_part_dn, 0, kPartDnWords * 8) != cudaSuccess ||
         cudaMemset(h->d_rp, 0, kRpWords * 8) != cudaSuccess ||
