@@ -150,14 +150,16 @@ struct PrefillWork {
     float *logits;            // [T][E]
     int32_t *top_idx;         // [T][4]
     float *top_w;             // [T][4]
-    int32_t *counts;          // [E]
-    int32_t *offsets;         // [E + 1]
-    int32_t *pair_token;      // [4T] token of each routed pair, grouped by expert
-    int32_t *pair_slot;       // [T][4] position of (token, rank) in the grouped order, -1 if not local
-    int32_t *tiles;           // [4T / 8 + E] work list: (expert << 20) | first pair
-    int32_t *tile_count;      // [1]
-    float *hidden;            // [4T][2880] SwiGLU output per pair
-    float *down;              // [4T][2880] down output per pair
+    int32_t *counts;          // [E] routed pairs per local expert
+    int32_t *offsets;         // [E + 1] first slot of each expert (its pairs padded to a multiple of 16)
+    int32_t *pair_token;      // [slots] token of each slot, -1 for padding
+    int32_t *pair_slot;       // [T][4] slot of (token, rank), -1 if not local
+    int32_t *tiles;           // [groups] work list: (expert << 20) | first slot of a 16-slot group
+    int32_t *tile_count;      // [1] groups
+    float *hidden;            // [slots][2880] SwiGLU output per slot
+    float *down;              // [slots][2880] down output per slot
+    uint8_t *bdig;            // [groups][96 K-blocks][16 slots][8 digit rows][16 B] MMA B operand
+    uint8_t *bsfb;            // [groups][24 chunks][512] its scale blocks (tcgen05.cp 32x128b order)
     uint32_t *status;
 };
 
@@ -172,9 +174,16 @@ struct PrefillShape {
 void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
                            cudaStream_t stream);
 void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStream_t stream);
-void launch_prefill_gateup(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
-                           cudaStream_t stream);
-void launch_prefill_down(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, cudaStream_t stream);
+void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
+                           const float *x, cudaStream_t stream);
+void launch_prefill_down(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
+                         cudaStream_t stream);
+// Slots and groups of a prefill of `tokens` tokens over `experts` local experts (capacity).
+constexpr size_t prefill_groups(size_t tokens, size_t experts) {
+    return (4 * tokens) / 16 + experts + 1;
+}
+constexpr size_t kPrefillGroupBytes = size_t(96) * 16 * 128;
+constexpr size_t kPrefillGroupScaleBytes = size_t(24) * 512;
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream);
 
 } // namespace ttl

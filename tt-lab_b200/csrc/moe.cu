@@ -27,6 +27,7 @@
 namespace ttl {
 void configure_decode_kernels();
 void configure_prefill_kernels();
+void configure_prefill_tc();
 } // namespace ttl
 
 using namespace ttl;
@@ -450,10 +451,14 @@ int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     PrefillShape s{int(h->cfg.experts), h->expert_begin, h->expert_count, int(tokens), h->sms};
     launch_prefill_router(L, h->pw, s, x, h->stream);
     launch_prefill_route(h->pw, s, h->stream);
-    launch_prefill_gateup(L, h->pw, s, x, h->stream);
-    launch_prefill_down(L, h->pw, s, h->stream);
+    const TmaDesc *tma = h->host_layers[size_t(layer)].tma;
+    if (!tma) {
+        return fail(h, TTL_ERR_STATE, "layer " + std::to_string(layer) + " has no tensor maps");
+    }
+    launch_prefill_gateup(L, tma, h->pw, s, x, h->stream);
+    launch_prefill_down(L, tma, h->pw, s, h->stream);
     launch_prefill_combine(h->pw, s, out, h->stream);
-    h->launches += 6;
+    h->launches += 8;
     TTL_TRY_CUDA(h, cudaGetLastError());
     if (h->cfg.world > 1) {
         return allreduce(h, out, tokens * kDim);
@@ -570,6 +575,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     }
     configure_decode_kernels();
     configure_prefill_kernels();
+    configure_prefill_tc();
     configure_stack_kernel();
     configure_decode_tc();
     if (cudaEventCreate(&h->stack_ev[0]) != cudaSuccess || cudaEventCreate(&h->stack_ev[1]) != cudaSuccess) {
@@ -617,12 +623,17 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.top_w, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.counts, E);
         rc = rc ? rc : alloc_n(h, &h->pw.offsets, E + 1);
-        rc = rc ? rc : alloc_n(h, &h->pw.pair_token, pairs);
+        // slots: each local expert's pairs padded to 16
+        const size_t groups = prefill_groups(T, size_t(h->expert_count));
+        const size_t slots = 16 * groups;
+        rc = rc ? rc : alloc_n(h, &h->pw.pair_token, slots);
         rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
-        rc = rc ? rc : alloc_n(h, &h->pw.tiles, pairs / 8 + E + 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.tiles, groups);
         rc = rc ? rc : alloc_n(h, &h->pw.tile_count, 1);
-        rc = rc ? rc : alloc_n(h, &h->pw.hidden, pairs * kDim);
-        rc = rc ? rc : alloc_n(h, &h->pw.down, pairs * kDim);
+        rc = rc ? rc : alloc_n(h, &h->pw.hidden, slots * kDim);
+        rc = rc ? rc : alloc_n(h, &h->pw.down, slots * kDim);
+        rc = rc ? rc : alloc_n(h, &h->pw.bdig, groups * kPrefillGroupBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bsfb, groups * kPrefillGroupScaleBytes);
         h->pw.status = h->d_status;
         if (rc) {
             return bail(rc);

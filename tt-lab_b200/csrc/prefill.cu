@@ -11,7 +11,9 @@
 //   histogram   per-expert counts, prefix offsets and buckets that are stable in
 //               token order (src/model.cpp:380-394).
 //   experts     grouped products over each expert's tokens (src/model.cpp:396-448)
-//               with the SwiGLU epilogue (:423-433).
+//               with the SwiGLU epilogue (:423-433): tcgen05 block-scaled MMAs
+//               in prefill_tc.cu, over groups of 16 slots (each expert's pairs
+//               padded to a multiple of 16).
 //   combine     per token, experts in ascending id order, out += w * down with
 //               the product rounded first (src/model.cpp:450-459).
 #include <cuda_runtime.h>
@@ -24,10 +26,7 @@ namespace {
 
 constexpr int kRouterTokens = 8;          // tokens per router CTA
 constexpr int kXRowStride = kDim + 4;     // padded shared row (bank spread)
-constexpr int kTile = 8;                  // routed pairs per expert-product tile
-constexpr int kXStride = 36;              // padded floats per K-block
-constexpr int kTileFloats = kBlocks * kXStride;  // one padded row
-constexpr int kProductThreads = 512;
+constexpr int kGroup = 16;                // slots per expert-product group
 
 __global__ void prefill_router_kernel(LayerDev L, PrefillWork w, int experts, int tokens,
                                       const float *__restrict__ x) {
@@ -130,16 +129,22 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
             offsets[le] = run;
             w.counts[le] = counts[le];
             w.offsets[le] = run;
-            for (int k = 0; k < counts[le]; k += kTile) {
+            for (int k = 0; k < counts[le]; k += kGroup) {
                 w.tiles[tiles++] = (le << 20) | (run + k);
             }
-            run += counts[le];
+            run += (counts[le] + kGroup - 1) / kGroup * kGroup;
         }
         offsets[expert_count] = run;
         w.offsets[expert_count] = run;
         *w.tile_count = tiles;
     }
     __syncthreads();
+    // padding slots of each expert's last group
+    for (int le = threadIdx.x; le < expert_count; le += blockDim.x) {
+        for (int sl = offsets[le] + counts[le]; sl < offsets[le + 1]; ++sl) {
+            w.pair_token[sl] = -1;
+        }
+    }
     // Stable placement: each warp owns experts; tokens are scanned in order.
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -165,176 +170,6 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
                 w.pair_slot[t * 4 + rank] = pos;
             }
             base += __popc(ballot);
-        }
-    }
-}
-
-__device__ __forceinline__ void load_row_padded(float *dst, const float *__restrict__ src) {
-    for (int i = threadIdx.x; i < kDim / 4; i += blockDim.x) {
-        const float4 q = *reinterpret_cast<const float4 *>(src + 4 * i);
-        const int kb = (4 * i) >> 5;
-        *reinterpret_cast<float4 *>(dst + kb * kXStride + ((4 * i) & 31)) = q;
-    }
-}
-
-// Decodes 16 packed bytes into 32 f32 E2M1 values (exact).
-__device__ __forceinline__ void decode_block(const uint4 q, float v[32]) {
-    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int wd = 0; wd < 4; ++wd) {
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const float2 f = __half22float2(e2m1x2_to_half2((words[wd] >> (8 * b)) & 0xffu));
-            v[wd * 8 + b * 2] = f.x;
-            v[wd * 8 + b * 2 + 1] = f.y;
-        }
-    }
-}
-
-__device__ __forceinline__ float dot32(const float v[32], const float *xb) {
-    float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-        const float4 p = *reinterpret_cast<const float4 *>(xb + i);
-        const float4 q = *reinterpret_cast<const float4 *>(xb + i + 4);
-        a0 = fmaf(v[i], p.x, a0);
-        a1 = fmaf(v[i + 1], p.y, a1);
-        a0 = fmaf(v[i + 2], p.z, a0);
-        a1 = fmaf(v[i + 3], p.w, a1);
-        a0 = fmaf(v[i + 4], q.x, a0);
-        a1 = fmaf(v[i + 5], q.y, a1);
-        a0 = fmaf(v[i + 6], q.z, a0);
-        a1 = fmaf(v[i + 7], q.w, a1);
-    }
-    return a0 + a1;
-}
-
-// Grouped gate/up products: one tile = up to kTile routed pairs of one expert.
-// The tile's activations sit in shared memory; each warp takes output rows,
-// lanes split K, and the decoded weights of a block are reused for every pair.
-__global__ void __launch_bounds__(kProductThreads, 1)
-    prefill_gateup_kernel(LayerDev L, PrefillWork w, const float *__restrict__ x) {
-    extern __shared__ __align__(16) float xs[];  // [kTile][kTileFloats]
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int nwarps = kProductThreads / 32;
-    const int tiles = *w.tile_count;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        const int code = w.tiles[tile];
-        const int le = code >> 20;
-        const int first = code & 0xfffff;
-        const int n = min(kTile, w.offsets[le + 1] - first);
-        __syncthreads();
-        for (int p = 0; p < n; ++p) {
-            load_row_padded(xs + p * kTileFloats, x + size_t(w.pair_token[first + p]) * kDim);
-        }
-        __syncthreads();
-        const uint8_t *gm = L.gate + size_t(le) * kPackedMatrixBytes;
-        const uint8_t *um = L.up + size_t(le) * kPackedMatrixBytes;
-        for (int row = warp; row < kDim; row += nwarps) {
-            float ag[kTile], au[kTile];
-#pragma unroll
-            for (int p = 0; p < kTile; ++p) {
-                ag[p] = 0.0f;
-                au[p] = 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const int kb = lane + 32 * j;
-                if (kb < kBlocks) {
-                    const uint4 gq = *reinterpret_cast<const uint4 *>(gm + size_t(row) * kNibbleRowBytes + kb * 16);
-                    const uint4 uq = *reinterpret_cast<const uint4 *>(um + size_t(row) * kNibbleRowBytes + kb * 16);
-                    const float gs = e8m0_ref_scale(gm[scale_offset(row, kb)]);
-                    const float us = e8m0_ref_scale(um[scale_offset(row, kb)]);
-                    float v[32];
-                    decode_block(gq, v);
-#pragma unroll
-                    for (int p = 0; p < kTile; ++p) {
-                        if (p < n) {
-                            ag[p] = fmaf(gs, 2.0f * dot32(v, xs + p * kTileFloats + kb * kXStride), ag[p]);
-                        }
-                    }
-                    decode_block(uq, v);
-#pragma unroll
-                    for (int p = 0; p < kTile; ++p) {
-                        if (p < n) {
-                            au[p] = fmaf(us, 2.0f * dot32(v, xs + p * kTileFloats + kb * kXStride), au[p]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int p = 0; p < kTile; ++p) {
-                ag[p] = warp_sum(ag[p]);
-                au[p] = warp_sum(au[p]);
-            }
-            if (lane == 0) {
-                const float gb = L.gate_b[size_t(le) * kDim + row];
-                const float ub = L.up_b[size_t(le) * kDim + row];
-#pragma unroll
-                for (int p = 0; p < kTile; ++p) {
-                    if (p < n) {
-                        w.hidden[size_t(first + p) * kDim + row] =
-                            swiglu_ref(__fadd_rn(gb, ag[p]), __fadd_rn(ub, au[p]));
-                    }
-                }
-            }
-        }
-    }
-}
-
-__global__ void __launch_bounds__(kProductThreads, 1) prefill_down_kernel(LayerDev L, PrefillWork w) {
-    extern __shared__ __align__(16) float hs[];  // [kTile][kTileFloats]
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int nwarps = kProductThreads / 32;
-    const int tiles = *w.tile_count;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        const int code = w.tiles[tile];
-        const int le = code >> 20;
-        const int first = code & 0xfffff;
-        const int n = min(kTile, w.offsets[le + 1] - first);
-        __syncthreads();
-        for (int p = 0; p < n; ++p) {
-            load_row_padded(hs + p * kTileFloats, w.hidden + size_t(first + p) * kDim);
-        }
-        __syncthreads();
-        const uint8_t *dm = L.down + size_t(le) * kPackedMatrixBytes;
-        for (int row = warp; row < kDim; row += nwarps) {
-            float acc[kTile];
-#pragma unroll
-            for (int p = 0; p < kTile; ++p) {
-                acc[p] = 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 3; ++j) {
-                const int kb = lane + 32 * j;
-                if (kb < kBlocks) {
-                    const uint4 q = *reinterpret_cast<const uint4 *>(dm + size_t(row) * kNibbleRowBytes + kb * 16);
-                    const float sc = e8m0_ref_scale(dm[scale_offset(row, kb)]);
-                    float v[32];
-                    decode_block(q, v);
-#pragma unroll
-                    for (int p = 0; p < kTile; ++p) {
-                        if (p < n) {
-                            acc[p] = fmaf(sc, 2.0f * dot32(v, hs + p * kTileFloats + kb * kXStride), acc[p]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int p = 0; p < kTile; ++p) {
-                acc[p] = warp_sum(acc[p]);
-            }
-            if (lane == 0) {
-                const float db = L.down_b[size_t(le) * kDim + row];
-#pragma unroll
-                for (int p = 0; p < kTile; ++p) {
-                    if (p < n) {
-                        w.down[size_t(first + p) * kDim + row] = __fadd_rn(db, acc[p]);
-                    }
-                }
-            }
         }
     }
 }
@@ -389,10 +224,6 @@ __global__ void prefill_combine_kernel(PrefillWork w, int tokens, float *__restr
 void configure_prefill_kernels() {
     cudaFuncSetAttribute(prefill_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          kRouterTokens * kXRowStride * int(sizeof(float)));
-    cudaFuncSetAttribute(prefill_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kTile * kTileFloats * int(sizeof(float)));
-    cudaFuncSetAttribute(prefill_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kTile * kTileFloats * int(sizeof(float)));
 }
 
 void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
@@ -406,15 +237,6 @@ void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const Prefil
 
 void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStream_t stream) {
     prefill_route_kernel<<<1, 1024, 0, stream>>>(w, s.experts, s.expert_begin, s.expert_count, s.tokens);
-}
-
-void launch_prefill_gateup(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
-                           cudaStream_t stream) {
-    prefill_gateup_kernel<<<s.sms, kProductThreads, kTile * kTileFloats * sizeof(float), stream>>>(L, w, x);
-}
-
-void launch_prefill_down(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, cudaStream_t stream) {
-    prefill_down_kernel<<<s.sms, kProductThreads, kTile * kTileFloats * sizeof(float), stream>>>(L, w);
 }
 
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream) {
