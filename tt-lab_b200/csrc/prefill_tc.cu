@@ -91,7 +91,7 @@ __device__ __forceinline__ uint32_t digit_split8_store(float v, uint8_t *dst, in
 // the scale blocks of its 24 chunks of 4 K-blocks (row m = slot * 8 + digit
 // at [m % 32][m / 32][K-block % 4], the order tcgen05.cp 32x128b moves).
 // from_tokens: slot rows are x of the slot's token; else w.hidden rows.
-__global__ void __launch_bounds__(512) prefill_split_kernel(PrefillWork w, const float *__restrict__ x,
+__global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork w, const float *__restrict__ x,
                                                             bool from_tokens) {
     __shared__ uint8_t codes[kGroup][kPadBlocks];
     const int g = blockIdx.x;
@@ -100,24 +100,31 @@ __global__ void __launch_bounds__(512) prefill_split_kernel(PrefillWork w, const
     }
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
-    const int nwarps = blockDim.x >> 5;
     const int code = w.tiles[g];
     const int le = code >> 20;
     const int first = code & 0xfffff;
     const int nvalid = min(kGroup, w.offsets[le] + w.counts[le] - first);
     uint8_t *dst = w.bdig + size_t(g) * kPrefillGroupBytes;
-    for (int task = warp; task < kGroup * kPadBlocks; task += nwarps) {
-        const int slot = task & (kGroup - 1);
-        const int kb = task >> 4;
-        float v = 0.0f;
-        if (slot < nvalid && kb < kBlocks) {
-            const float *row = from_tokens ? x + size_t(w.pair_token[first + slot]) * kDim
-                                           : w.hidden + size_t(first + slot) * kDim;
-            v = __ldcg(row + kb * 32 + lane);
+    // warp w splits slot w's row (16 warps, 16 slots), eight K-blocks' loads in flight
+    const int slot = warp;
+    const float *row = nullptr;
+    if (slot < nvalid) {
+        row = from_tokens ? x + size_t(w.pair_token[first + slot]) * kDim : w.hidden + size_t(first + slot) * kDim;
+    }
+    static_assert(kPadBlocks % 8 == 0, "K-blocks in batches of 8");
+    for (int kb0 = 0; kb0 < kPadBlocks; kb0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            v[j] = (row && kb0 + j < kBlocks) ? __ldcg(row + (kb0 + j) * 32 + lane) : 0.0f;
         }
-        const uint32_t c = digit_split8_store(v, dst + size_t(kb) * kGroupKbBytes + slot * kDigits * 16, lane);
-        if (lane == 0) {
-            codes[slot][kb] = uint8_t(c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int kb = kb0 + j;
+            const uint32_t c = digit_split8_store(v[j], dst + size_t(kb) * kGroupKbBytes + slot * kDigits * 16, lane);
+            if (lane == 0) {
+                codes[slot][kb] = uint8_t(c);
+            }
         }
     }
     __syncthreads();
