@@ -345,34 +345,49 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
                 break;
             }
             tc::fence_after_sync();
+            // each slot's 8 digit columns added up, four slots of both
+            // accumulators per read; the accumulators are free once read
             const uint32_t lanebase = tbase + (uint32_t(32 * warp) << 16);
-#pragma unroll 1
-            for (int c = 0; c < 128; c += 16) {
-                float d0[16], d1[16];
-                tc::tmem_ld16(lanebase + kColD + uint32_t(c), d0);
-                tc::tmem_ld16(lanebase + kColD + 128 + uint32_t(c), d1);
+            float v0[kGroup], v1[kGroup];
+#pragma unroll
+            for (int c = 0; c < 128; c += 32) {
+                float a0[16], a1[16], b0[16], b1[16];
+                tc::tmem_ld16(lanebase + kColD + uint32_t(c), a0);
+                tc::tmem_ld16(lanebase + kColD + uint32_t(c + 16), a1);
+                tc::tmem_ld16(lanebase + kColD + 128 + uint32_t(c), b0);
+                tc::tmem_ld16(lanebase + kColD + 128 + uint32_t(c + 16), b1);
                 tc::wait_ld();
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int slot = (c >> 3) + h;
-                    float v0 = 0.0f, v1 = 0.0f;
+                    float g0 = 0.0f, g1 = 0.0f, u0 = 0.0f, u1 = 0.0f;
 #pragma unroll
                     for (int d = 0; d < kDigits; ++d) {
-                        v0 += d0[8 * h + d];
-                        v1 += d1[8 * h + d];
+                        g0 += a0[8 * h + d];
+                        g1 += a1[8 * h + d];
+                        u0 += b0[8 * h + d];
+                        u1 += b1[8 * h + d];
                     }
-                    if (row < kDim && slot < it.nvalid) {
-                        const size_t o = size_t(it.first + slot) * kDim + row;
-                        if (kGateUp) {
-                            w.hidden[o] = swiglu_ref(__fadd_rn(bias0, v0), __fadd_rn(bias1, v1));
-                        } else {
-                            w.down[o] = __fadd_rn(bias0, __fadd_rn(v0, v1));
-                        }
-                    }
+                    v0[(c >> 3) + h] = g0;
+                    v0[(c >> 3) + 2 + h] = g1;
+                    v1[(c >> 3) + h] = u0;
+                    v1[(c >> 3) + 2 + h] = u1;
                 }
             }
             tc::fence_before_sync();
             arrive(&s.acc_empty);
+            if (row < kDim) {
+#pragma unroll
+                for (int slot = 0; slot < kGroup; ++slot) {
+                    if (slot < it.nvalid) {
+                        const size_t o = size_t(it.first + slot) * kDim + row;
+                        if (kGateUp) {
+                            w.hidden[o] = swiglu_ref(__fadd_rn(bias0, v0[slot]), __fadd_rn(bias1, v1[slot]));
+                        } else {
+                            w.down[o] = __fadd_rn(bias0, __fadd_rn(v0[slot], v1[slot]));
+                        }
+                    }
+                }
+            }
         }
     }
     tc::fence_before_sync();
