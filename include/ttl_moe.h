@@ -118,7 +118,8 @@ int ttl_moe_forward(ttl_moe *handle, int layer_begin, int layer_end, const float
 
 /* Device-pointer forms of the three calls above: all pointers are device
  * memory of the handle's GPU; the work is enqueued on the handle's stream and
- * the call returns without waiting.  ttl_moe_sync() waits and reports. */
+ * the call returns without waiting.  ttl_moe_sync() waits and reports.
+ * Prefill's x must be 16-byte aligned (TTL_ERR_ARGUMENT otherwise). */
 int ttl_moe_decode_async(ttl_moe *handle, int layer, const float *x, float *out, int32_t *top4_idx,
                          float *top4_w);
 int ttl_moe_prefill_async(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out,

@@ -89,6 +89,30 @@ def test_decode_exact_ties_follow_reference_order(ttl):
         assert_close(out, r_out)
 
 
+def test_prefill_exact_ties_follow_reference_order(ttl):
+    """The prefill router's parallel ranking must hand exact ties to the
+    selection sort (src/model.cpp:344-357): tokens whose logits tie at the top,
+    mixed with tokens without ties."""
+    from test_oracle import tie_layer
+    from ttl_moe import synth
+    t = tie_layer()
+    x = synth.inputs_host(5, 6)
+    x[0] = 0.0
+    x[0, ::7] = 0.5
+    x[1] = 0.0
+    x[2] = 0.0
+    x[2, 1::5] = -0.25
+    x[4] = x[0]
+    with ttl.MoE(experts=32, layers=1, max_tokens=8, device=0) as m:
+        m.upload_layer(0, t)
+        out, idx, w = m.moe_batch(0, x)
+    r_out, r_idx, r_w = oracle.moe_prefill(t, x, impl=impl())
+    assert len({3, 9, 17} & set(r_idx[1])) >= 2
+    assert np.array_equal(idx, r_idx), (idx, r_idx)
+    np.testing.assert_allclose(w, r_w, rtol=1e-5, atol=0)
+    assert_close(out, r_out)
+
+
 @pytest.mark.parametrize("tokens", [1, 3, 17, 64])
 def test_prefill_matches_reference(moe32, layer32, tokens):
     from ttl_moe import synth

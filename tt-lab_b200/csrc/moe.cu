@@ -458,7 +458,7 @@ int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     launch_prefill_gateup(L, tma, h->pw, s, x, h->stream);
     launch_prefill_down(L, tma, h->pw, s, h->stream);
     launch_prefill_combine(h->pw, s, out, h->stream);
-    h->launches += 8;
+    h->launches += 7;
     TTL_TRY_CUDA(h, cudaGetLastError());
     if (h->cfg.world > 1) {
         return allreduce(h, out, tokens * kDim);
@@ -865,6 +865,9 @@ int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, 
     }
     if (!x || !out) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
+    }
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) {
+        return fail(h, TTL_ERR_ARGUMENT, "prefill input must be 16-byte aligned");
     }
     if (tokens == 0) {
         return fail(h, TTL_ERR_ARGUMENT, "prefill needs at least one token");  // src/model.cpp:464-466

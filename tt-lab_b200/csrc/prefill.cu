@@ -24,54 +24,35 @@
 namespace ttl {
 namespace {
 
-constexpr int kRouterTokens = 8;          // tokens per router CTA
-constexpr int kXRowStride = kDim + 4;     // padded shared row (bank spread)
-constexpr int kGroup = 16;                // slots per expert-product group
+constexpr int kRouterTokens = 4;                  // tokens per router CTA (one warp selects each)
+constexpr int kRouterChunk = 64;                  // columns per staged chunk
+constexpr int kRouterStages = 4;                  // chunks in flight
+constexpr int kRouterRow = kRouterChunk + 4;      // padded shared row, floats (bank spread)
+constexpr int kRouterChunks = kDim / kRouterChunk;  // 45
+constexpr int kGroup = 16;                        // slots per expert-product group
+static_assert(kDim % kRouterChunk == 0, "router chunks");
 
-__global__ void prefill_router_kernel(LayerDev L, PrefillWork w, int experts, int tokens,
-                                      const float *__restrict__ x) {
-    extern __shared__ float xs[];  // [kRouterTokens][kXRowStride]
-    const int t0 = blockIdx.x * kRouterTokens;
-    const int nt = min(kRouterTokens, tokens - t0);
-    for (int i = threadIdx.x; i < nt * kDim; i += blockDim.x) {
-        const int t = i / kDim;
-        const int c = i - t * kDim;
-        xs[t * kXRowStride + c] = x[size_t(t0 + t) * kDim + c];
-    }
-    __syncthreads();
-    const int e = threadIdx.x / kRouterTokens;
-    const int t = threadIdx.x % kRouterTokens;
-    if (e >= experts || t >= nt) {
-        return;
-    }
-    const float *wr = L.router_w + size_t(e) * kDim;
-    const float *xr = xs + t * kXRowStride;
-    float s = L.router_b[e];
-    for (int c = 0; c < kDim; c += 8) {
-        float p[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            p[j] = __fmul_rn(__ldg(wr + c + j), xr[c + j]);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            s = __fadd_rn(s, p[j]);
-        }
-    }
-    w.logits[size_t(t0 + t) * experts + e] = s;
+__host__ __device__ constexpr int router_threads(int experts) {
+    return (experts * kRouterTokens + 31) / 32 * 32 < 32 * kRouterTokens ? 32 * kRouterTokens
+                                                                       : (experts * kRouterTokens + 31) / 32 * 32;
+}
+__host__ __device__ constexpr size_t router_smem_bytes(int experts) {
+    return (size_t(kRouterStages) * (experts + kRouterTokens) * kRouterRow + size_t(kRouterTokens) * kMaxExperts) *
+               sizeof(float) +
+           size_t(kRouterTokens) * kTopK * sizeof(int);
 }
 
-__global__ void prefill_select_kernel(PrefillWork w, int experts, int tokens) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= tokens) {
-        return;
-    }
-    const float *r = w.logits + size_t(t) * experts;
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// The reference's selection sort (src/model.cpp:344-357): strict ">" over the
+// permuted order the swaps leave, so ties and NaNs resolve as it does.
+__device__ void select_sort_top4(const float *r, int experts, int idx[4]) {
     uint8_t order[kMaxExperts];
     for (int i = 0; i < experts; ++i) {
         order[i] = uint8_t(i);
     }
-    float sel[4];
     for (int i = 0; i < kTopK; ++i) {
         int best = i;
         for (int j = i + 1; j < experts; ++j) {
@@ -82,21 +63,158 @@ __global__ void prefill_select_kernel(PrefillWork w, int experts, int tokens) {
         const uint8_t tmp = order[i];
         order[i] = order[best];
         order[best] = tmp;
-        w.top_idx[t * 4 + i] = order[i];
-        sel[i] = r[order[i]];
+        idx[i] = order[i];
     }
+}
+
+// Router logits, top-4 and softmax for kRouterTokens tokens.  Thread (e, t)
+// runs the reference's sequential chain for one logit (bias first, f32
+// products rounded, added in column order), so logits -- and the indices --
+// equal the reference's bit for bit.  Router rows and token rows stream
+// through shared memory in 64-column chunks, kRouterStages in flight.
+// Then warp t ranks token t's logits (larger first, lower index among equal
+// values); when a NaN is present or a selected logit equals another expert's,
+// the selection sort itself decides.
+__global__ void prefill_router_kernel(LayerDev L, PrefillWork w, int experts, int tokens,
+                                      const float *__restrict__ x) {
+    extern __shared__ __align__(16) float rsm[];
+    float *wst = rsm;                                                    // [stage][experts][kRouterRow]
+    float *xst = wst + size_t(kRouterStages) * experts * kRouterRow;     // [stage][kRouterTokens][kRouterRow]
+    float *lg = xst + kRouterStages * kRouterTokens * kRouterRow;        // [kRouterTokens][kMaxExperts]
+    int *sel = reinterpret_cast<int *>(lg + kRouterTokens * kMaxExperts);  // [kRouterTokens][4]
+    const int t0 = blockIdx.x * kRouterTokens;
+    const int nt = min(kRouterTokens, tokens - t0);
+    const int tid = threadIdx.x;
+    const int per_chunk = (experts + nt) * (kRouterChunk / 4);
+
+    auto issue = [&](int chunk) {
+        const int st = chunk % kRouterStages;
+        const int c0 = chunk * kRouterChunk;
+        for (int i = tid; i < per_chunk; i += blockDim.x) {
+            const int row = i / (kRouterChunk / 4);
+            const int q = i - row * (kRouterChunk / 4);
+            const float *src;
+            float *dst;
+            if (row < experts) {
+                src = L.router_w + size_t(row) * kDim + c0 + 4 * q;
+                dst = wst + (size_t(st) * experts + row) * kRouterRow + 4 * q;
+            } else {
+                const int t = row - experts;
+                src = x + size_t(t0 + t) * kDim + c0 + 4 * q;
+                dst = xst + (st * kRouterTokens + t) * kRouterRow + 4 * q;
+            }
+            cp_async16(static_cast<uint32_t>(__cvta_generic_to_shared(dst)), src);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    const int t = tid % kRouterTokens;
+    const int e = tid / kRouterTokens;
+    const bool active = e < experts && t < nt;
+    float acc = active ? L.router_b[e] : 0.0f;
+#pragma unroll
+    for (int c = 0; c < kRouterStages - 1; ++c) {
+        issue(c);
+    }
+    for (int c = 0; c < kRouterChunks; ++c) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kRouterStages - 2) : "memory");
+        __syncthreads();
+        if (c + kRouterStages - 1 < kRouterChunks) {
+            issue(c + kRouterStages - 1);
+        } else {
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+        if (active) {
+            const int st = c % kRouterStages;
+            const float4 *wr = reinterpret_cast<const float4 *>(wst + (size_t(st) * experts + e) * kRouterRow);
+            const float4 *xr = reinterpret_cast<const float4 *>(xst + (st * kRouterTokens + t) * kRouterRow);
+#pragma unroll
+            for (int j = 0; j < kRouterChunk / 4; ++j) {
+                const float4 a = wr[j];
+                const float4 b = xr[j];
+                acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+                acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+                acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+                acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (active) {
+        lg[t * kMaxExperts + e] = acc;
+        w.logits[size_t(t0 + t) * experts + e] = acc;
+    }
+    __syncthreads();
+
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    if (warp >= nt) {
+        return;
+    }
+    const float *r = lg + warp * kMaxExperts;
+    float v[4];
+    int rank[4];
+    bool tie[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int ek = lane + 32 * k;
+        v[k] = ek < experts ? r[ek] : 0.0f;
+        rank[k] = 0;
+        tie[k] = false;
+    }
+    bool amb = false;
+    for (int j = 0; j < experts; ++j) {
+        const float u = r[j];
+        amb = amb | (u != u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int ek = lane + 32 * k;
+            rank[k] += ((u > v[k]) | ((u == v[k]) & (j < ek))) ? 1 : 0;
+            tie[k] = tie[k] | ((u == v[k]) & (j != ek));
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int ek = lane + 32 * k;
+        if (ek < experts && rank[k] < kTopK) {
+            sel[warp * kTopK + rank[k]] = ek;
+            amb = amb | tie[k];
+        }
+    }
+    amb = __any_sync(0xffffffffu, amb);
+    __syncwarp();
+    if (lane != 0) {
+        return;
+    }
+    int idx[4];
+    if (amb) {
+        select_sort_top4(r, experts, idx);
+    } else {
+#pragma unroll
+        for (int i = 0; i < kTopK; ++i) {
+            idx[i] = sel[warp * kTopK + i];
+        }
+    }
+    // softmax over the selected logits in rank order (src/model.cpp:358-378)
+    const int tok = t0 + warp;
+    float sv[4];
     float maximum = -INFINITY;
+#pragma unroll
     for (int i = 0; i < kTopK; ++i) {
-        maximum = (maximum < sel[i]) ? sel[i] : maximum;
+        sv[i] = r[idx[i]];
+        w.top_idx[tok * 4 + i] = idx[i];
+        maximum = (maximum < sv[i]) ? sv[i] : maximum;
     }
     float wt[4];
     float sum = 0.0f;
+#pragma unroll
     for (int i = 0; i < kTopK; ++i) {
-        wt[i] = expf(__fsub_rn(sel[i], maximum));
+        wt[i] = expf(__fsub_rn(sv[i], maximum));
         sum = __fadd_rn(sum, wt[i]);
     }
+#pragma unroll
     for (int i = 0; i < kTopK; ++i) {
-        w.top_w[t * 4 + i] = __fdiv_rn(wt[i], sum);
+        w.top_w[tok * 4 + i] = __fdiv_rn(wt[i], sum);
     }
 }
 
@@ -223,16 +341,14 @@ __global__ void prefill_combine_kernel(PrefillWork w, int tokens, float *__restr
 
 void configure_prefill_kernels() {
     cudaFuncSetAttribute(prefill_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kRouterTokens * kXRowStride * int(sizeof(float)));
+                         int(router_smem_bytes(kMaxExperts)));
 }
 
 void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,
                            cudaStream_t stream) {
     const int grid = (s.tokens + kRouterTokens - 1) / kRouterTokens;
-    const int threads = s.experts * kRouterTokens;
-    prefill_router_kernel<<<grid, threads, kRouterTokens * kXRowStride * sizeof(float), stream>>>(
+    prefill_router_kernel<<<grid, router_threads(s.experts), router_smem_bytes(s.experts), stream>>>(
         L, w, s.experts, s.tokens, x);
-    prefill_select_kernel<<<(s.tokens + 127) / 128, 128, 0, stream>>>(w, s.experts, s.tokens);
 }
 
 void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStream_t stream) {
