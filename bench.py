@@ -178,6 +178,62 @@ def run_reference(args, world, rank):
     return 0
 
 
+# Dense FP4 tensor-core peak of one B200 (nominal; MEASURED_PEAKS.json has no FP4 figure).
+FP4_PEAK_TFLOPS = 9000.0
+PREFILL_DIGITS = 8      # base-4 digit rows per activation (B operand of the prefill MMAs)
+PREFILL_GROUP = 16      # slots per expert group (N = 16 x 8 = 128 per MMA)
+
+
+def prefill_cfg2(torch, ttl_moe, synth, device, iters=20):
+    """one gpt-oss-20b layer, prefill T = 512, router
+    bias Zipf(1.1)-skewed.  Device time per layer (CUDA events on the library's
+    stream, 425 MB of experts per layer > L2), the host-buffer call end to end,
+    and the MXFP4 MMA work the grouped kernels execute."""
+    import numpy as np
+    T, E = 512, 32
+    with ttl_moe.MoE(experts=E, layers=1, max_tokens=T, device=device) as m:
+        m.upload_layer(0, synth.layer_device(2, 0, E, device="cuda", zipf_s=1.1))
+        xh = synth.inputs_host(2, T)
+        x = torch.from_numpy(xh).cuda()
+        out = torch.empty_like(x)
+        st = torch.cuda.ExternalStream(m.stream())
+        for _ in range(3):
+            m.prefill_async(0, x, T, out)
+        m.sync()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(iters):
+            m.prefill_async(0, x, T, out)
+        e1.record(st)
+        e1.synchronize()
+        m.sync()
+        ms = e0.elapsed_time(e1) / iters
+        _, idx, _ = m.moe_batch(0, xh)
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            m.moe_batch(0, xh)
+        e2e_ms = (time.perf_counter() - t0) / iters * 1e3
+    counts = np.bincount(np.asarray(idx).ravel(), minlength=E)
+    groups = int(sum((c + PREFILL_GROUP - 1) // PREFILL_GROUP for c in counts))
+    rows = (DIM + 127) // 128 * 128
+    mma_flop = 3 * groups * PREFILL_GROUP * PREFILL_DIGITS * rows * DIM * 2
+    useful_flop = 3 * T * 4 * DIM * DIM * 2
+    return {
+        "workload": "cfg2: gpt-oss-20b single MoE layer, prefill T=512, router bias Zipf(1.1)",
+        "ms_per_layer": ms,
+        "tokens_per_s": T / (ms * 1e-3),
+        "e2e": {"ms_per_layer": e2e_ms, "tokens_per_s": T / (e2e_ms * 1e-3),
+                "h2d_bytes_per_step": T * DIM * 4, "d2h_bytes_per_step": T * DIM * 4 + T * 4 * 8},
+        "expert_groups": groups,
+        "max_expert_pairs": int(counts.max()),
+        "mma_tflops": mma_flop / (ms * 1e-3) / 1e12,
+        "mma_frac_of_nominal_fp4": mma_flop / (ms * 1e-3) / 1e12 / FP4_PEAK_TFLOPS,
+        "reference_math_tflops": useful_flop / (ms * 1e-3) / 1e12,
+        "tensor_pipe_source": "profiles/prefill_mma_cfg2_T512.md (ncu sm__pipe_tensor_cycles_active)",
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -188,6 +244,7 @@ def main():
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     args = ap.parse_args()
 
     world, rank, local = dist_env()
@@ -294,8 +351,11 @@ def main():
         for ln in prof.read_text().splitlines():
             if ln.startswith("traffic_bytes_per_token_layer:"):
                 traffic = int(ln.split(":")[1]) * kms["steps"]
-    # numerical spot check of this run against the oracle (first token, layer 0)
-    ok_note = None
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        moe.close()
+        torch.cuda.empty_cache()
+        prefill = prefill_cfg2(torch, ttl_moe, synth, local)
 
     if rank == 0:
         cpu = None
@@ -349,6 +409,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tokens * DIM * 4,
                     "d2h_bytes_per_step": tokens * DIM * 4},
             "gpu_launches": launches,
+            "prefill": prefill,
         }
         print(json.dumps(line))
     moe.close()

@@ -104,8 +104,10 @@ int ttl_moe_decode(ttl_moe *handle, int layer, const float *x, float *out, int32
 
 /* Prefill MoE of `tokens` tokens: GptOssModel::moe_batch.
  * x, out: HOST f32 [tokens][2880]; idx/w: optional host [tokens][4].
- * tokens <= max_tokens.  With world > 1 each rank passes its own contiguous
- * share of the tokens.  Blocking. */
+ * tokens <= max_tokens.  With world > 1 every rank passes the same tokens,
+ * computes the pairs routed to its own experts, and the ranks' partial outputs
+ * are summed by an NCCL all-reduce, so every rank returns the full output.
+ * Blocking. */
 int ttl_moe_prefill(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
                     float *top4_w);
 

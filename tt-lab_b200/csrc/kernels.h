@@ -156,10 +156,11 @@ struct PrefillWork {
     int32_t *pair_slot;       // [T][4] slot of (token, rank), -1 if not local
     int32_t *tiles;           // [groups] work list: (expert << 20) | first slot of a 16-slot group
     int32_t *tile_count;      // [1] groups
-    float *hidden;            // [slots][2880] SwiGLU output per slot
     float *down;              // [slots][2880] down output per slot
-    uint8_t *bdig;            // [groups][96 K-blocks][16 slots][8 digit rows][16 B] MMA B operand
+    uint8_t *bdig;            // [groups][96 K-blocks][16 slots][8 digit rows][16 B] gate/up B operand (x)
     uint8_t *bsfb;            // [groups][24 chunks][512] its scale blocks (tcgen05.cp 32x128b order)
+    uint8_t *bdig_dn;         // the down B operand (SwiGLU output per slot), same layout, written by
+    uint8_t *bsfb_dn;         //   the gate/up epilogue, and its scale blocks
     uint32_t *status;
 };
 

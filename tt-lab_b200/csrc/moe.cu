@@ -458,7 +458,7 @@ int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     launch_prefill_gateup(L, tma, h->pw, s, x, h->stream);
     launch_prefill_down(L, tma, h->pw, s, h->stream);
     launch_prefill_combine(h->pw, s, out, h->stream);
-    h->launches += 7;
+    h->launches += 6;
     TTL_TRY_CUDA(h, cudaGetLastError());
     if (h->cfg.world > 1) {
         return allreduce(h, out, tokens * kDim);
@@ -630,10 +630,11 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.tiles, groups);
         rc = rc ? rc : alloc_n(h, &h->pw.tile_count, 1);
-        rc = rc ? rc : alloc_n(h, &h->pw.hidden, slots * kDim);
         rc = rc ? rc : alloc_n(h, &h->pw.down, slots * kDim);
         rc = rc ? rc : alloc_n(h, &h->pw.bdig, groups * kPrefillGroupBytes);
         rc = rc ? rc : alloc_n(h, &h->pw.bsfb, groups * kPrefillGroupScaleBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bdig_dn, groups * kPrefillGroupBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bsfb_dn, groups * kPrefillGroupScaleBytes);
         h->pw.status = h->d_status;
         if (rc) {
             return bail(rc);

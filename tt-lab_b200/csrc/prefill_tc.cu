@@ -17,13 +17,15 @@
 // slot's 8 digit columns.
 //
 //   prefill_split_kernel   one CTA per group: the B rows of the group (x of
-//                          each slot's token, or the slot's hidden row) and
-//                          their scale blocks, written once.
-//   prefill_gateup_kernel  persistent: item = (128-row tile, group); two MMA
-//                          issuers (gate, up) into two accumulators; the
-//                          epilogue applies the biases and SwiGLU and writes
-//                          the slots' hidden rows.
-//   prefill_down_kernel    persistent: item = (128-row tile, group); two
+//                          each slot's token) and their scale blocks, written
+//                          once.
+//   prefill_mma_kernel<1>  gate/up, persistent: item = (128-row tile, group);
+//                          two MMA issuers (gate, up) into two accumulators;
+//                          the epilogue applies the biases and SwiGLU, and
+//                          each of its warps -- 32 rows of the tile, which are
+//                          one K-block of the down product -- splits its
+//                          slots' values into the down B operand directly.
+//   prefill_mma_kernel<0>  down, persistent: item = (128-row tile, group); two
 //                          issuers take alternate stages into two
 //                          accumulators; the epilogue adds them and the bias.
 // Items run row-tile-major, so the groups of one expert read the same weight
@@ -90,9 +92,8 @@ __device__ __forceinline__ uint32_t digit_split8_store(float v, uint8_t *dst, in
 // One CTA per group: its B rows ([96 K-blocks][16 slots][8 rows][16 B]) and
 // the scale blocks of its 24 chunks of 4 K-blocks (row m = slot * 8 + digit
 // at [m % 32][m / 32][K-block % 4], the order tcgen05.cp 32x128b moves).
-// from_tokens: slot rows are x of the slot's token; else w.hidden rows.
-__global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork w, const float *__restrict__ x,
-                                                            bool from_tokens) {
+// Slot rows are x of the slot's token (zero for padding slots).
+__global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork w, const float *__restrict__ x) {
     __shared__ uint8_t codes[kGroup][kPadBlocks];
     const int g = blockIdx.x;
     if (g >= *w.tile_count) {
@@ -109,7 +110,7 @@ __global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork 
     const int slot = warp;
     const float *row = nullptr;
     if (slot < nvalid) {
-        row = from_tokens ? x + size_t(w.pair_token[first + slot]) * kDim : w.hidden + size_t(first + slot) * kDim;
+        row = x + size_t(w.pair_token[first + slot]) * kDim;
     }
     static_assert(kPadBlocks % 8 == 0, "K-blocks in batches of 8");
     for (int kb0 = 0; kb0 < kPadBlocks; kb0 += 8) {
@@ -234,8 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
             bool ok = true;
             for (int i = blockIdx.x; ok && i < items; i += gridDim.x) {
                 const Item it = item_of(w, i, groups);
-                const uint8_t *bg = w.bdig + size_t(it.g) * kPrefillGroupBytes;
-                const uint8_t *sg = w.bsfb + size_t(it.g) * kPrefillGroupScaleBytes;
+                const uint8_t *bg = (kGateUp ? w.bdig : w.bdig_dn) + size_t(it.g) * kPrefillGroupBytes;
+                const uint8_t *sg = (kGateUp ? w.bsfb : w.bsfb_dn) + size_t(it.g) * kPrefillGroupScaleBytes;
                 for (int k = 0; k < kBoxes; ++k, ++stage) {
                     const uint32_t st = stage % kStg;
                     const uint32_t use = stage / kStg;
@@ -375,16 +376,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
             }
             tc::fence_before_sync();
             arrive(&s.acc_empty);
-            if (row < kDim) {
+            if (kGateUp) {
+                // this warp's 32 rows are K-block 4 mt + warp of the down
+                // product: each slot's 32 values become its 8 digit rows there
+                // (zero for padding slots and rows past 2879), and lane j < 16
+                // keeps slot j's block code for the scale bytes
+                const int kb = 4 * it.mt + warp;
+                uint8_t *dg = w.bdig_dn + size_t(it.g) * kPrefillGroupBytes + size_t(kb) * kGroupKbBytes;
+                uint32_t mycode = 0;
+#pragma unroll
+                for (int slot = 0; slot < kGroup; ++slot) {
+                    float h = 0.0f;
+                    if (row < kDim && slot < it.nvalid) {
+                        h = swiglu_ref(__fadd_rn(bias0, v0[slot]), __fadd_rn(bias1, v1[slot]));
+                    }
+                    const uint32_t c = digit_split8_store(h, dg + slot * kDigits * 16, lane);
+                    mycode = (lane == slot) ? c : mycode;
+                }
+                // digit row m = slot * 8 + d of chunk mt at [m % 32][m / 32][kb % 4]
+                uint8_t *sf = w.bsfb_dn + size_t(it.g) * kPrefillGroupScaleBytes + size_t(it.mt) * kScaleBlockBytes;
+#pragma unroll
+                for (int q = lane; q < kGroup * kDigits; q += 32) {
+                    const uint32_t c = __shfl_sync(0xffffffffu, mycode, q >> 3);
+                    sf[(q & 31) * 16 + (q >> 5) * 4 + warp] = uint8_t(digit_scales8(c, q & 7));
+                }
+            } else if (row < kDim) {
 #pragma unroll
                 for (int slot = 0; slot < kGroup; ++slot) {
                     if (slot < it.nvalid) {
-                        const size_t o = size_t(it.first + slot) * kDim + row;
-                        if (kGateUp) {
-                            w.hidden[o] = swiglu_ref(__fadd_rn(bias0, v0[slot]), __fadd_rn(bias1, v1[slot]));
-                        } else {
-                            w.down[o] = __fadd_rn(bias0, __fadd_rn(v0[slot], v1[slot]));
-                        }
+                        w.down[size_t(it.first + slot) * kDim + row] = __fadd_rn(bias0, __fadd_rn(v0[slot], v1[slot]));
                     }
                 }
             }
@@ -411,14 +431,12 @@ void configure_prefill_tc() {
 void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
                            const float *x, cudaStream_t stream) {
     const int groups = int(prefill_groups(size_t(s.tokens), size_t(s.expert_count)));
-    prefill_split_kernel<<<groups, 512, 0, stream>>>(w, x, true);
+    prefill_split_kernel<<<groups, 512, 0, stream>>>(w, x);
     prefill_mma_kernel<true><<<s.sms, kThreads, sizeof(PSmem) + 1024, stream>>>(L, tma, w);
 }
 
 void launch_prefill_down(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
                          cudaStream_t stream) {
-    const int groups = int(prefill_groups(size_t(s.tokens), size_t(s.expert_count)));
-    prefill_split_kernel<<<groups, 512, 0, stream>>>(w, nullptr, false);
     prefill_mma_kernel<false><<<s.sms, kThreads, sizeof(PSmem) + 1024, stream>>>(L, tma, w);
 }
 
