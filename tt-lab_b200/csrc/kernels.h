@@ -156,6 +156,8 @@ struct PrefillWork {
     int32_t *pair_slot;       // [T][4] slot of (token, rank), -1 if not local
     int32_t *tiles;           // [groups] work list: (expert << 20) | first slot of a 16-slot group
     int32_t *tile_count;      // [1] groups
+    int32_t *dtiles;          // [groups] down work list: first group | (groups in the pair - 1) << 24,
+    int32_t *dtile_count;     //   pairs of consecutive groups of one expert; [1] its length
     float *down;              // [slots][2880] down output per slot
     uint8_t *bdig;            // [groups][96 K-blocks][16 slots][8 digit rows][16 B] gate/up B operand (x)
     uint8_t *bsfb;            // [groups][24 chunks][512] its scale blocks (tcgen05.cp 32x128b order)

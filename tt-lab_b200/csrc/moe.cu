@@ -630,6 +630,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.tiles, groups);
         rc = rc ? rc : alloc_n(h, &h->pw.tile_count, 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.dtiles, groups);
+        rc = rc ? rc : alloc_n(h, &h->pw.dtile_count, 1);
         rc = rc ? rc : alloc_n(h, &h->pw.down, slots * kDim);
         rc = rc ? rc : alloc_n(h, &h->pw.bdig, groups * kPrefillGroupBytes);
         rc = rc ? rc : alloc_n(h, &h->pw.bsfb, groups * kPrefillGroupScaleBytes);

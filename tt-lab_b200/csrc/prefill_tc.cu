@@ -25,9 +25,11 @@
 //                          each of its warps -- 32 rows of the tile, which are
 //                          one K-block of the down product -- splits its
 //                          slots' values into the down B operand directly.
-//   prefill_mma_kernel<0>  down, persistent: item = (128-row tile, group); two
-//                          issuers take alternate stages into two
-//                          accumulators; the epilogue adds them and the bias.
+//   prefill_mma_kernel<0>  down, persistent: item = (128-row tile, pair of
+//                          consecutive groups of one expert); the stage's
+//                          weight box is shared, issuer m multiplies it by
+//                          group m's B rows into accumulator m; the epilogue
+//                          adds the bias.
 // Items run row-tile-major, so the groups of one expert read the same weight
 // tile at about the same time (from L2 after the first).
 // Every wait is bounded; on timeout the kernels record kStatusWaitTimeout.
@@ -138,11 +140,13 @@ __global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork 
     }
 }
 
+// A stage holds three 16 KB operand tiles: gate/up -- the gate box, the up
+// box (swizzled) and the group's B rows of the box's 8 K-blocks; down -- the
+// down box and the B rows of the pair's two groups.
 struct alignas(1024) PSmem {
-    uint8_t a[kStg][2][128][128];                 // weight boxes (gate, up; or two down boxes), swizzled
-    uint8_t b[kStg][8][kGroupKbBytes];            // the group's B rows of the stage's 8 K-blocks
+    uint8_t t[kStg][3][16384];                    // operand tiles (weight boxes at 1024-byte boundaries)
     uint8_t sfa[kStg][2][2][kScaleBlockBytes];    // [box][chunk] weight scale blocks
-    uint8_t sfb[kStg][2][kScaleBlockBytes];       // [chunk] B scale blocks
+    uint8_t sfb[kStg][2][2][kScaleBlockBytes];    // [group][chunk] B scale blocks
     uint64_t full[kStg];
     uint64_t empty[kStg];
     uint64_t acc_full;
@@ -152,9 +156,9 @@ struct alignas(1024) PSmem {
     int go;
 };
 static_assert(sizeof(PSmem) + 1024 <= 232448, "shared memory per CTA");
-static_assert(offsetof(PSmem, a) % 1024 == 0 && offsetof(PSmem, b) % 16 == 0 && offsetof(PSmem, sfa) % 16 == 0 &&
-                  offsetof(PSmem, sfb) % 16 == 0,
+static_assert(offsetof(PSmem, t) % 1024 == 0 && offsetof(PSmem, sfa) % 16 == 0 && offsetof(PSmem, sfb) % 16 == 0,
               "copy destinations");
+static_assert(8 * kGroupKbBytes == 16384 && 128 * 128 == 16384, "operand tiles");
 
 __device__ __forceinline__ void bulk(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -171,19 +175,34 @@ __device__ __forceinline__ bool wait(uint64_t *bar, uint32_t parity, uint32_t *s
     return false;
 }
 
-// Item i of `items` (row tile mt, group g), row-tile-major.
+// Item i of `items` (row tile mt, unit u), row-tile-major.  A unit is one
+// group (gate/up) or an entry of the pair list (down): groups g .. g + n - 1.
 struct Item {
-    int mt, g, le, first, nvalid;
+    int mt, g, n, le;
 };
-__device__ __forceinline__ Item item_of(const PrefillWork &w, int i, int groups) {
+template <bool kGateUp>
+__device__ __forceinline__ Item item_of(const PrefillWork &w, int i, int units) {
     Item it;
-    it.mt = i / groups;
-    it.g = i - it.mt * groups;
-    const int code = w.tiles[it.g];
-    it.le = code >> 20;
-    it.first = code & 0xfffff;
-    it.nvalid = min(kGroup, w.offsets[it.le] + w.counts[it.le] - it.first);
+    it.mt = i / units;
+    const int u = i - it.mt * units;
+    if (kGateUp) {
+        it.g = u;
+        it.n = 1;
+    } else {
+        const int code = w.dtiles[u];
+        it.g = code & 0xffffff;
+        it.n = (code >> 24) + 1;
+    }
+    it.le = w.tiles[it.g] >> 20;
     return it;
+}
+
+// First slot and valid slots of group g.
+__device__ __forceinline__ int2 group_slots(const PrefillWork &w, int g) {
+    const int code = w.tiles[g];
+    const int le = code >> 20;
+    const int first = code & 0xfffff;
+    return make_int2(first, min(kGroup, w.offsets[le] + w.counts[le] - first));
 }
 
 // K-blocks of box x (8, or 2 for the last box).
@@ -195,24 +214,26 @@ __device__ __forceinline__ void arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(bar)) : "memory");
 }
 
-// Stage k of an item is weight box k (8 K-blocks) with the group's B rows and
-// scale blocks of those K-blocks.  Gate/up: the stage holds box k of gate
-// (a[st][0]) and of up (a[st][1]); issuer 0 multiplies gate, issuer 1 up,
-// each into its accumulator.  Down: the stage holds box k of down; issuer
-// k % 2 multiplies it into its accumulator and the epilogue adds the two.
+// Stage k of an item is weight box k (8 K-blocks) with the B rows and scale
+// blocks of those K-blocks.  Gate/up: the stage holds box k of gate (tile 0)
+// and of up (tile 1) and the group's B rows (tile 2); issuer 0 multiplies
+// gate, issuer 1 up, each into its accumulator.  Down: the stage holds box k
+// of down (tile 0) and the B rows of the pair's groups (tiles 1, 2); issuer m
+// multiplies the box by group m into accumulator m (idle when the pair has
+// one group).
 template <bool kGateUp>
 __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, const TmaDesc *tma, PrefillWork w) {
     extern __shared__ __align__(1024) unsigned char raw[];
     PSmem &s = *reinterpret_cast<PSmem *>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int groups = *w.tile_count;
-    const int items = kScaleTiles * groups;
+    const int units = kGateUp ? *w.tile_count : *w.dtile_count;
+    const int items = kScaleTiles * units;
     constexpr int kBoxA = kGateUp ? 2 : 1;  // weight boxes per stage
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStg; ++i) {
             tc::mbar_init(&s.full[i], 1);
-            tc::mbar_init(&s.empty[i], kGateUp ? 2 : 1);
+            tc::mbar_init(&s.empty[i], 2);
         }
         tc::mbar_init(&s.acc_full, 2);
         tc::mbar_init(&s.acc_empty, kEpiThreads);
@@ -234,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
             uint32_t stage = 0;
             bool ok = true;
             for (int i = blockIdx.x; ok && i < items; i += gridDim.x) {
-                const Item it = item_of(w, i, groups);
+                const Item it = item_of<kGateUp>(w, i, units);
                 const uint8_t *bg = (kGateUp ? w.bdig : w.bdig_dn) + size_t(it.g) * kPrefillGroupBytes;
                 const uint8_t *sg = (kGateUp ? w.bsfb : w.bsfb_dn) + size_t(it.g) * kPrefillGroupScaleBytes;
                 for (int k = 0; k < kBoxes; ++k, ++stage) {
@@ -246,17 +267,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
                     const int nchunk = (box_blocks(k) + 3) / 4;
                     // full boxes are counted even where they reach past the matrix (zero fill)
                     const uint32_t tx = uint32_t(kBoxA) * (128 * 128 + uint32_t(nchunk) * kScaleBlockBytes) +
-                                        8 * kGroupKbBytes + 2 * kScaleBlockBytes;
+                                        uint32_t(it.n) * (8 * kGroupKbBytes + 2 * kScaleBlockBytes);
                     tc::mbar_expect_tx(&s.full[st], tx);
                     for (int b = 0; b < kBoxA; ++b) {
                         const int map = kGateUp ? (b == 0 ? kTmaGate : kTmaUp) : kTmaDown;
                         const uint8_t *mat = kGateUp ? (b == 0 ? L.gate : L.up) : L.down;
-                        tc::tma_load_3d(&s.a[st][b][0][0], tma + map, 128 * k, 128 * it.mt, it.le, &s.full[st]);
+                        tc::tma_load_3d(&s.t[st][b][0], tma + map, 128 * k, 128 * it.mt, it.le, &s.full[st]);
                         bulk(&s.sfa[st][b][0][0], mat + size_t(it.le) * kPackedMatrixBytes + scale_block_offset(it.mt, 2 * k),
                              uint32_t(nchunk) * kScaleBlockBytes, &s.full[st]);
                     }
-                    bulk(&s.b[st][0][0], bg + size_t(8 * k) * kGroupKbBytes, 8 * kGroupKbBytes, &s.full[st]);
-                    bulk(&s.sfb[st][0][0], sg + size_t(2 * k) * kScaleBlockBytes, 2 * kScaleBlockBytes, &s.full[st]);
+                    for (int j = 0; j < it.n; ++j) {
+                        bulk(&s.t[st][kBoxA + j][0], bg + size_t(j) * kPrefillGroupBytes + size_t(8 * k) * kGroupKbBytes,
+                             8 * kGroupKbBytes, &s.full[st]);
+                        bulk(&s.sfb[st][j][0][0],
+                             sg + size_t(j) * kPrefillGroupScaleBytes + size_t(2 * k) * kScaleBlockBytes,
+                             2 * kScaleBlockBytes, &s.full[st]);
+                    }
                 }
             }
             // every load issued has landed before the CTA exits
@@ -268,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
     } else if (warp >= kIssuerWarp0 && warp < kIssuerWarp0 + 2) {
         if (lane == 0) {
             const int m = warp - kIssuerWarp0;
-            const uint32_t a0 = tc::smem_u32(&s.a[0][0][0][0]);
+            const uint32_t t0 = tc::smem_u32(&s.t[0][0][0]);
             const uint32_t dcol = tbase + kColD + 128 * uint32_t(m);
             uint32_t stage = 0;
             uint32_t item_no = 0;
@@ -278,27 +304,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
                     break;
                 }
                 tc::fence_after_sync();
+                // down: issuer 1 idles (but still releases the stages) for a one-group pair
+                const bool active = kGateUp || m < item_of<kGateUp>(w, i, units).n;
                 bool first = true;
                 for (int k = 0; k < kBoxes; ++k, ++stage) {
-                    if (!kGateUp && (k & 1) != m) {
-                        continue;  // the other issuer's stage
-                    }
                     const uint32_t st = stage % kStg;
                     if (!(ok = wait(&s.full[st], (stage / kStg) & 1, w.status))) {
                         break;
                     }
                     tc::fence_after_sync();
+                    if (!active) {
+                        tc::mma_commit(&s.empty[st]);
+                        continue;
+                    }
                     const int box = kGateUp ? m : 0;
+                    const int grp = kGateUp ? 0 : m;
                     const int nkb = box_blocks(k);
                     const int nchunk = (nkb + 3) / 4;
                     const uint32_t sfa_col = tbase + kColSfa + 16 * st + 8 * uint32_t(m);
                     const uint32_t sfb_col = tbase + kColSfb + 16 * st + 8 * uint32_t(m);
                     for (int j = 0; j < nchunk; ++j) {
                         tc::sf_copy(sfa_col + 4 * j, tc::smem_u32(&s.sfa[st][box][j][0]));
-                        tc::sf_copy(sfb_col + 4 * j, tc::smem_u32(&s.sfb[st][j][0]));
+                        tc::sf_copy(sfb_col + 4 * j, tc::smem_u32(&s.sfb[st][grp][j][0]));
                     }
-                    const uint32_t abase = a0 + st * uint32_t(sizeof(s.a[0])) + uint32_t(box) * 16384u;
-                    const uint32_t bbase = tc::smem_u32(&s.b[st][0][0]);
+                    const uint32_t abase = t0 + st * uint32_t(sizeof(s.t[0])) + uint32_t(box) * 16384u;
+                    const uint32_t bbase = t0 + st * uint32_t(sizeof(s.t[0])) + uint32_t(kBoxA + grp) * 16384u;
                     for (int p = 0; 2 * p < nkb; ++p) {
                         const uint32_t sel = uint32_t((2 * p) & 3);
                         const uint32_t j = uint32_t(p >> 1);
@@ -324,7 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
         const int i = threadIdx.x;
         uint32_t item_no = 0;
         for (int ii = blockIdx.x; ii < items; ii += gridDim.x, ++item_no) {
-            const Item it = item_of(w, ii, groups);
+            const Item it = item_of<kGateUp>(w, ii, units);
+            const int2 gs0 = group_slots(w, it.g);
             const int row = 128 * it.mt + i;
             float bias0 = 0.0f, bias1 = 0.0f;
             if (row < kDim) {
@@ -387,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
 #pragma unroll
                 for (int slot = 0; slot < kGroup; ++slot) {
                     float h = 0.0f;
-                    if (row < kDim && slot < it.nvalid) {
+                    if (row < kDim && slot < gs0.y) {
                         h = swiglu_ref(__fadd_rn(bias0, v0[slot]), __fadd_rn(bias1, v1[slot]));
                     }
                     const uint32_t c = digit_split8_store(h, dg + slot * kDigits * 16, lane);
@@ -401,10 +432,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_mma_kernel(LayerDev L, co
                     sf[(q & 31) * 16 + (q >> 5) * 4 + warp] = uint8_t(digit_scales8(c, q & 7));
                 }
             } else if (row < kDim) {
+                const int2 gs1 = it.n > 1 ? group_slots(w, it.g + 1) : make_int2(0, 0);
 #pragma unroll
                 for (int slot = 0; slot < kGroup; ++slot) {
-                    if (slot < it.nvalid) {
-                        w.down[size_t(it.first + slot) * kDim + row] = __fadd_rn(bias0, __fadd_rn(v0[slot], v1[slot]));
+                    if (slot < gs0.y) {
+                        w.down[size_t(gs0.x + slot) * kDim + row] = __fadd_rn(bias0, v0[slot]);
+                    }
+                    if (slot < gs1.y) {
+                        w.down[size_t(gs1.x + slot) * kDim + row] = __fadd_rn(bias0, v1[slot]);
                     }
                 }
             }
