@@ -156,11 +156,11 @@ struct PrefillWork {
     int32_t *pair_slot;       // [T][4] slot of (token, rank), -1 if not local
     int32_t *tiles;           // [groups] work list: (expert << 20) | first slot of a 16-slot group
     int32_t *tile_count;      // [1] groups
-    int32_t *dtiles;          // [groups] down work list: first group | (groups in the pair - 1) << 24,
-    int32_t *dtile_count;     //   pairs of consecutive groups of one expert; [1] its length
+    int32_t *units;           // [groups] expert-product work list: first group | (groups - 1) << 24, a
+    int32_t *unit_count;      //   unit being one or two consecutive groups of one expert; [1] its length
     float *down;              // [slots][2880] down output per slot
-    uint8_t *bdig;            // [groups][96 K-blocks][16 slots][8 digit rows][16 B] gate/up B operand (x)
-    uint8_t *bsfb;            // [groups][24 chunks][512] its scale blocks (tcgen05.cp 32x128b order)
+    uint8_t *bdig;            // [units][96 K-blocks][192 rows][16 B] gate/up B operand (digit rows of x)
+    uint8_t *bsfb;            // [units][24 chunks][2][512] its scale blocks (tcgen05.cp 32x128b order)
     uint8_t *bdig_dn;         // the down B operand (SwiGLU output per slot), same layout, written by
     uint8_t *bsfb_dn;         //   the gate/up epilogue, and its scale blocks
     uint32_t *status;
@@ -181,12 +181,18 @@ void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillW
                            const float *x, cudaStream_t stream);
 void launch_prefill_down(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
                          cudaStream_t stream);
-// Slots and groups of a prefill of `tokens` tokens over `experts` local experts (capacity).
+// Groups and units of a prefill of `tokens` tokens over `experts` local
+// experts (capacity): groups <= 4T/16 + E, units <= 4T/32 + E.
 constexpr size_t prefill_groups(size_t tokens, size_t experts) {
     return (4 * tokens) / 16 + experts + 1;
 }
-constexpr size_t kPrefillGroupBytes = size_t(96) * 16 * 128;
-constexpr size_t kPrefillGroupScaleBytes = size_t(24) * 512;
+constexpr size_t prefill_units(size_t tokens, size_t experts) {
+    return tokens / 8 + experts + 1;
+}
+// Per unit: [96 K-blocks][2 groups x 16 slots x 6 digit rows][16 B] and
+// [24 chunks][2 blocks (rows 0-127, 128-191)][512 B].
+constexpr size_t kPrefillUnitBytes = size_t(96) * 192 * 16;
+constexpr size_t kPrefillUnitScaleBytes = size_t(24) * 2 * 512;
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream);
 
 } // namespace ttl

@@ -630,13 +630,14 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.tiles, groups);
         rc = rc ? rc : alloc_n(h, &h->pw.tile_count, 1);
-        rc = rc ? rc : alloc_n(h, &h->pw.dtiles, groups);
-        rc = rc ? rc : alloc_n(h, &h->pw.dtile_count, 1);
+        rc = rc ? rc : alloc_n(h, &h->pw.units, groups);
+        rc = rc ? rc : alloc_n(h, &h->pw.unit_count, 1);
         rc = rc ? rc : alloc_n(h, &h->pw.down, slots * kDim);
-        rc = rc ? rc : alloc_n(h, &h->pw.bdig, groups * kPrefillGroupBytes);
-        rc = rc ? rc : alloc_n(h, &h->pw.bsfb, groups * kPrefillGroupScaleBytes);
-        rc = rc ? rc : alloc_n(h, &h->pw.bdig_dn, groups * kPrefillGroupBytes);
-        rc = rc ? rc : alloc_n(h, &h->pw.bsfb_dn, groups * kPrefillGroupScaleBytes);
+        const size_t units = prefill_units(T, size_t(h->expert_count));
+        rc = rc ? rc : alloc_n(h, &h->pw.bdig, units * kPrefillUnitBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bsfb, units * kPrefillUnitScaleBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bdig_dn, units * kPrefillUnitBytes);
+        rc = rc ? rc : alloc_n(h, &h->pw.bsfb_dn, units * kPrefillUnitScaleBytes);
         h->pw.status = h->d_status;
         if (rc) {
             return bail(rc);

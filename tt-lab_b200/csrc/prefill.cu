@@ -243,14 +243,14 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
     if (threadIdx.x == 0) {
         int run = 0;
         int tiles = 0;
-        int dtiles = 0;
+        int units = 0;
         for (int le = 0; le < expert_count; ++le) {
             offsets[le] = run;
             w.counts[le] = counts[le];
             w.offsets[le] = run;
             const int n = (counts[le] + kGroup - 1) / kGroup;
             for (int j = 0; j < n; j += 2) {
-                w.dtiles[dtiles++] = (tiles + j) | (min(2, n - j) - 1) << 24;
+                w.units[units++] = (tiles + j) | (min(2, n - j) - 1) << 24;
             }
             for (int k = 0; k < counts[le]; k += kGroup) {
                 w.tiles[tiles++] = (le << 20) | (run + k);
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
         offsets[expert_count] = run;
         w.offsets[expert_count] = run;
         *w.tile_count = tiles;
-        *w.dtile_count = dtiles;
+        *w.unit_count = units;
     }
     __syncthreads();
     // padding slots of each expert's last group
