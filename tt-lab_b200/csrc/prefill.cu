@@ -218,83 +218,103 @@ __global__ void prefill_router_kernel(LayerDev L, PrefillWork w, int experts, in
     }
 }
 
-// One CTA: histogram, offsets, stable buckets and the tile work list.
+// One CTA per local expert le (src/model.cpp:380-394): every CTA counts the
+// routed pairs of all local experts (the same counts in every CTA), takes
+// le's first slot, first group and first unit from the counts of the experts
+// before it, writes le's groups, units and padding slots, and places le's
+// pairs in its slots in token order (a block-wide scan over the tokens).
+// CTA 0 also writes the totals and marks pairs of experts that are not local.
 __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int experts, int expert_begin,
                                                              int expert_count, int tokens) {
     __shared__ int counts[kMaxExperts];
-    __shared__ int offsets[kMaxExperts + 1];
-    for (int e = threadIdx.x; e < experts; e += blockDim.x) {
+    __shared__ int warp_total[32];
+    __shared__ int first[3];  // le's first slot, group and unit
+    const int le = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    for (int e = threadIdx.x; e < expert_count; e += blockDim.x) {
         counts[e] = 0;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < tokens * kTopK; i += blockDim.x) {
-        w.pair_slot[i] = -1;
         const int e = w.top_idx[i];
+        const int l = e - expert_begin;
         if (e < 0 || e >= experts) {
-            set_status(w.status, kStatusBadExpert);
-            continue;
-        }
-        const int le = e - expert_begin;
-        if (le >= 0 && le < expert_count) {
-            atomicAdd(&counts[le], 1);
+            if (le == 0) {
+                set_status(w.status, kStatusBadExpert);
+                w.pair_slot[i] = -1;
+            }
+        } else if (l >= 0 && l < expert_count) {
+            atomicAdd(&counts[l], 1);
+        } else if (le == 0) {
+            w.pair_slot[i] = -1;
         }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int run = 0;
-        int tiles = 0;
-        int units = 0;
-        for (int le = 0; le < expert_count; ++le) {
-            offsets[le] = run;
-            w.counts[le] = counts[le];
-            w.offsets[le] = run;
-            const int n = (counts[le] + kGroup - 1) / kGroup;
-            for (int j = 0; j < n; j += 2) {
-                w.units[units++] = (tiles + j) | (min(2, n - j) - 1) << 24;
+        int run = 0, groups = 0, units = 0;
+        for (int l = 0; l < expert_count; ++l) {
+            if (l == le) {
+                first[0] = run;
+                first[1] = groups;
+                first[2] = units;
             }
-            for (int k = 0; k < counts[le]; k += kGroup) {
-                w.tiles[tiles++] = (le << 20) | (run + k);
-            }
+            const int n = (counts[l] + kGroup - 1) / kGroup;
             run += n * kGroup;
+            groups += n;
+            units += (n + 1) / 2;
         }
-        offsets[expert_count] = run;
-        w.offsets[expert_count] = run;
-        *w.tile_count = tiles;
-        *w.unit_count = units;
+        if (le == 0) {
+            w.offsets[expert_count] = run;
+            *w.tile_count = groups;
+            *w.unit_count = units;
+        }
     }
     __syncthreads();
-    // padding slots of each expert's last group
-    for (int le = threadIdx.x; le < expert_count; le += blockDim.x) {
-        for (int sl = offsets[le] + counts[le]; sl < offsets[le + 1]; ++sl) {
-            w.pair_token[sl] = -1;
+    const int count = counts[le];
+    const int n = (count + kGroup - 1) / kGroup;
+    const int slot0 = first[0];
+    if (threadIdx.x == 0) {
+        w.counts[le] = count;
+        w.offsets[le] = slot0;
+    }
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        w.tiles[first[1] + k] = (le << 20) | (slot0 + k * kGroup);
+        if ((k & 1) == 0) {
+            w.units[first[2] + k / 2] = (first[1] + k) | (min(2, n - k) - 1) << 24;
         }
     }
-    // Stable placement: each warp owns experts; tokens are scanned in order.
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int nwarps = blockDim.x >> 5;
-    for (int le = warp; le < expert_count; le += nwarps) {
-        const int e = le + expert_begin;
-        int base = offsets[le];
-        for (int t0 = 0; t0 < tokens; t0 += 32) {
-            const int t = t0 + lane;
-            int rank = -1;
-            if (t < tokens) {
-#pragma unroll
-                for (int r = 0; r < kTopK; ++r) {
-                    if (w.top_idx[t * 4 + r] == e) {
-                        rank = r;
-                    }
-                }
-            }
-            const unsigned ballot = __ballot_sync(0xffffffffu, rank >= 0);
-            if (rank >= 0) {
-                const int pos = base + __popc(ballot & ((1u << lane) - 1u));
-                w.pair_token[pos] = t;
-                w.pair_slot[t * 4 + rank] = pos;
-            }
-            base += __popc(ballot);
+    for (int sl = slot0 + count + threadIdx.x; sl < slot0 + n * kGroup; sl += blockDim.x) {
+        w.pair_token[sl] = -1;  // padding slots of the last group
+    }
+    // stable placement: token order within the expert
+    const int e = le + expert_begin;
+    int base = slot0;
+    for (int t0 = 0; t0 < tokens; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        int rank = -1;
+        if (t < tokens) {
+            const int4 q = *reinterpret_cast<const int4 *>(w.top_idx + size_t(t) * 4);
+            rank = q.x == e ? 0 : q.y == e ? 1 : q.z == e ? 2 : q.w == e ? 3 : -1;
         }
+        const unsigned ballot = __ballot_sync(0xffffffffu, rank >= 0);
+        if (lane == 0) {
+            warp_total[warp] = __popc(ballot);
+        }
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int k = 0; k < int(blockDim.x >> 5); ++k) {
+            const int c = warp_total[k];
+            before += k < warp ? c : 0;
+            total += c;
+        }
+        if (rank >= 0) {
+            const int pos = base + before + __popc(ballot & ((1u << lane) - 1u));
+            w.pair_token[pos] = t;
+            w.pair_slot[t * 4 + rank] = pos;
+        }
+        base += total;
+        __syncthreads();
     }
 }
 
@@ -358,7 +378,8 @@ void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const Prefil
 }
 
 void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStream_t stream) {
-    prefill_route_kernel<<<1, 1024, 0, stream>>>(w, s.experts, s.expert_begin, s.expert_count, s.tokens);
+    prefill_route_kernel<<<s.expert_count, 1024, 0, stream>>>(w, s.experts, s.expert_begin, s.expert_count,
+                                                               s.tokens);
 }
 
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream) {

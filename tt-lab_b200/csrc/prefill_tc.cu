@@ -18,8 +18,9 @@
 // groups N = 192.  The digits are exact to 2^-16 of each K-block's largest
 // value; the epilogue adds a slot's 6 digit columns.
 //
-//   prefill_split_kernel   one CTA per (unit, group): the B rows of its slots
-//                          (x of each slot's token) and their scale bytes.
+//   prefill_split_kernel   one CTA per (unit, group, quarter of K): the B rows
+//                          of its slots (x of each slot's token) and their
+//                          scale bytes.
 //   prefill_mma_kernel<1>  gate/up, persistent: item = (128-row tile, unit);
 //                          two MMA issuers (gate, up) into two N <= 192
 //                          accumulators; eight epilogue warps (four per group
@@ -137,15 +138,18 @@ __device__ __forceinline__ int unit_scale_offset(int m, int kb) {
     return (kb >> 2) * 1024 + (m >> 7) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (kb & 3);
 }
 
-// One CTA per (unit, group j), warp w = slot w: the group's B rows of the
-// unit ([96 K-blocks][192 rows][16 B], row = j * 96 + slot * 6 + digit; slots
-// past the group's end are zero rows) and their scale bytes in the unit's 24
-// chunks.  A one-group unit's second group is left unwritten: its products
+// One CTA per (unit, group j, quarter h of the K-blocks), warp w = slot w:
+// the group's B rows of the unit ([96 K-blocks][192 rows][16 B], row =
+// j * 96 + slot * 6 + digit; slots past the group's end are zero rows) for
+// K-blocks 24 h .. 24 h + 23, and their scale bytes (6 of the unit's 24
+// chunks).  A one-group unit's second group is left unwritten: its products
 // use N = 96 and never read those rows.
+constexpr int kSplitBlocks = kPadBlocks / 4;  // K-blocks per split CTA
 __global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork w, const float *__restrict__ x) {
-    __shared__ __align__(4) uint8_t codes[kGroup][kPadBlocks];
-    const int u = blockIdx.x >> 1;
-    const int j = blockIdx.x & 1;
+    __shared__ __align__(4) uint8_t codes[kGroup][kSplitBlocks];
+    const int u = blockIdx.x >> 3;
+    const int j = (blockIdx.x >> 2) & 1;
+    const int kb_first = (blockIdx.x & 3) * kSplitBlocks;
     if (u >= *w.unit_count) {
         return;
     }
@@ -159,30 +163,31 @@ __global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork 
     const int2 gs = group_slots(w, ug.x + j);
     const float *row = slot < gs.y ? x + size_t(w.pair_token[gs.x + slot]) * kDim : nullptr;
     uint8_t *dst = w.bdig + size_t(u) * kPrefillUnitBytes + (j * kGroupRows + slot * kDigits) * 16;
-    static_assert(kPadBlocks % 8 == 0, "K-blocks in batches of 8");
-    for (int kb0 = 0; kb0 < kPadBlocks; kb0 += 8) {
+    static_assert(kSplitBlocks % 8 == 0, "K-blocks in batches of 8");
+    for (int k0 = 0; k0 < kSplitBlocks; k0 += 8) {
         float v[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            v[q] = (row && kb0 + q < kBlocks) ? __ldcg(row + (kb0 + q) * 32 + lane) : 0.0f;
+            const int kb = kb_first + k0 + q;
+            v[q] = (row && kb < kBlocks) ? __ldcg(row + kb * 32 + lane) : 0.0f;
         }
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            const int kb = kb0 + q;
+            const int kb = kb_first + k0 + q;
             const uint32_t c = digit_split6_store(v[q], dst + size_t(kb) * kUnitKbBytes, lane);
             if (lane == 0) {
-                codes[warp][kb] = uint8_t(c);
+                codes[slot][k0 + q] = uint8_t(c);
             }
         }
     }
     __syncthreads();
     // one word per (chunk, row): the row's scale bytes of the chunk's 4 K-blocks
     uint8_t *sfb = w.bsfb + size_t(u) * kPrefillUnitScaleBytes;
-    for (int idx = threadIdx.x; idx < 24 * kGroupRows; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < (kSplitBlocks / 4) * kGroupRows; idx += blockDim.x) {
         const int chunk = idx / kGroupRows;
         const int r = idx - chunk * kGroupRows;
         const int s = r / kDigits;
-        *reinterpret_cast<uint32_t *>(sfb + unit_scale_offset(j * kGroupRows + r, 4 * chunk)) =
+        *reinterpret_cast<uint32_t *>(sfb + unit_scale_offset(j * kGroupRows + r, kb_first + 4 * chunk)) =
             digit_scales6(*reinterpret_cast<const uint32_t *>(&codes[s][4 * chunk]), r - s * kDigits);
     }
 }
@@ -520,7 +525,7 @@ void configure_prefill_tc() {
 void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
                            const float *x, cudaStream_t stream) {
     const int units = int(prefill_units(size_t(s.tokens), size_t(s.expert_count)));
-    prefill_split_kernel<<<2 * units, 32 * kGroup, 0, stream>>>(w, x);
+    prefill_split_kernel<<<8 * units, 32 * kGroup, 0, stream>>>(w, x);
     prefill_mma_kernel<true><<<s.sms, kThreads, sizeof(PSmem<true>) + 1024, stream>>>(L, tma, w);
 }
 
