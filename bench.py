@@ -7,6 +7,10 @@ sequential tokens; per token and layer h = RMSNorm(x), x = x + MoE(h)
 MXFP4 (csrc/synth.h), 10.2 GB of experts resident in HBM, so every token streams
 1.28 GB and no step can be served from the 126 MB L2.
 
+The line also carries "prefill": BASELINE.json configs[2] (one gpt-oss-20b
+layer, T = 512, Zipf(1.1)-skewed routing) through the same library, timed with
+CUDA events; --prefill-only runs just that part.
+
 Arms
   default            libttl_moe through its C ABI (this repo's kernels).
   --impl reference   tt-lab's own CPU MoE (GptOssModel::moe, compiled from its
@@ -180,15 +184,37 @@ def run_reference(args, world, rank):
 
 # Dense FP4 tensor-core peak of one B200 (nominal; MEASURED_PEAKS.json has no FP4 figure).
 FP4_PEAK_TFLOPS = 9000.0
-PREFILL_DIGITS = 8      # base-4 digit rows per activation (B operand of the prefill MMAs)
-PREFILL_GROUP = 16      # slots per expert group (N = 16 x 8 = 128 per MMA)
+PREFILL_DIGITS = 6      # radix-8 digit rows per activation (B operand of the prefill MMAs)
+PREFILL_GROUP = 16      # slots per expert group (N = 16 x 6 = 96 per group)
 
 
-def prefill_cfg2(torch, ttl_moe, synth, device, iters=20):
+def cpu_prefill_sample(seconds, seed=2, experts=32):
+    """tt-lab's own GptOssModel::moe_batch (oracle/_ref, 1 thread) on the cfg2
+    layer, on a bounded prefix of the cfg2 tokens sized to take about
+    `seconds`.  Returns (tokens per second, tokens, elapsed, isa)."""
+    import oracle
+    from ttl_moe import synth
+    t = synth.layer_host(seed, 0, experts, zipf_s=1.1)
+    x = synth.inputs_host(seed, 512)
+    oracle.moe_prefill(t, x[:4], impl="ref")  # page-in
+    t0 = time.perf_counter()
+    oracle.moe_prefill(t, x[:8], impl="ref")
+    per_token = (time.perf_counter() - t0) / 8
+    n = int(min(512, max(8, seconds / max(per_token, 1e-6))))
+    t0 = time.perf_counter()
+    oracle.moe_prefill(t, x[:n], impl="ref")
+    el = time.perf_counter() - t0
+    R = oracle.ref()
+    return n / el, n, el, ("x86-64-v4" if R.tref_isa_v4() else "default")
+
+
+def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
     """one gpt-oss-20b layer, prefill T = 512, router
     bias Zipf(1.1)-skewed.  Device time per layer (CUDA events on the library's
     stream, 425 MB of experts per layer > L2), the host-buffer call end to end,
-    and the MXFP4 MMA work the grouped kernels execute."""
+    and the MXFP4 MMA work the grouped kernels execute.  The end-to-end figure
+    is the host-buffer call (ttl_moe_prefill) on pinned buffers: H2D of x, the
+    kernels, D2H of the output and the top-4 indices and weights."""
     import numpy as np
     T, E = 512, 32
     with ttl_moe.MoE(experts=E, layers=1, max_tokens=T, device=device) as m:
@@ -210,10 +236,23 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20):
         m.sync()
         ms = e0.elapsed_time(e1) / iters
         _, idx, _ = m.moe_batch(0, xh)
+        x_pin = torch.from_numpy(xh).pin_memory()
+        o_pin = torch.empty_like(x_pin).pin_memory()
+        i_pin = torch.empty((T, 4), dtype=torch.int32).pin_memory()
+        w_pin = torch.empty((T, 4), dtype=torch.float32).pin_memory()
+        m.prefill_host(0, x_pin, T, o_pin, i_pin, w_pin)
         t0 = time.perf_counter()
         for _ in range(iters):
-            m.moe_batch(0, xh)
+            m.prefill_host(0, x_pin, T, o_pin, i_pin, w_pin)
         e2e_ms = (time.perf_counter() - t0) / iters * 1e3
+    cpu = None
+    if cpu_seconds > 0:
+        try:
+            rate, n, el, isa = cpu_prefill_sample(cpu_seconds)
+            cpu = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                   "sample": f"GptOssModel::moe_batch on the first {n} cfg2 tokens ({el:.1f}s, 1 thread, {isa} clone)"}
+        except Exception as e:  # the reference build is optional on the box
+            cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
     counts = np.bincount(np.asarray(idx).ravel(), minlength=E)
     groups = int(sum((c + PREFILL_GROUP - 1) // PREFILL_GROUP for c in counts))
     rows = (DIM + 127) // 128 * 128
@@ -231,6 +270,7 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20):
         "mma_frac_of_nominal_fp4": mma_flop / (ms * 1e-3) / 1e12 / FP4_PEAK_TFLOPS,
         "reference_math_tflops": useful_flop / (ms * 1e-3) / 1e12,
         "tensor_pipe_source": "profiles/prefill_mma_cfg2_T512.md (ncu sm__pipe_tensor_cycles_active)",
+        "cpu_baseline": cpu,
     }
 
 
@@ -245,6 +285,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the cfg2 prefill measurement (one JSON line with its figures)")
     args = ap.parse_args()
 
     world, rank, local = dist_env()
@@ -257,6 +299,13 @@ def main():
     from ttl_moe import parallel, synth
 
     torch.cuda.set_device(local)
+    if args.prefill_only:
+        if rank == 0:
+            pf = prefill_cfg2(torch, ttl_moe, synth, local, iters=max(1, args.steps),
+                              cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
+            print(json.dumps({"metric": "MoE prefill tokens/s (gpt-oss-20b layer, T=512)", "value": pf["tokens_per_s"],
+                              "unit": "tokens/s", "n_gpus": 1, "higher_is_better": True, "prefill": pf}))
+        return 0
     dist = None
     if world > 1:
         import datetime
@@ -355,7 +404,8 @@ def main():
     if world == 1 and not args.no_prefill:
         moe.close()
         torch.cuda.empty_cache()
-        prefill = prefill_cfg2(torch, ttl_moe, synth, local)
+        prefill = prefill_cfg2(torch, ttl_moe, synth, local,
+                               cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
 
     if rank == 0:
         cpu = None

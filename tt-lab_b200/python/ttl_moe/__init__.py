@@ -216,6 +216,10 @@ class MoE:
     def forward_async(self, begin, end, x, y, tokens):
         self._check(lib().ttl_moe_forward_async(self.h, begin, end, _ptr(x), _ptr(y), tokens))
 
+    def prefill_host(self, layer, x, tokens, out, idx=None, w=None):
+        """ttl_moe_prefill on caller-owned host buffers (pinned or pageable)."""
+        self._check(lib().ttl_moe_prefill(self.h, layer, _ptr(x), tokens, _ptr(out), _ptr(idx), _ptr(w)))
+
     def forward_host(self, begin, end, x, y, tokens):
         """ttl_moe_forward on caller-owned host buffers (pinned or pageable)."""
         self._check(lib().ttl_moe_forward(self.h, begin, end, _ptr(x), _ptr(y), tokens))
