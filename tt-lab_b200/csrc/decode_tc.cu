@@ -78,7 +78,6 @@ constexpr int kN = 16;                        // B rows: tc::kDigitTerms digit t
 constexpr int kPairs = kBlocks / 2;           // 45 K-block pairs (one MMA each) per row
 constexpr int kBRowBytes = 256;               // B bytes per K-block: [2 row groups][8 rows][16 B]
 constexpr int kCodeBytes = 96;                // block codes per B operand (90 + padding, 127)
-constexpr int kSfChunks = kScaleChunks;       // 23 scale chunks of 4 K-blocks
 constexpr int kTiles = kScaleTiles;           // 23 tiles of 128 rows
 constexpr int kStages = 4;
 constexpr int kEpiWarps = 4;                  // warps 0-3
