@@ -164,6 +164,27 @@ def test_forward_stack_matches_reference(ttl):
         assert_close(y[k], r[k])
 
 
+def test_forward_graph_replay_with_new_inputs(ttl):
+    """The second forward call on the same buffers replays the captured graph;
+    with new inputs its outputs must follow them (the split-K partials carry
+    per-launch tags, so a replay never reads the previous launch's words)."""
+    from ttl_moe import synth
+    layers = [synth_layer(20 + l, 32, layer=l, norm=True) for l in range(2)]
+    xa = synth.inputs_host(31, 4)
+    xb = synth.inputs_host(32, 4)
+    with ttl.MoE(experts=32, layers=2, device=0) as m:
+        for l, t in enumerate(layers):
+            m.upload_layer(l, t)
+        m.forward(0, 2, xa)
+        yb = m.forward(0, 2, xb)
+        ya = m.forward(0, 2, xa)
+    rb = oracle.forward(layers, xb, impl=impl())
+    ra = oracle.forward(layers, xa, impl=impl())
+    for k in range(4):
+        assert_close(yb[k], rb[k])
+        assert_close(ya[k], ra[k])
+
+
 def test_pack_roundtrip_hostile_bytes(ttl):
     rng = np.random.default_rng(3)
     g = rng.integers(0, 256, 2 * ttl.GGUF_MATRIX_BYTES, dtype=np.uint8)

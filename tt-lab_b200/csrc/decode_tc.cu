@@ -156,6 +156,7 @@ struct alignas(1024) Smem {
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier / end-of-step verdict, written by thread 0 only
+    uint32_t seq;  // tag base of this launch, read from the device at the start
     int epi_go;  // epilogue verdict, written by thread 0 only
     int sel[kTopK];
     int local[kTopK];
@@ -195,8 +196,8 @@ __device__ __forceinline__ void fail_wait(Smem &s, uint32_t *status) {
 // An f32 in the low half and, in the high half, the tag seq + step + 1 of the
 // step that wrote it: one 8-byte access carries both, so a reader that sees
 // the tag has the value, and words of other steps or launches never match.
-__device__ __forceinline__ uint32_t step_tag(const StackArgs &a, int step) {
-    return a.seq + uint32_t(step) + 1u;
+__device__ __forceinline__ uint32_t step_tag(const Smem &s, int step) {
+    return s.seq + uint32_t(step) + 1u;
 }
 __device__ __forceinline__ unsigned long long tagged(uint32_t tag, float v) {
     return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
@@ -762,7 +763,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const bool more_layers = (li + 1 < nl);
     const int tile = et.tile;
     const int step = t_token * nl + li;
-    const uint32_t tag = step_tag(a, step);
+    const uint32_t tag = step_tag(s, step);
     if (et.nslot > 1) {
         // the other contributors' tagged partials (after an abort the sums
         // are garbage; every later wait returns at once)
@@ -890,7 +891,7 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
         }
     }
     const int step = t_token * (a.layer_end - a.layer_begin) + li;
-    const uint32_t tag = step_tag(a, step);
+    const uint32_t tag = step_tag(s, step);
     TileOps ops;
     if (first_owned >= 0) {
         load_tile_ops(c, p, first_owned, t_token, li, next_router, ops);
@@ -1278,6 +1279,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
 
     if (threadIdx.x == 0) {
         s.abort = 0;
+        // the tag base lives on the device, so a replayed graph of this launch
+        // gets new tags: the last CTA to finish advances it by the steps
+        s.seq = *reinterpret_cast<const volatile uint32_t *>(a.seq_state);
         for (int i = 0; i < kStages; ++i) {
             tc::mbar_init(&s.full[i], 1);
             tc::mbar_init(&s.empty[i], kIssuers);
@@ -1643,6 +1647,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     if (warp == 0) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tbase, kTmemCols);
+    }
+    if (threadIdx.x == 0) {
+        unsigned done;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(done) : "l"(a.seq_state + 1) : "memory");
+        if (done == gridDim.x - 1) {
+            a.seq_state[0] = s.seq + uint32_t(steps);
+            a.seq_state[1] = 0u;
+        }
     }
 }
 

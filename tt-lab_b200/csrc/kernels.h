@@ -111,7 +111,8 @@ struct StackArgs {
     // tensor-core decode workspace.  Buffers marked [2] are used by steps of
     // even and odd index in turn; "tagged" words hold an f32 in the low half
     // and, in the high half, the tag seq + step + 1 of the step that wrote it.
-    uint32_t seq;                  // tag base of this launch (the host advances it by the launch's steps)
+    uint32_t *seq_state;           // [0] tag base of the next launch, [1] CTAs finished (the last one
+                                   //     advances [0] by the launch's steps and clears [1])
     unsigned long long *part_gu;   // [2][4 * 23 tiles][16 slots][256] gate/up tile partials, tagged
     unsigned long long *part_dn;   // [2][23 tiles][16 slots][128] down tile partials, tagged
     double *rp;                    // [2][23 tiles][129] next step's router sums per down tile
@@ -124,7 +125,18 @@ struct StackArgs {
     uint8_t *bnext_code;           // [2][96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
+    // Expert parallelism inside the launch (world > 1): every rank's exchange
+    // buffer as this GPU addresses it (its own, and the peers' mapped over
+    // NVLink), [2 step parities][world][kXchRow] tagged partial output rows.
+    int rank;
+    int world;
+    unsigned long long *xch[8];
 };
+constexpr int kMaxWorld = 8;
+constexpr int kXchRow = 23 * 128;  // rows of one rank's partial output (2880, padded to whole tiles)
+constexpr size_t xch_words(int world) {
+    return size_t(2) * size_t(world) * kXchRow;
+}
 
 constexpr int kTracePoints = 10;
 

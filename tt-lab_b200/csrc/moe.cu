@@ -99,7 +99,7 @@ struct ttl_moe {
     uint8_t *d_sfb_down = nullptr;
     uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
     uint8_t *d_bnext_code = nullptr;
-    uint32_t seq = 0;                 // tag base of the next launch
+    uint32_t *d_seq = nullptr;        // [2] tag base of the next launch and its finish count
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
@@ -350,8 +350,7 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.barrier = h->d_barrier;
     a.status = h->d_status;
     a.counters = h->d_counters;
-    a.seq = h->seq;
-    h->seq += uint32_t(tokens) * uint32_t(end - begin);
+    a.seq_state = h->d_seq;
     a.part_gu = h->d_part_gu;
     a.part_dn = h->d_part_dn;
     a.rp = h->d_rp;
@@ -607,6 +606,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_part_dn, kPartDnWords);
     rc = rc ? rc : alloc_n(h, &h->d_rp, kRpWords);
     rc = rc ? rc : alloc_n(h, &h->d_cnt, 6);
+    rc = rc ? rc : alloc_n(h, &h->d_seq, 2);
     rc = rc ? rc : alloc_n(h, &h->d_bdown, kBdownBytes);
     rc = rc ? rc : alloc_n(h, &h->d_sfb_down, kSfbDownBytes);
     rc = rc ? rc : alloc_n(h, &h->d_bnext, kBnextBytes);
@@ -652,6 +652,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(h->d_cnt, 0, 6 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_seq, 0, 2 * sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(h->d_part_gu, 0, kPartGuWords * 8) != cudaSuccess ||
         cudaMemset(h->d_part_dn, 0, kPartDnWords * 8) != cudaSuccess ||
         cudaMemset(h->d_rp, 0, kRpWords * 8) != cudaSuccess ||
