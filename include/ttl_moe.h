@@ -137,7 +137,9 @@ int ttl_moe_sync(ttl_moe *handle);
 void *ttl_moe_stream(ttl_moe *handle);
 
 /* Diagnostic counters: [0] decode router exact re-evaluations at near-ties,
- * [1] prefill tokens re-evaluated, [2] kernels launched by this handle.
+ * [1] prefill tokens re-evaluated, [2] kernels launched by this handle,
+ * [3] 1 when decode runs in the persistent kernel (with world > 1: the ranks
+ * exchange their partial outputs inside it), 0 when it runs per layer.
  * Returns the number written (<= n). */
 int ttl_moe_counters(const ttl_moe *handle, uint64_t *out, size_t n);
 

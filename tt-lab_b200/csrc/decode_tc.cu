@@ -249,6 +249,56 @@ __device__ __forceinline__ float wait_tagged(Smem &s, const unsigned long long *
     return (uint32_t(w >> 32) == tag) ? __uint_as_float(uint32_t(w)) : wait_tagged_slow(s, p, tag, status);
 }
 
+// ---- expert parallelism: the partial output rows of the ranks ----
+// System scope: the words of the exchange buffers are written by other GPUs
+// over NVLink (their stores to this GPU's memory) and read here.
+__device__ __forceinline__ void st_tagged_sys(unsigned long long *p, unsigned long long w) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged_sys(const unsigned long long *p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ float wait_tagged_sys(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status) {
+    const unsigned long long t0 = tc::now_ns();
+    while (true) {
+        const unsigned long long w = ld_tagged_sys(p);
+        if (uint32_t(w >> 32) == tag) {
+            return __uint_as_float(uint32_t(w));
+        }
+        if (aborted(s)) {
+            return 0.0f;
+        }
+        if (tc::now_ns() - t0 > 2000000000ull) {
+            fail_wait(s, status);
+            return 0.0f;
+        }
+    }
+}
+
+// This rank's partial v of output row `row` (the sum over its own selected
+// experts) goes to slot [step parity][rank][row] of every other rank's
+// exchange buffer; the ranks' partials are then added in rank order, so every
+// rank gets the same bits (and so the same next selection).  A rank that
+// never writes ends the wait with kStatusWaitTimeout.
+__device__ __forceinline__ float exchange_row(Smem &s, const StackArgs &a, int step, int row, float v, uint32_t tag) {
+    const size_t par = size_t(step & 1) * size_t(a.world) * kXchRow;
+    const unsigned long long word = tagged(tag, v);
+    for (int r = 0; r < a.world; ++r) {
+        if (r != a.rank) {
+            st_tagged_sys(a.xch[r] + par + size_t(a.rank) * kXchRow + row, word);
+        }
+    }
+    const unsigned long long *own = a.xch[a.rank] + par + row;
+    float tot = 0.0f;
+    for (int r = 0; r < a.world; ++r) {
+        const float pv = (r == a.rank) ? v : wait_tagged_sys(s, own + size_t(r) * kXchRow, tag, a.status);
+        tot = (r == 0) ? pv : __fadd_rn(tot, pv);
+    }
+    return tot;
+}
+
 // Waits (bounded) until the counter at p reaches `want`; acquire.
 __device__ __forceinline__ void wait_count(Smem &s, const unsigned *p, unsigned want, uint32_t *status) {
     const unsigned long long t0 = tc::now_ns();
@@ -802,7 +852,10 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const int row = 128 * tile + i;
     float yv = 0.0f;
     if (row < kDim) {
-        const float out = __fadd_rn(pg, o.bsum);
+        float out = __fadd_rn(pg, o.bsum);
+        if (a.world > 1) {
+            out = exchange_row(s, a, step, row, out, tag);
+        }
         yv = (a.mode == 1) ? __fadd_rn(o.resid, out) : out;
     }
     if (!next_router && row < kDim) {
@@ -983,6 +1036,17 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
         if (aborted(s)) {
             return;
         }
+    }
+    if (p.kind == 1 && p.kunits == 0 && int(blockIdx.x) < kTiles) {
+        // no selected expert is this rank's (expert parallelism): CTA t still
+        // reduces down tile t, with a zero partial, for the exchange and the
+        // rows, router sums and B operand that follow it
+        load_tile_ops(c, p, int(blockIdx.x), t_token, li, next_router, ops);
+        EpiTile et;
+        et.tile = int(blockIdx.x);
+        et.nslot = 1;
+        et.slot = 0;
+        finish_tile(c, p, et, ops, 0.0f, 0.0f, t_token, li, next_router);
     }
 }
 

@@ -125,12 +125,13 @@ struct StackArgs {
     uint8_t *bnext_code;           // [2][96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
-    // Expert parallelism inside the launch (world > 1): every rank's exchange
-    // buffer as this GPU addresses it (its own, and the peers' mapped over
-    // NVLink), [2 step parities][world][kXchRow] tagged partial output rows.
+    // Expert parallelism inside the launch (world > 1): a device array of
+    // every rank's exchange buffer as this GPU addresses it (its own, and the
+    // peers' mapped over NVLink), each [2 step parities][world][kXchRow]
+    // tagged partial output rows.
     int rank;
     int world;
-    unsigned long long *xch[8];
+    unsigned long long *const *xch;
 };
 constexpr int kMaxWorld = 8;
 constexpr int kXchRow = 23 * 128;  // rows of one rank's partial output (2880, padded to whole tiles)

@@ -100,6 +100,11 @@ struct ttl_moe {
     uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
     uint8_t *d_bnext_code = nullptr;
     uint32_t *d_seq = nullptr;        // [2] tag base of the next launch and its finish count
+    // expert parallelism inside the persistent kernel (world > 1)
+    unsigned long long *d_xch = nullptr;         // this rank's exchange buffer [2][world][kXchRow]
+    unsigned long long **d_xch_peers = nullptr;  // [world] every rank's buffer as this GPU addresses it
+    void *xch_open[kMaxWorld] = {};              // the peers' buffers, opened from their IPC handles
+    bool xch_ready = false;                      // every rank mapped every buffer
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
@@ -215,6 +220,75 @@ int allreduce(ttl_moe *h, float *buf, size_t n) {
     }
     return nccl_check(h, nccl(nullptr)->AllReduce(buf, buf, n, ncclFloat32, ncclSum, h->comm, h->stream),
                       "ncclAllReduce");
+}
+
+// The persistent decode kernel serves world == 1, and world > 1 once every
+// rank's exchange buffer is mapped on every rank (tensor-core kernel only);
+// otherwise decode runs per layer with an NCCL all-reduce.
+bool stack_path(const ttl_moe *h) {
+    return h->use_stack && (h->cfg.world == 1 || (h->use_tc && h->xch_ready));
+}
+
+// Exchange buffers for expert parallelism inside the persistent kernel: this
+// rank's buffer, the IPC handles of all ranks gathered over NCCL, the peers'
+// buffers opened (peer access over NVLink), and a table of all of them on the
+// device.  The ranks then agree (NCCL min) that every one of them succeeded,
+// so all take the same decode path.  Returns TTL_OK either way; a rank that
+// could not map stays on the per-layer path together with the others.
+int setup_exchange(ttl_moe *h) {
+    const int W = int(h->cfg.world);
+    const int R = int(h->cfg.rank);
+    const NcclApi *api = nccl(nullptr);
+    int ok = 1;
+    uint8_t *d_handles = nullptr;
+    int *d_ok = nullptr;
+    int rc = alloc_n(h, &h->d_xch, xch_words(W));
+    rc = rc ? rc : alloc_n(h, &h->d_xch_peers, size_t(W));
+    rc = rc ? rc : alloc_n(h, &d_handles, size_t(W) * sizeof(cudaIpcMemHandle_t));
+    rc = rc ? rc : alloc_n(h, &d_ok, 1);
+    if (rc) {
+        return rc;
+    }
+    cudaIpcMemHandle_t mine{};
+    if (cudaMemset(h->d_xch, 0, xch_words(W) * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine, h->d_xch) != cudaSuccess) {
+        ok = 0;
+        cudaGetLastError();
+    }
+    TTL_TRY_CUDA(h, cudaMemcpy(d_handles + size_t(R) * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    rc = nccl_check(h, api->AllGather(d_handles + size_t(R) * sizeof(mine), d_handles, sizeof(mine), ncclUint8,
+                                      h->comm, h->stream),
+                    "ncclAllGather");
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(W));
+    TTL_TRY_CUDA(h, cudaMemcpy(all.data(), d_handles, size_t(W) * sizeof(mine), cudaMemcpyDeviceToHost));
+    std::vector<unsigned long long *> ptrs(static_cast<size_t>(W), nullptr);
+    for (int r = 0; r < W && ok; ++r) {
+        if (r == R) {
+            ptrs[size_t(r)] = h->d_xch;
+            continue;
+        }
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[size_t(r)], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            ok = 0;
+            cudaGetLastError();
+            break;
+        }
+        h->xch_open[r] = p;
+        ptrs[size_t(r)] = static_cast<unsigned long long *>(p);
+    }
+    TTL_TRY_CUDA(h, cudaMemcpy(h->d_xch_peers, ptrs.data(), size_t(W) * sizeof(void *), cudaMemcpyHostToDevice));
+    TTL_TRY_CUDA(h, cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice));
+    rc = nccl_check(h, api->AllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, h->comm, h->stream), "ncclAllReduce");
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpy(&ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost));
+    h->xch_ready = ok != 0;
+    return TTL_OK;
 }
 
 // Enqueues one decode layer: router -> gate/up -> down (+ combine, residual).
@@ -351,6 +425,9 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.status = h->d_status;
     a.counters = h->d_counters;
     a.seq_state = h->d_seq;
+    a.rank = int(h->cfg.rank);
+    a.world = h->xch_ready ? int(h->cfg.world) : 1;
+    a.xch = h->d_xch_peers;
     a.part_gu = h->d_part_gu;
     a.part_dn = h->d_part_dn;
     a.rp = h->d_rp;
@@ -392,7 +469,7 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
 }
 
 int enqueue_forward(ttl_moe *h, int begin, int end, const float *x, float *y, size_t tokens) {
-    if (h->use_stack && h->cfg.world == 1 && end > begin) {
+    if (stack_path(h) && end > begin) {
         return enqueue_stack(h, begin, end, x, y, tokens, 1);
     }
     for (size_t t = 0; t < tokens; ++t) {
@@ -676,6 +753,12 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
             h->comm = nullptr;
             return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + api->GetErrorString(r)));
         }
+        if (h->use_stack && h->use_tc) {
+            const int xrc = setup_exchange(h);
+            if (xrc) {
+                return bail(xrc);
+            }
+        }
     }
     *handle_out = h;
     return TTL_OK;
@@ -699,6 +782,11 @@ void ttl_moe_destroy(ttl_moe *h) {
     for (cudaEvent_t e : h->stack_ev) {
         if (e) {
             cudaEventDestroy(e);
+        }
+    }
+    for (void *p : h->xch_open) {
+        if (p) {
+            cudaIpcCloseMemHandle(p);
         }
     }
     if (h->comm) {
@@ -812,7 +900,7 @@ int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int3
     }
     int rc = check_layer(h, layer);
     rc = rc ? rc : set_device(h);
-    if (!rc && h->use_stack && h->cfg.world == 1) {
+    if (!rc && stack_path(h)) {
         rc = enqueue_stack(h, layer, layer + 1, x, out, 1, 0);
     } else if (!rc) {
         rc = enqueue_decode_layer(h, layer, x, 0, nullptr, out);
@@ -844,7 +932,7 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
         return rc;
     }
     TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    if (h->use_stack && h->cfg.world == 1) {
+    if (stack_path(h)) {
         rc = enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0);
     } else {
         rc = enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
@@ -1103,8 +1191,8 @@ int ttl_moe_counters(const ttl_moe *h, uint64_t *out, size_t n) {
     unsigned long long dev[4] = {0, 0, 0, 0};
     cudaSetDevice(h->device);
     cudaMemcpy(dev, h->d_counters, sizeof(dev), cudaMemcpyDeviceToHost);
-    const uint64_t vals[3] = {dev[0], dev[1], h->launches};
-    const size_t k = std::min<size_t>(n, 3);
+    const uint64_t vals[4] = {dev[0], dev[1], h->launches, stack_path(h) ? 1u : 0u};
+    const size_t k = std::min<size_t>(n, 4);
     for (size_t i = 0; i < k; ++i) {
         out[i] = vals[i];
     }

@@ -251,10 +251,11 @@ class MoE:
         return np.frombuffer(out, dtype=np.uint64).reshape(n, 10).astype(np.int64)
 
     def counters(self):
-        out = (ctypes.c_uint64 * 3)()
-        n = lib().ttl_moe_counters(self.h, out, 3)
+        out = (ctypes.c_uint64 * 4)()
+        n = lib().ttl_moe_counters(self.h, out, 4)
         vals = [int(out[i]) for i in range(n)]
-        return {"router_exact_reevals": vals[0], "prefill_reevals": vals[1], "launches": vals[2]}
+        return {"router_exact_reevals": vals[0], "prefill_reevals": vals[1], "launches": vals[2],
+                "persistent_decode": vals[3]}
 
 
 def packed_bytes(matrices: int) -> int:
