@@ -104,10 +104,11 @@ int ttl_moe_decode(ttl_moe *handle, int layer, const float *x, float *out, int32
 
 /* Prefill MoE of `tokens` tokens: GptOssModel::moe_batch.
  * x, out: HOST f32 [tokens][2880]; idx/w: optional host [tokens][4].
- * tokens <= max_tokens.  With world > 1 every rank passes the same tokens,
- * computes the pairs routed to its own experts, and the ranks' partial outputs
- * are summed by an NCCL all-reduce, so every rank returns the full output.
- * Blocking. */
+ * tokens <= max_tokens.  With world > 1 each rank passes its own tokens (its
+ * share of the batch) and receives their outputs: the token rows go to the
+ * ranks owning their experts and the weighted expert outputs come back
+ * (NCCL send/recv), then the owner combines them in ascending expert id.
+ * Every rank must call it (with at least one token).  Blocking. */
 int ttl_moe_prefill(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
                     float *top4_w);
 
@@ -121,7 +122,8 @@ int ttl_moe_forward(ttl_moe *handle, int layer_begin, int layer_end, const float
 /* Device-pointer forms of the three calls above: all pointers are device
  * memory of the handle's GPU; the work is enqueued on the handle's stream and
  * the call returns without waiting.  ttl_moe_sync() waits and reports.
- * Prefill's x must be 16-byte aligned (TTL_ERR_ARGUMENT otherwise). */
+ * Prefill's x must be 16-byte aligned (TTL_ERR_ARGUMENT otherwise); with
+ * world > 1 prefill waits once inside the call, for the ranks' send counts. */
 int ttl_moe_decode_async(ttl_moe *handle, int layer, const float *x, float *out, int32_t *top4_idx,
                          float *top4_w);
 int ttl_moe_prefill_async(ttl_moe *handle, int layer, const float *x, size_t tokens, float *out,

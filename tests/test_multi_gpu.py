@@ -6,9 +6,10 @@ persistent kernel: every rank computes the selected experts it owns, and the
 ranks exchange their partial output rows inside the kernel over NVLink (peer
 stores of tagged words into each other's buffers), adding them in rank order.
 So all ranks return the same bits, and those match tt-lab's CPU MoE (the
-oracle) within the same tolerance as one GPU.  Prefill sums the ranks'
-partial outputs with NCCL.  The processes exchange the NCCL id over gloo
-(127.0.0.1).
+oracle) within the same tolerance as one GPU.  Prefill is token-sharded:
+each rank passes its own share of the tokens, which go to their experts'
+owners and come back as weighted rows by NCCL send/recv.  The processes
+exchange the NCCL id over gloo (127.0.0.1).
 """
 import json
 import os
@@ -51,6 +52,7 @@ def _worker(rank, world, port, outdir):
     layers = [layer_of(40 + l, 32, layer=l, norm=True) for l in range(2)]
     xs = synth.inputs_host(41, 3)
     xp = synth.inputs_host(42, 17)
+    lo, hi = (rank * xp.shape[0]) // world, ((rank + 1) * xp.shape[0]) // world
     res = {"rank": rank}
     with ttl_moe.MoE(experts=32, layers=2, max_tokens=32, device=rank, rank=rank, world=world,
                      nccl_id_bytes=nid) as m:
@@ -60,7 +62,7 @@ def _worker(rank, world, port, outdir):
         y = m.forward(0, 2, xs)
         y2 = m.forward(0, 2, xs[::-1].copy())  # a replay of the captured forward with new inputs
         out, idx, w = m.moe(0, np.ascontiguousarray(xs[0]))
-        pout, pidx, pw = m.moe_batch(0, xp)
+        pout, pidx, pw = m.moe_batch(0, xp[lo:hi])
     np.save(pathlib.Path(outdir) / f"y{rank}.npy", y)
     np.save(pathlib.Path(outdir) / f"y2_{rank}.npy", y2)
     np.save(pathlib.Path(outdir) / f"d{rank}.npy", out)
@@ -113,6 +115,8 @@ def test_two_gpu_expert_parallel_matches_reference(tmp_path):
     assert all(r["idx"] == [int(v) for v in ridx] for r in res)
     assert _rel(ds[0], rd) <= TOL
     rp, rpidx, _ = oracle.moe_prefill(layers[0], xp, impl=impl)
-    assert res[0]["pidx"] == rpidx.tolist()
+    n = xp.shape[0]
+    assert sum((res[r]["pidx"] for r in range(world)), []) == rpidx.tolist()
     for r in range(world):
-        assert _rel(ps[r], rp) <= TOL
+        lo, hi = (r * n) // world, ((r + 1) * n) // world
+        assert _rel(ps[r], rp[lo:hi]) <= TOL

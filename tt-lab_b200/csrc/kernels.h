@@ -208,4 +208,19 @@ constexpr size_t kPrefillUnitBytes = size_t(96) * 192 * 16;
 constexpr size_t kPrefillUnitScaleBytes = size_t(24) * 2 * 512;
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream);
 
+// Expert-parallel prefill (prefill_ep.cu): dispatch plan, pack, return and
+// owner combine around the expert pipeline.  Row offsets per rank, by value.
+struct EpOffsets {
+    int v[kMaxWorld];
+};
+void launch_ep_plan(const int32_t *idx, int tokens, int world, int per_rank, int32_t *tok_off, int32_t *pair_off,
+                    int32_t *cnt, cudaStream_t stream);
+void launch_ep_pack(const float *x, const int32_t *idx, const float *wts, int tokens, int world,
+                    const int32_t *tok_off, const EpOffsets &send_off, float *sendx, int32_t *send_idx,
+                    float *send_w, cudaStream_t stream);
+void launch_ep_return(const PrefillWork &w, int tokens, int rank, int per_rank, int32_t *ret_off, float *ret,
+                      cudaStream_t stream);
+void launch_ep_combine(const int32_t *idx, int tokens, int world, int per_rank, const int32_t *pair_off,
+                       const EpOffsets &back_off, const float *back, float *out, cudaStream_t stream);
+
 } // namespace ttl

@@ -105,6 +105,24 @@ struct ttl_moe {
     unsigned long long **d_xch_peers = nullptr;  // [world] every rank's buffer as this GPU addresses it
     void *xch_open[kMaxWorld] = {};              // the peers' buffers, opened from their IPC handles
     bool xch_ready = false;                      // every rank mapped every buffer
+    // expert-parallel prefill (world > 1): the own tokens' routing, the
+    // dispatch plan, and the send / receive / return row buffers
+    struct {
+        int32_t *own_idx = nullptr;    // [T][4] top-4 of this rank's own tokens
+        float *own_w = nullptr;        // [T][4]
+        float *own_logits = nullptr;   // [T][E]
+        int32_t *tok_off = nullptr;    // [T][world] send index of each own token per destination (-1: none)
+        int32_t *pair_off = nullptr;   // [T][world] pairs to the destination before the token
+        int32_t *cnt = nullptr;        // [2 world] tokens, then pairs, sent to each rank
+        int32_t *cnt_all = nullptr;    // [world][2 world] every rank's cnt
+        float *sendx = nullptr;        // [min(world, 4) T] token rows, by destination
+        int32_t *send_idx = nullptr;   // [min(world, 4) T][4]
+        float *send_w = nullptr;
+        float *recvx = nullptr;        // [world T] the received token rows (the expert pipeline's input)
+        int32_t *ret_off = nullptr;    // [world T]
+        float *ret = nullptr;          // [4 world T] rows w * down returned to the senders
+        float *back = nullptr;         // [4 T] rows returned to this rank
+    } ep;
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
     uint32_t *d_pack_flags = nullptr; // packer flags of the last upload
@@ -522,7 +540,133 @@ int sync_and_check(ttl_moe *h) {
     return check_status(h);
 }
 
+// Expert-parallel prefill of this rank's own tokens (prefill_ep.cu has the
+// steps): router, dispatch plan, counts all-gathered (one host sync: NCCL
+// takes the sizes from the host), token rows out by grouped NCCL send/recv,
+// the expert pipeline on the received tokens, rows w * down back, owner
+// combine.  A rank's block to itself is a device copy.
+int enqueue_prefill_ep(ttl_moe *h, int layer, const float *x, size_t tokens, float *out) {
+    const int W = int(h->cfg.world);
+    const int R = int(h->cfg.rank);
+    const int P = h->expert_count;
+    const NcclApi *api = nccl(nullptr);
+    const LayerDev L = layer_view(h, layer);
+    const TmaDesc *tma = h->host_layers[size_t(layer)].tma;
+    if (!tma) {
+        return fail(h, TTL_ERR_STATE, "layer " + std::to_string(layer) + " has no tensor maps");
+    }
+    auto &ep = h->ep;
+    PrefillWork own = h->pw;
+    own.logits = ep.own_logits;
+    own.top_idx = ep.own_idx;
+    own.top_w = ep.own_w;
+    PrefillShape so{int(h->cfg.experts), h->expert_begin, h->expert_count, int(tokens), h->sms};
+    launch_prefill_router(L, own, so, x, h->stream);
+    launch_ep_plan(ep.own_idx, int(tokens), W, P, ep.tok_off, ep.pair_off, ep.cnt, h->stream);
+    int rc = nccl_check(h, api->AllGather(ep.cnt, ep.cnt_all, size_t(2 * W), ncclInt32, h->comm, h->stream),
+                        "ncclAllGather");
+    if (rc) {
+        return rc;
+    }
+    std::vector<int32_t> cnt(size_t(2 * W * W));
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(cnt.data(), ep.cnt_all, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                    h->stream));
+    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    auto sent = [&](int from, int to) { return cnt[size_t(from) * 2 * W + to]; };          // tokens
+    auto pairs = [&](int from, int to) { return cnt[size_t(from) * 2 * W + W + to]; };    // pairs
+    EpOffsets send_off{}, recv_off{}, ret_off{}, back_off{};
+    int ns = 0, nr = 0, nret = 0, nback = 0;
+    for (int d = 0; d < W; ++d) {
+        send_off.v[d] = ns;
+        ns += sent(R, d);
+        recv_off.v[d] = nr;  // from rank d
+        nr += sent(d, R);
+        ret_off.v[d] = nret;  // to rank d
+        nret += pairs(d, R);
+        back_off.v[d] = nback;  // from rank d
+        nback += pairs(R, d);
+    }
+    // ns <= min(W, 4) * tokens and nr <= W * max_tokens by construction (each
+    // rank sends each own token at most once per destination), so the buffers
+    // hold them; no rank leaves here alone, which would strand the others in
+    // the send/recv below
+    launch_ep_pack(x, ep.own_idx, ep.own_w, int(tokens), W, ep.tok_off, send_off, ep.sendx, ep.send_idx, ep.send_w,
+                   h->stream);
+    // token rows and their top-4 to the experts' owners
+    auto rows = [&](float *base, int row) { return base + size_t(row) * kDim; };
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(rows(ep.recvx, recv_off.v[R]), rows(ep.sendx, send_off.v[R]),
+                                    size_t(sent(R, R)) * kDim * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->pw.top_idx + 4 * size_t(recv_off.v[R]), ep.send_idx + 4 * size_t(send_off.v[R]),
+                                    size_t(sent(R, R)) * 4 * sizeof(int32_t), cudaMemcpyDeviceToDevice, h->stream));
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->pw.top_w + 4 * size_t(recv_off.v[R]), ep.send_w + 4 * size_t(send_off.v[R]),
+                                    size_t(sent(R, R)) * 4 * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
+    api->GroupStart();
+    for (int d = 0; d < W && !rc; ++d) {
+        if (d == R) {
+            continue;
+        }
+        if (sent(R, d) > 0) {
+            rc = rc ? rc : nccl_check(h, api->Send(rows(ep.sendx, send_off.v[d]), size_t(sent(R, d)) * kDim,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
+            rc = rc ? rc : nccl_check(h, api->Send(ep.send_idx + 4 * size_t(send_off.v[d]), size_t(sent(R, d)) * 4,
+                                                   ncclInt32, d, h->comm, h->stream), "ncclSend");
+            rc = rc ? rc : nccl_check(h, api->Send(ep.send_w + 4 * size_t(send_off.v[d]), size_t(sent(R, d)) * 4,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
+        }
+        if (sent(d, R) > 0) {
+            rc = rc ? rc : nccl_check(h, api->Recv(rows(ep.recvx, recv_off.v[d]), size_t(sent(d, R)) * kDim,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
+            rc = rc ? rc : nccl_check(h, api->Recv(h->pw.top_idx + 4 * size_t(recv_off.v[d]), size_t(sent(d, R)) * 4,
+                                                   ncclInt32, d, h->comm, h->stream), "ncclRecv");
+            rc = rc ? rc : nccl_check(h, api->Recv(h->pw.top_w + 4 * size_t(recv_off.v[d]), size_t(sent(d, R)) * 4,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
+        }
+    }
+    const int grc = nccl_check(h, api->GroupEnd(), "ncclGroupEnd");
+    rc = rc ? rc : grc;
+    if (rc) {
+        return rc;
+    }
+    // the experts of this rank on the received tokens
+    if (nr > 0) {
+        PrefillShape sp{int(h->cfg.experts), h->expert_begin, h->expert_count, nr, h->sms};
+        launch_prefill_route(h->pw, sp, h->stream);
+        launch_prefill_gateup(L, tma, h->pw, sp, ep.recvx, h->stream);
+        launch_prefill_down(L, tma, h->pw, sp, h->stream);
+        launch_ep_return(h->pw, nr, R, P, ep.ret_off, ep.ret, h->stream);
+    }
+    // rows w * down back to the tokens' owners
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(rows(ep.back, back_off.v[R]), rows(ep.ret, ret_off.v[R]),
+                                    size_t(pairs(R, R)) * kDim * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
+    api->GroupStart();
+    for (int d = 0; d < W && !rc; ++d) {
+        if (d == R) {
+            continue;
+        }
+        if (pairs(d, R) > 0) {
+            rc = rc ? rc : nccl_check(h, api->Send(rows(ep.ret, ret_off.v[d]), size_t(pairs(d, R)) * kDim,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
+        }
+        if (pairs(R, d) > 0) {
+            rc = rc ? rc : nccl_check(h, api->Recv(rows(ep.back, back_off.v[d]), size_t(pairs(R, d)) * kDim,
+                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
+        }
+    }
+    const int grc2 = nccl_check(h, api->GroupEnd(), "ncclGroupEnd");
+    rc = rc ? rc : grc2;
+    if (rc) {
+        return rc;
+    }
+    launch_ep_combine(ep.own_idx, int(tokens), W, P, ep.pair_off, back_off, ep.back, out, h->stream);
+    h->launches += 10;
+    TTL_TRY_CUDA(h, cudaGetLastError());
+    return TTL_OK;
+}
+
 int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float *out) {
+    if (h->cfg.world > 1) {
+        return enqueue_prefill_ep(h, layer, x, tokens, out);
+    }
     const LayerDev L = layer_view(h, layer);
     PrefillShape s{int(h->cfg.experts), h->expert_begin, h->expert_count, int(tokens), h->sms};
     launch_prefill_router(L, h->pw, s, x, h->stream);
@@ -536,10 +680,16 @@ int enqueue_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     launch_prefill_combine(h->pw, s, out, h->stream);
     h->launches += 6;
     TTL_TRY_CUDA(h, cudaGetLastError());
-    if (h->cfg.world > 1) {
-        return allreduce(h, out, tokens * kDim);
-    }
     return TTL_OK;
+}
+
+// The own tokens' top-4 of the last prefill (world > 1: the routing of this
+// rank's tokens, not of the tokens it received).
+const int32_t *prefill_top_idx(const ttl_moe *h) {
+    return h->cfg.world > 1 ? h->ep.own_idx : h->pw.top_idx;
+}
+const float *prefill_top_w(const ttl_moe *h) {
+    return h->cfg.world > 1 ? h->ep.own_w : h->pw.top_w;
 }
 
 } // namespace
@@ -694,14 +844,35 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     h->dw.counters = h->d_counters;
     h->dw.status = h->d_status;
     if (c.max_tokens > 0) {
-        const size_t pairs = 4 * T;
-        rc = rc ? rc : alloc_n(h, &h->pw.logits, T * E);
+        // at world > 1 the expert pipeline runs on the tokens received from
+        // every rank (each sends each own token at most once)
+        const size_t Tp = size_t(c.world) * T;
+        if (c.world > 1) {
+            const size_t W = c.world;
+            const size_t Ts = std::min<size_t>(W, 4) * T;
+            rc = rc ? rc : alloc_n(h, &h->ep.own_idx, 4 * T);
+            rc = rc ? rc : alloc_n(h, &h->ep.own_w, 4 * T);
+            rc = rc ? rc : alloc_n(h, &h->ep.own_logits, T * E);
+            rc = rc ? rc : alloc_n(h, &h->ep.tok_off, T * W);
+            rc = rc ? rc : alloc_n(h, &h->ep.pair_off, T * W);
+            rc = rc ? rc : alloc_n(h, &h->ep.cnt, 2 * W);
+            rc = rc ? rc : alloc_n(h, &h->ep.cnt_all, 2 * W * W);
+            rc = rc ? rc : alloc_n(h, &h->ep.sendx, Ts * kDim);
+            rc = rc ? rc : alloc_n(h, &h->ep.send_idx, 4 * Ts);
+            rc = rc ? rc : alloc_n(h, &h->ep.send_w, 4 * Ts);
+            rc = rc ? rc : alloc_n(h, &h->ep.recvx, Tp * kDim);
+            rc = rc ? rc : alloc_n(h, &h->ep.ret_off, Tp);
+            rc = rc ? rc : alloc_n(h, &h->ep.ret, 4 * Tp * kDim);
+            rc = rc ? rc : alloc_n(h, &h->ep.back, 4 * T * kDim);
+        }
+        const size_t pairs = 4 * Tp;
+        rc = rc ? rc : alloc_n(h, &h->pw.logits, Tp * E);
         rc = rc ? rc : alloc_n(h, &h->pw.top_idx, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.top_w, pairs);
         rc = rc ? rc : alloc_n(h, &h->pw.counts, E);
         rc = rc ? rc : alloc_n(h, &h->pw.offsets, E + 1);
         // slots: each local expert's pairs padded to 16
-        const size_t groups = prefill_groups(T, size_t(h->expert_count));
+        const size_t groups = prefill_groups(Tp, size_t(h->expert_count));
         const size_t slots = 16 * groups;
         rc = rc ? rc : alloc_n(h, &h->pw.pair_token, slots);
         rc = rc ? rc : alloc_n(h, &h->pw.pair_slot, pairs);
@@ -710,7 +881,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.units, groups);
         rc = rc ? rc : alloc_n(h, &h->pw.unit_count, 1);
         rc = rc ? rc : alloc_n(h, &h->pw.down, slots * kDim);
-        const size_t units = prefill_units(T, size_t(h->expert_count));
+        const size_t units = prefill_units(Tp, size_t(h->expert_count));
         rc = rc ? rc : alloc_n(h, &h->pw.bdig, units * kPrefillUnitBytes);
         rc = rc ? rc : alloc_n(h, &h->pw.bsfb, units * kPrefillUnitScaleBytes);
         rc = rc ? rc : alloc_n(h, &h->pw.bdig_dn, units * kPrefillUnitBytes);
@@ -975,11 +1146,11 @@ int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, 
         return rc;
     }
     if (top4_idx) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->pw.top_idx, tokens * 4 * sizeof(int32_t),
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, prefill_top_idx(h), tokens * 4 * sizeof(int32_t),
                                         cudaMemcpyDeviceToDevice, h->stream));
     }
     if (top4_w) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->pw.top_w, tokens * 4 * sizeof(float), cudaMemcpyDeviceToDevice,
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, prefill_top_w(h), tokens * 4 * sizeof(float), cudaMemcpyDeviceToDevice,
                                         h->stream));
     }
     return TTL_OK;
@@ -1011,11 +1182,11 @@ int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     }
     TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->d_y, tokens * kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
     if (top4_idx) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->pw.top_idx, tokens * 4 * sizeof(int32_t),
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, prefill_top_idx(h), tokens * 4 * sizeof(int32_t),
                                         cudaMemcpyDeviceToHost, h->stream));
     }
     if (top4_w) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->pw.top_w, tokens * 4 * sizeof(float), cudaMemcpyDeviceToHost,
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, prefill_top_w(h), tokens * 4 * sizeof(float), cudaMemcpyDeviceToHost,
                                         h->stream));
     }
     return sync_and_check(h);
