@@ -274,6 +274,52 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
     }
 
 
+def prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist, iters=10):
+    """one gpt-oss-120b layer (128 experts), prefill
+    of T = 2048 tokens with Zipf(1.2)-skewed routing, expert-parallel over the
+    job's ranks: rank r passes tokens [r T / N, (r + 1) T / N), which go to
+    their experts' owners and come back as weighted rows (the library's NCCL
+    send/recv).  Time per call: CUDA events on the library's stream (the call
+    waits once inside for the ranks' send counts), max over ranks."""
+    from ttl_moe import parallel
+    E, T = 128, 2048
+    lo, hi = rank * T // world, (rank + 1) * T // world
+    nid = None
+    if world > 1:
+        nid = parallel.share_bytes(dist, ttl_moe.nccl_id() if rank == 0 else None, ttl_moe.NCCL_ID_BYTES,
+                                   device="cuda")
+    with ttl_moe.MoE(experts=E, layers=1, max_tokens=hi - lo, device=local, rank=rank, world=world,
+                     nccl_id_bytes=nid) as m:
+        t = synth.layer_device(4, 0, E, device="cuda", zipf_s=1.2)
+        m.upload_layer(0, t)
+        del t
+        torch.cuda.empty_cache()
+        x = torch.from_numpy(synth.inputs_host(4, T)[lo:hi].copy()).cuda()
+        out = torch.empty_like(x)
+        st = torch.cuda.ExternalStream(m.stream())
+        for _ in range(3):
+            m.prefill_async(0, x, hi - lo, out)
+        m.sync()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(iters):
+            m.prefill_async(0, x, hi - lo, out)
+        e1.record(st)
+        e1.synchronize()
+        m.sync()
+        ms = e0.elapsed_time(e1) / iters
+    if dist:
+        ms = parallel.max_over_ranks(dist, [ms], device="cuda")[0]
+    return {"workload": "cfg4: gpt-oss-120b single MoE layer, prefill T=2048, router bias Zipf(1.2), "
+                        f"expert-parallel over {world} GPU(s), tokens sharded T/N per rank",
+            "ms_per_layer": ms, "tokens_per_s": T / (ms * 1e-3), "n_gpus": world,
+            "timing": "CUDA events on the library stream around 10 calls, max over ranks"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -401,11 +447,14 @@ def main():
             if ln.startswith("traffic_bytes_per_token_layer:"):
                 traffic = int(ln.split(":")[1]) * kms["steps"]
     prefill = None
-    if world == 1 and not args.no_prefill:
+    prefill_ep = None
+    if not args.no_prefill:
         moe.close()
         torch.cuda.empty_cache()
-        prefill = prefill_cfg2(torch, ttl_moe, synth, local,
-                               cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
+        if world == 1:
+            prefill = prefill_cfg2(torch, ttl_moe, synth, local,
+                                   cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
+        prefill_ep = prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist)
 
     if rank == 0:
         cpu = None
@@ -460,6 +509,7 @@ def main():
                     "d2h_bytes_per_step": tokens * DIM * 4},
             "gpu_launches": launches,
             "prefill": prefill,
+            "prefill_ep": prefill_ep,
         }
         print(json.dumps(line))
     moe.close()
