@@ -658,7 +658,7 @@ int enqueue_prefill_ep(ttl_moe *h, int layer, const float *x, size_t tokens, flo
         return rc;
     }
     launch_ep_combine(ep.own_idx, int(tokens), W, P, ep.pair_off, back_off, ep.back, out, h->stream);
-    h->launches += 10;
+    h->launches += (nr > 0) ? 10 : 4;  // router, plan, pack, combine (+ route, split, 2 MMA, 2 return)
     TTL_TRY_CUDA(h, cudaGetLastError());
     return TTL_OK;
 }
