@@ -25,6 +25,7 @@
 #include <cstdio>
 #include <cstring>
 #include <initializer_list>
+#include <latch>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -446,10 +447,12 @@ int tref_moe_prefill(size_t experts, const float *router_w, const float *router_
 }
 
 // Expert-parallel harness for the CPU baseline: the reference's router
-// (matvec_add_f32) and per-expert MXFP4 kernels, one host thread per selected
-// expert, combine kept serial in rank order as in src/model.cpp:323-337.  The
-// selection and softmax are src/model.cpp:296-321 restated.  Up to `threads`
-// threads (1 = the reference's own single-threaded order).
+// (matvec_add_f32) and per-expert MXFP4 kernels on host threads, combine kept
+// serial in rank order as in src/model.cpp:323-337.  The selection and softmax
+// are src/model.cpp:296-321 restated.  threads = 1: the reference's own
+// single-threaded order; 2..4: one thread per selected expert (gate, up,
+// down); 8: the eight gate and up products at once, each expert's down after
+// its up (the most the unmodified whole-matrix kernels can overlap).
 int tref_moe_decode_threaded(size_t experts, const float *router_w, const float *router_b, const uint8_t *gate_w,
                              const float *gate_b, const uint8_t *up_w, const float *up_b, const uint8_t *down_w,
                              const float *down_b, const float *x, float *out, int threads) {
@@ -503,10 +506,42 @@ int tref_moe_decode_threaded(size_t experts, const float *router_w, const float 
             }
             matvec_add_mxfp4_2880(dw, db, hidden.data(), down.data() + sel * kDim, e);
         };
-        const size_t n = size_t(std::clamp(threads, 1, 4));
+        const size_t n = size_t(std::clamp(threads, 1, 8));
         if (n == 1) {
             for (size_t sel = 0; sel < 4; ++sel) {
                 run_expert(sel);
+            }
+        } else if (n >= 8) {
+            // threads 0-3: gate of expert t, then (once thread t + 4 has its
+            // up) SwiGLU and down; threads 4-7: up of expert t - 4
+            std::vector<float> gate(4 * kDim), up(4 * kDim);
+            std::array<std::unique_ptr<std::latch>, 4> up_done;
+            for (auto &l : up_done) {
+                l = std::make_unique<std::latch>(1);
+            }
+            std::vector<std::thread> pool;
+            for (size_t t = 0; t < 8; ++t) {
+                pool.emplace_back([&, t] {
+                    const size_t sel = t & 3;
+                    const size_t e = order[sel];
+                    if (t >= 4) {
+                        matvec_add_mxfp4_2880(uw, ub, x, up.data() + sel * kDim, e);
+                        up_done[sel]->count_down();
+                        return;
+                    }
+                    matvec_add_mxfp4_2880(gw, gb, x, gate.data() + sel * kDim, e);
+                    up_done[sel]->wait();
+                    std::vector<float> hidden(kDim);
+                    for (size_t i = 0; i < kDim; ++i) {
+                        const float a = std::min(gate[sel * kDim + i], 7.0f);
+                        const float b = std::clamp(up[sel * kDim + i], -7.0f, 7.0f);
+                        hidden[i] = (a / (1.0f + std::exp(-1.702f * a))) * (b + 1.0f);
+                    }
+                    matvec_add_mxfp4_2880(dw, db, hidden.data(), down.data() + sel * kDim, e);
+                });
+            }
+            for (std::thread &th : pool) {
+                th.join();
             }
         } else {
             std::vector<std::thread> pool;
