@@ -426,6 +426,20 @@ def main():
         dist.barrier()
     clk = clocks.stop()
 
+    # the drop-in call of tt-lab's GptOssModel::moe: one (token, layer) per
+    # blocking ttl_moe_decode on host buffers (H2D, one launch, D2H, sync)
+    calls = 200
+    xh = np.ascontiguousarray(x_host[0])
+    moe.moe(0, xh)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(calls):
+        moe.moe(i % layers, xh)
+    call_us = (time.perf_counter() - t0) / calls * 1e6
+    if dist:
+        call_us = parallel.max_over_ranks(dist, [call_us], device="cuda")[0]
+
     if dist:
         ms, e2e_s = parallel.max_over_ranks(dist, [ms, e2e_s], device="cuda")
 
@@ -511,6 +525,9 @@ def main():
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tokens * DIM * 4,
                     "d2h_bytes_per_step": tokens * DIM * 4},
             "gpu_launches": launches,
+            "decode_call": {"us_per_call": call_us, "calls": calls,
+                            "what": "ttl_moe_decode (tt-lab's GptOssModel::moe drop-in): one token-layer per "
+                                    "blocking call on host buffers, wall clock, max over ranks"},
             "prefill": prefill,
             "prefill_ep": prefill_ep,
         }
