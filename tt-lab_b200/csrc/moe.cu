@@ -85,6 +85,18 @@ struct ttl_moe {
     ncclComm_t comm = nullptr;
     std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;  // exec, kernels per replay
     bool use_graphs = true;
+    // the blocking single-layer decode (ttl_moe_decode): pinned staging of its
+    // input and outputs, and one captured graph per layer (copies in, the
+    // persistent kernel, copies out with the status word)
+    struct DecodePin {
+        float x[kDim];
+        float y[kDim];
+        int32_t idx[4];
+        float w[4];
+        uint32_t status;
+    };
+    DecodePin *pin = nullptr;
+    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> decode_graphs;
     bool profile = false;
     int profile_layers = 0;        // layers covered by the recorded events
     std::vector<cudaEvent_t> events;  // [layers][4]
@@ -947,6 +959,13 @@ void ttl_moe_destroy(ttl_moe *h) {
         cudaGraphExecDestroy(g.second.first);
     }
     h->graphs.clear();
+    for (auto &g : h->decode_graphs) {
+        cudaGraphExecDestroy(g.second.first);
+    }
+    h->decode_graphs.clear();
+    if (h->pin) {
+        cudaFreeHost(h->pin);
+    }
     for (cudaEvent_t e : h->events) {
         cudaEventDestroy(e);
     }
@@ -1102,24 +1121,72 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
     if (rc) {
         return rc;
     }
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    if (stack_path(h)) {
+    if (!stack_path(h) || !h->use_graphs) {
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
+        rc = stack_path(h) ? enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0)
+                           : enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
+        if (rc) {
+            return rc;
+        }
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->d_y, kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+        if (top4_idx) {
+            TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                            h->stream));
+        }
+        if (top4_w) {
+            TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToHost,
+                                            h->stream));
+        }
+        return sync_and_check(h);
+    }
+    // one launch of a captured graph per call: the input from pinned staging,
+    // the persistent kernel, the output, top-4 and status word back to it
+    if (!h->pin) {
+        TTL_TRY_CUDA(h, cudaHostAlloc(reinterpret_cast<void **>(&h->pin), sizeof(*h->pin), cudaHostAllocDefault));
+    }
+    auto found = h->decode_graphs.find(layer);
+    if (found == h->decode_graphs.end()) {
+        cudaGraph_t graph = nullptr;
+        TTL_TRY_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+        const uint64_t launches = h->launches;
+        cudaMemcpyAsync(h->d_x, h->pin->x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream);
         rc = enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0);
-    } else {
-        rc = enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
+        cudaMemcpyAsync(h->pin->y, h->d_y, kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
+        cudaMemcpyAsync(h->pin->idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream);
+        cudaMemcpyAsync(h->pin->w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
+        cudaMemcpyAsync(&h->pin->status, h->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, h->stream);
+        const cudaError_t end = cudaStreamEndCapture(h->stream, &graph);
+        if (rc || end != cudaSuccess) {
+            if (graph) {
+                cudaGraphDestroy(graph);
+            }
+            return rc ? rc : fail(h, TTL_ERR_CUDA, std::string("stream capture: ") + cudaGetErrorString(end));
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (inst != cudaSuccess) {
+            return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
+        }
+        const uint64_t per_replay = h->launches - launches;
+        h->launches = launches;
+        found = h->decode_graphs.emplace(layer, std::make_pair(exec, per_replay)).first;
     }
-    if (rc) {
-        return rc;
+    std::memcpy(h->pin->x, x, kDim * sizeof(float));
+    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.first, h->stream));
+    h->launches += found->second.second;
+    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    if (h->pin->status) {
+        return check_status(h);  // reads, clears and reports the device status word
     }
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(out, h->d_y, kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+    std::memcpy(out, h->pin->y, kDim * sizeof(float));
     if (top4_idx) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                                        h->stream));
+        std::memcpy(top4_idx, h->pin->idx, 4 * sizeof(int32_t));
     }
     if (top4_w) {
-        TTL_TRY_CUDA(h, cudaMemcpyAsync(top4_w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
+        std::memcpy(top4_w, h->pin->w, 4 * sizeof(float));
     }
-    return sync_and_check(h);
+    return TTL_OK;
 }
 
 int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, float *out, int32_t *top4_idx,
