@@ -277,6 +277,61 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
     }
 
 
+# Algorithmic bytes of one gpt-oss-120b decode token-layer (E = 128): router W
+# + bias, 12 expert matrices + their biases, x / out.
+LAYER_BYTES_120B = 128 * DIM * 4 + 128 * 4 + 12 * GGUF_MATRIX + 12 * BIAS + 2 * DIM * 4
+
+
+def decode_cfg3(torch, ttl_moe, synth, local, world, rank, dist, tokens=64, steps=3):
+    """gpt-oss-120b 36-layer MoE stack (128 experts,
+    seeded synthetic weights, 61 GB packed), decode T = 1 for `tokens`
+    sequential tokens, experts sharded E/N per rank with the in-kernel
+    exchange of partial outputs.  CUDA events on the library's stream around
+    `steps` forward launches, max over ranks."""
+    from ttl_moe import parallel
+    E, layers = 128, 36
+    nid = None
+    if world > 1:
+        nid = parallel.share_bytes(dist, ttl_moe.nccl_id() if rank == 0 else None, ttl_moe.NCCL_ID_BYTES,
+                                   device="cuda")
+    with ttl_moe.MoE(experts=E, layers=layers, max_tokens=0, device=local, rank=rank, world=world,
+                     nccl_id_bytes=nid) as m:
+        for l in range(layers):
+            t = synth.layer_device(3, l, E, device="cuda")
+            m.upload_layer(l, t)
+            del t
+        torch.cuda.empty_cache()
+        x = torch.from_numpy(synth.inputs_host(3, tokens)).cuda()
+        y = torch.empty_like(x)
+        st = torch.cuda.ExternalStream(m.stream())
+        for _ in range(2):
+            m.forward_async(0, layers, x, y, tokens)
+        m.sync()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            m.forward_async(0, layers, x, y, tokens)
+        e1.record(st)
+        e1.synchronize()
+        m.sync()
+        ms = e0.elapsed_time(e1) / steps
+        persistent = m.counters()["persistent_decode"]
+    if dist:
+        ms = parallel.max_over_ranks(dist, [ms], device="cuda")[0]
+    tps = tokens / (ms * 1e-3)
+    return {"workload": f"cfg3: gpt-oss-120b 36-layer MoE stack, decode T=1, {tokens} sequential tokens, "
+                        f"experts sharded 128/{world} per GPU",
+            "tokens_per_s": tps, "ms_per_step": ms, "n_gpus": world, "persistent_kernel": bool(persistent),
+            "algorithmic_gbs": tps * layers * LAYER_BYTES_120B / 1e9,
+            "bytes_per_token_layer": LAYER_BYTES_120B,
+            "timing": f"CUDA events on the library stream around {steps} launches of {tokens} tokens x {layers} "
+                      "layers, max over ranks"}
+
+
 def prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist, iters=10):
     """one gpt-oss-120b layer (128 experts), prefill
     of T = 2048 tokens with Zipf(1.2)-skewed routing, expert-parallel over the
@@ -334,6 +389,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-120b", action="store_true", help="skip the cfg3 (120b, 36-layer) decode line")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the cfg2 prefill measurement (one JSON line with its figures)")
     args = ap.parse_args()
@@ -472,6 +528,11 @@ def main():
             prefill = prefill_cfg2(torch, ttl_moe, synth, local,
                                    cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
         prefill_ep = prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist)
+    decode_120b = None
+    if not args.no_120b:
+        moe.close()
+        torch.cuda.empty_cache()
+        decode_120b = decode_cfg3(torch, ttl_moe, synth, local, world, rank, dist)
 
     if rank == 0:
         cpu = None
@@ -530,6 +591,7 @@ def main():
                                     "blocking call on host buffers, wall clock, max over ranks"},
             "prefill": prefill,
             "prefill_ep": prefill_ep,
+            "decode_120b": decode_120b,
         }
         print(json.dumps(line))
     moe.close()
