@@ -766,6 +766,19 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
         return;
     }
     const int row = 128 * tile + i;
+    if (next_router) {
+        // the next layer's router weights of this tile's rows for the experts
+        // past kPreE (loaded by the reducer after the exchange, when the sums
+        // are on the step's critical path) go to L2 now: one bulk prefetch of
+        // the tile's row slice per expert
+        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
+        const uint32_t bytes = uint32_t(min(128, kDim - 128 * tile)) * 4u;
+        for (int e = kPreE + i; e < a.experts; e += 32 * kEpiWarps) {
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(N.router_w + size_t(e) * kDim + 128 * tile),
+                         "r"(bytes)
+                         : "memory");
+        }
+    }
     if (row >= kDim) {
         return;
     }
