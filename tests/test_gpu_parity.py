@@ -164,6 +164,22 @@ def test_forward_stack_matches_reference(ttl):
         assert_close(y[k], r[k])
 
 
+def test_forward_stack_120b_matches_reference(ttl):
+    """gpt-oss-120b shapes (128 experts): RMSNorm -> MoE -> residual over 2
+    layers for 2 tokens; the down reducers stage the next layer's router
+    weights past the first 32 experts through shared memory."""
+    from ttl_moe import synth
+    layers = [synth_layer(70 + l, 128, layer=l, norm=True) for l in range(2)]
+    x = synth.inputs_host(71, 2)
+    with ttl.MoE(experts=128, layers=2, device=0) as m:
+        for l, t in enumerate(layers):
+            m.upload_layer(l, t)
+        y = m.forward(0, 2, x)
+    r = oracle.forward(layers, x, impl=impl())
+    for k in range(2):
+        assert_close(y[k], r[k])
+
+
 def test_forward_graph_replay_with_new_inputs(ttl):
     """The second forward call on the same buffers replays the captured graph;
     with new inputs its outputs must follow them (the split-K partials carry

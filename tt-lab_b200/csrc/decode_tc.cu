@@ -153,6 +153,8 @@ struct alignas(1024) Smem {
     uint64_t acc_empty[2];
     uint64_t sel_full;            // the step's selection is published
     uint64_t setup;               // the down B operands of the step landed
+    uint64_t rwbar;               // a down reducer's staged router weights landed
+    uint32_t rw_uses;             // stagings so far (its parity), written by thread 0 only
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier / end-of-step verdict, written by thread 0 only
@@ -742,6 +744,7 @@ struct TileOps {
     float rw[kPreE];       // down: next layer's router weights of this row
 };
 
+template <bool kWideRouter>
 __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int tile, int t_token, int li, bool next_router,
                                               TileOps &o) {
     const Smem &s = *c.s;
@@ -766,7 +769,7 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
         return;
     }
     const int row = 128 * tile + i;
-    if (next_router) {
+    if (kWideRouter && next_router) {
         // the next layer's router weights of this tile's rows for the experts
         // past kPreE (loaded by the reducer after the exchange, when the sums
         // are on the step's critical path) go to L2 now: one bulk prefetch of
@@ -814,6 +817,7 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
 // The tile's epilogue proper (reducer only): gate/up -> SwiGLU, routing
 // weight and the digit terms of the down projection's input; down -> bias,
 // residual, output rows and the next layer's router sums.
+template <bool kWideRouter>
 __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, const TileOps &o, float pg, float pu,
                             int t_token, int li, bool next_router) {
     Smem &s = *c.s;
@@ -827,6 +831,21 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const int tile = et.tile;
     const int step = t_token * nl + li;
     const uint32_t tag = step_tag(s, step);
+    // down with the next router: the router weights of this tile's rows for
+    // the experts past kPreE (warm in L2 from load_tile_ops) go into the stage
+    // ring, idle until this CTA publishes the next selection, one bulk copy per
+    // expert, while the partials below are summed
+    const bool stage_rw = kWideRouter && p.kind == 1 && next_router;
+    const uint32_t rw_parity = kWideRouter ? (s.rw_uses & 1u) : 0u;
+    if (stage_rw && i == 0) {
+        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
+        const uint32_t rb = uint32_t(min(128, kDim - 128 * tile)) * 4u;
+        tc::mbar_expect_tx(&s.rwbar, uint32_t(E - kPreE) * rb);
+        float *dst = reinterpret_cast<float *>(&s.a[0][0][0][0]);
+        for (int e = kPreE; e < E; ++e) {
+            bulk_load(dst + size_t(e - kPreE) * 128, N.router_w + size_t(e) * kDim + 128 * tile, rb, &s.rwbar);
+        }
+    }
     if (et.nslot > 1) {
         // the other contributors' tagged partials (after an abort the sums
         // are garbage; every later wait returns at once)
@@ -877,7 +896,6 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     if (next_router) {
         // router sums of the next (token, layer) over these rows: per warp,
         // f32 products transposed-summed over the 32 rows (f64 from there on)
-        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const float xr = more_layers ? yv : o.xnext;
         const float xg = __fmul_rn(xr, o.nw);  // 0 past the last row
         for (int b = 0; 16 * b < E; ++b) {
@@ -887,11 +905,19 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
                 for (int j = 0; j < 16; ++j) {
                     v[j] = __fmul_rn(b == 0 ? o.rw[j] : o.rw[16 + j], xg);
                 }
-            } else {
+            } else if (kWideRouter) {
+                if (b == kPreE / 16) {
+                    // every thread waits for the staged weights (bounded, and
+                    // not cut short by an abort: no copy is in flight at exit)
+                    if (!tc::mbar_wait(&s.rwbar, rw_parity)) {
+                        fail_wait(s, a.status);
+                    }
+                }
+                const float *rws = reinterpret_cast<const float *>(&s.a[0][0][0][0]);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int e = 16 * b + j;
-                    v[j] = (e < E && row < kDim) ? __fmul_rn(__ldg(N.router_w + size_t(e) * kDim + row), xg) : 0.0f;
+                    v[j] = (e < E && row < kDim) ? __fmul_rn(rws[size_t(e - kPreE) * 128 + i], xg) : 0.0f;
                 }
             }
             const float tot = transpose_sum16(v, lane);
@@ -904,7 +930,14 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         if (lane == 0) {
             s.rsum[w][E] = sq;
         }
+        if (stage_rw) {
+            // the ring's next writers are bulk copies and TMA loads
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
         epi_sync();
+        if (stage_rw && i == 0) {
+            ++s.rw_uses;
+        }
         // this tile's router sums for the next step, counted first
         double *rp = a.rp + (size_t(step & 1) * kTiles + tile) * (kMaxExperts + 1);
         for (int e = i; e < E + 1; e += 32 * kEpiWarps) {
@@ -942,6 +975,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     }
 }
 
+template <bool kWideRouter>
 __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe &pp, int t_token, int li,
                              bool next_router) {
     Smem &s = *c.s;
@@ -960,7 +994,7 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
     const uint32_t tag = step_tag(s, step);
     TileOps ops;
     if (first_owned >= 0) {
-        load_tile_ops(c, p, first_owned, t_token, li, next_router, ops);
+        load_tile_ops<kWideRouter>(c, p, first_owned, t_token, li, next_router, ops);
     }
     EpiTile own[kOwnMax];
     int nown = 0;
@@ -1043,9 +1077,9 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
             break;
         }
         if (own[k].tile != first_owned) {
-            load_tile_ops(c, p, own[k].tile, t_token, li, next_router, ops);
+            load_tile_ops<kWideRouter>(c, p, own[k].tile, t_token, li, next_router, ops);
         }
-        finish_tile(c, p, own[k], ops, s.own_part[k][0][i], s.own_part[k][1][i], t_token, li, next_router);
+        finish_tile<kWideRouter>(c, p, own[k], ops, s.own_part[k][0][i], s.own_part[k][1][i], t_token, li, next_router);
         if (aborted(s)) {
             return;
         }
@@ -1054,12 +1088,12 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
         // no selected expert is this rank's (expert parallelism): CTA t still
         // reduces down tile t, with a zero partial, for the exchange and the
         // rows, router sums and B operand that follow it
-        load_tile_ops(c, p, int(blockIdx.x), t_token, li, next_router, ops);
+        load_tile_ops<kWideRouter>(c, p, int(blockIdx.x), t_token, li, next_router, ops);
         EpiTile et;
         et.tile = int(blockIdx.x);
         et.nslot = 1;
         et.slot = 0;
-        finish_tile(c, p, et, ops, 0.0f, 0.0f, t_token, li, next_router);
+        finish_tile<kWideRouter>(c, p, et, ops, 0.0f, 0.0f, t_token, li, next_router);
     }
 }
 
@@ -1341,6 +1375,10 @@ __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps,
     }
 }
 
+// kWideRouter: more experts than kPreE (gpt-oss-120b), whose next-layer router
+// weights the down reducers stage through shared memory; a separate
+// instantiation, so the 32-expert kernel carries none of it.
+template <bool kWideRouter>
 __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // aligned by offsetting the shared array itself, so that accesses through
@@ -1369,6 +1407,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         }
         tc::mbar_init(&s.sel_full, 1);
         tc::mbar_init(&s.setup, 1);
+        tc::mbar_init(&s.rwbar, 1);
+        s.rw_uses = 0;
         tc::mbar_init(&s.fin, kIssuers);
         tc::fence_mbar_init();
     }
@@ -1614,7 +1654,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 const Phase pb = gateup_phase(s.n_local);
                 const Plan &plb = s.plan[s.n_local][0];
                 if (warp < kEpiWarps) {
-                    run_epilogue(cx, pb, plb, pipe, t, li, false);
+                    run_epilogue<kWideRouter>(cx, pb, plb, pipe, t, li, false);
                 } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
                     run_mma(cx, plb, 0, pipe, warp - kIssuerWarp0);
                 }
@@ -1693,7 +1733,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 const Phase pc = down_phase(s.n_local);
                 const Plan &plc = s.plan[s.n_local][1];
                 if (warp < kEpiWarps) {
-                    run_epilogue(cx, pc, plc, pipe, t, li, next_router);
+                    run_epilogue<kWideRouter>(cx, pc, plc, pipe, t, li, next_router);
                 } else if (warp < kIssuerWarp0 + kIssuers && lane == 0) {
                     run_mma(cx, plc, 1, pipe, warp - kIssuerWarp0);
                 }
@@ -1742,7 +1782,10 @@ size_t decode_tc_smem_bytes() {
 }
 
 void configure_decode_tc() {
-    cudaFuncSetAttribute(decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(decode_tc_smem_bytes()));
+    cudaFuncSetAttribute(decode_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int(decode_tc_smem_bytes()));
+    cudaFuncSetAttribute(decode_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         int(decode_tc_smem_bytes()));
 }
 
 cudaError_t launch_decode_tc(const StackArgs &args, int sms, cudaStream_t stream) {
@@ -1756,7 +1799,8 @@ cudaError_t launch_decode_tc(const StackArgs &args, int sms, cudaStream_t stream
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_tc_kernel, args);
+    return args.experts > kPreE ? cudaLaunchKernelEx(&cfg, decode_tc_kernel<true>, args)
+                                : cudaLaunchKernelEx(&cfg, decode_tc_kernel<false>, args);
 }
 
 } // namespace ttl
