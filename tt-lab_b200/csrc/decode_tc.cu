@@ -58,9 +58,18 @@
 //               rows and (stack mode) the next step's B operand and router
 //               sums for them, then counts the tile.
 // Split-K partials travel as tagged words (value + step tag in one 8-byte
-// store), so a reducer polls the data itself.  Buffers alternate between
-// even and odd steps: a CTA starts step s + 2 only after every CTA has
-// contributed to step s + 1, so nothing of step s is still being read.
+// store), so a reducer polls the data itself; the tag base lives on the
+// device and advances per launch, so a replayed graph never matches an old
+// word.  Buffers alternate between even and odd steps: a CTA starts step
+// s + 2 only after every CTA has contributed to step s + 1, so nothing of
+// step s is still being read.
+//
+// Expert parallelism (world > 1): each rank runs this kernel over its own
+// experts; the down reducers exchange the ranks' partial output rows as
+// tagged words stored into each other's buffers over NVLink and add them in
+// rank order (exchange_row), so every rank continues with the same bits.
+// With more than 32 experts (decode_tc_kernel<true>) the down reducers stage
+// the next layer's router weights of their rows in the idle stage ring.
 // Every wait is bounded; on timeout the kernel records kStatusWaitTimeout,
 // drains its own copies and MMAs, frees its tensor memory and returns.
 #include <cuda_runtime.h>

@@ -2,10 +2,14 @@
 // prefill and layer-stack entry points of include/ttl_moe.h.
 //
 // One handle drives one GPU.  Expert parallelism (world > 1) runs one process
-// per GPU; each rank holds experts [rank*E/world, (rank+1)*E/world) and the
-// ranks combine their partial outputs with NCCL over NVLink.  The router is
-// replicated (it is 0.7% of a layer's bytes) so every rank derives the same
-// top-4 without an exchange.
+// per GPU; each rank holds experts [rank*E/world, (rank+1)*E/world).  The
+// router is replicated (it is 0.7% of a layer's bytes) so every rank derives
+// the same top-4 for the same token.  Decode: the ranks add their partial
+// outputs inside the persistent kernel, through exchange buffers they map from
+// each other's CUDA IPC handles (NVLink peer stores); per-layer kernels with
+// an NCCL all-reduce stand in when that mapping is unavailable.  Prefill: each
+// rank passes its own tokens, which go to their experts' owners and come back
+// as weighted rows (NCCL send/recv, prefill_ep.cu).
 #include <cuda.h>  // CUtensorMap types; the encoder is resolved through the runtime
 #include <cuda_runtime.h>
 #include <nccl.h>
