@@ -33,6 +33,8 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 ROOT = pathlib.Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tt-lab_b200" / "python"))
@@ -118,11 +120,10 @@ def cpu_reference_sample(experts, seconds, threads, seed=0):
     """tt-lab's own GptOssModel::moe on host cores for ~`seconds` on one
     seeded layer (423 MB of experts, far above the LLC) and a stream of
     seeded tokens.  Returns (token-layers per second, calls, elapsed, isa)."""
-    import numpy as np
     import oracle
-    from ttl_moe import synth
-    t = synth.layer_host(seed, 0, experts)
-    xs = synth.inputs_host(seed, 64)
+    from oracle import synth as osynth
+    t = osynth.layer_host(seed, 0, experts)
+    xs = osynth.inputs_host(seed, 64)
     out = np.empty(DIM, np.float32)
     R = oracle.ref()
     args = [t[n].ctypes.data for n in ("router_w", "router_b", "gate_w", "gate_b", "up_w", "up_b", "down_w",
@@ -146,39 +147,66 @@ def cpu_reference_sample(experts, seconds, threads, seed=0):
     return calls / el, calls, el, ("x86-64-v4" if R.tref_isa_v4() else "default")
 
 
+def cfg1_config(layers, tokens):
+    """The workload both arms name (identical dict in both JSON lines)."""
+    return {"workload": "cfg1: gpt-oss-20b 24-layer MoE stack, decode T=1, 256 sequential tokens",
+            "experts": 32, "layers": layers, "tokens_per_step": tokens,
+            "l2": "inputs larger than L2: 1.28 GB of expert weights streamed per token",
+            "weights": "MXFP4 (E2M1 + E8M0 per 32), f32 activations and accumulation"}
+
+
 def run_reference(args, world, rank):
-    """--impl reference: tt-lab's CPU MoE with all useful host threads."""
+    """--impl reference: tt-lab's own CPU decode path (GptOssModel::moe with
+    rms_norm and the residual, compiled from its sources into oracle/_ref) on
+    all host threads.  The 256 tokens are independent sequences, so the
+    threads run them side by side, one token per thread through all 24
+    layers (each token's arithmetic is the single-threaded reference's).  A
+    step is one such round: `threads` of the 256 tokens (a bounded sample of
+    the workload), timed as it runs.  Inputs come from the oracle's own
+    generator (the same seeded tensors as the GPU arm); the product library is
+    never loaded in this process."""
     layers, tokens = args.layers, args.tokens
     if rank != 0:
         return 0
     try:
         import oracle
+        from oracle import synth as osynth
         oracle.ref()
     except OSError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path not built: {e}"}))
         return 0
-    # the eight gate/up products of a token at once, then each expert's down
-    # (tt-lab's kernels compute whole matrices; that is all they can overlap)
-    threads = 8 if (os.cpu_count() or 1) >= 8 else min(4, os.cpu_count() or 1)
-    sample_s = max(2.0, 20.0 / max(1, args.steps + args.warmup))
-    vals = []
+    threads = max(1, os.cpu_count() or 1)
+    per_step = max(1, min(tokens, threads))
+    t0 = time.perf_counter()
+    weights = [osynth.layer_host(0, l, 32) for l in range(layers)]
+    x = osynth.inputs_host(0, tokens)
+    gen_s = time.perf_counter() - t0
+    times = []
     for i in range(args.warmup + args.steps):
-        rate, calls, el, isa = cpu_reference_sample(32, sample_s, threads, seed=0)
+        lo = (i * per_step) % tokens
+        idx = [(lo + j) % tokens for j in range(per_step)]
+        xs = np.ascontiguousarray(x[idx])
+        t1 = time.perf_counter()
+        oracle.forward_tokens(weights, xs, threads=threads)
+        dt = time.perf_counter() - t1
         if i >= args.warmup:
-            vals.append(rate / layers)  # token-layers/s -> tokens/s of the 24-layer stack
-    value = statistics.median(vals)
+            times.append(dt)
+    step_s = statistics.median(times)
+    value = per_step / step_s
+    isa = "x86-64-v4" if oracle.ref().tref_isa_v4() else "default"
     line = {
         "metric": "MoE decode tokens/s (gpt-oss-20b, 24 MoE layers, T=1)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": tokens / value * 1e3, "higher_is_better": True, "impl": "reference",
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg1: gpt-oss-20b 24-layer MoE stack, decode T=1, 256 sequential tokens",
-                   "experts": 32, "layers": layers, "tokens_per_step": tokens, "parallelism": "host threads"},
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "impl": "reference",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE.json cfg1 "
+        "distributions, the GPU arm's tensors)", "parallelism": f"{threads} host threads, one token each",
+        "config": cfg1_config(layers, tokens),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{sample_s:.1f}s per step of tt-lab's decode MoE kernels on one 423 MB layer "
-                                   f"(expert-parallel harness, {threads} threads: gate/up products in parallel, "
-                                   f"each down after its up; {isa} clone), "
-                                   f"tokens/s = calls/s / {layers} layers"},
+                         "sample": f"each step: {per_step} of the {tokens} tokens, one per host thread, through "
+                                   f"all {layers} layers with tt-lab's GptOssModel::moe + rms_norm + residual "
+                                   f"({isa} clone); median of {args.steps} timed steps ({step_s * 1e3:.0f} ms "
+                                   f"each) after {args.warmup} warm-up; inputs generated in {gen_s:.1f}s before "
+                                   "timing"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -504,8 +532,7 @@ def main():
     e2e_value = tokens * args.steps / e2e_s
     hbm_peak, peak_kind = peaks()
     if kms["persistent"]:
-        simt = os.environ.get("TTL_MOE_SIMT_DECODE") == "1"
-        kernel = "decode_stack_kernel" if simt else "decode_tc_kernel"
+        kernel = "decode_tc_kernel"
         bytes_launch = LAYER_BYTES_20B * kms["steps"]
     else:  # expert-parallel handles: the gate/up kernel of one layer
         kernel = "decode_gateup_kernel"
@@ -558,13 +585,8 @@ def main():
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded; BASELINE.json cfg1 distributions)",
-            "config": {
-                "workload": "cfg1: gpt-oss-20b 24-layer MoE stack, decode T=1, 256 sequential tokens",
-                "experts": experts, "layers": layers, "tokens_per_step": tokens,
-                "parallelism": f"ep{world}",
-                "l2": "inputs larger than L2: 1.28 GB of expert weights streamed per token",
-                "weights": "MXFP4 (E2M1 + E8M0 per 32), f32 activations and accumulation",
-            },
+            "parallelism": f"ep{world}",
+            "config": cfg1_config(layers, tokens),
             "hbm_gbs_step": LAYER_BYTES_20B * layers * value / 1e9,
             "roofline": {
                 "bound": "hbm",

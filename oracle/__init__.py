@@ -85,6 +85,8 @@ def ref():
         L.tref_moe_decode.argtypes = [sz] + [vp] * 12
         L.tref_moe_prefill.argtypes = [sz] + [vp] * 9 + [sz, vp, vp, vp]
         L.tref_moe_decode_threaded.argtypes = [sz] + [vp] * 10 + [i32]
+        L.tref_moe_layer_tokens.argtypes = [sz, vp, vp, vp, vp, sz, i32, vp, vp, vp]
+        L.tref_forward_tokens.argtypes = [sz, sz, vp, vp, vp, vp, sz, i32]
         _ref = L
     return _ref
 
@@ -158,6 +160,59 @@ def forward(layers, x, isa=ISA_V4, impl="port"):
             cur = (cur + out).astype(np.float32)
         x[t] = cur
     return x
+
+
+_TENSORS = ("router_w", "router_b", "gate_w", "gate_b", "up_w", "up_b", "down_w", "down_b")
+
+
+def _table(layers):
+    """Pointer table for the reference drivers: 8 tensor pointers per layer
+    (router_w, router_b, gate_w, gate_b, up_w, up_b, down_w, down_b)."""
+    arr = (ctypes.c_void_p * (8 * len(layers)))()
+    for l, t in enumerate(layers):
+        for k, n in enumerate(_TENSORS):
+            a = t[n]
+            if not (a.flags["C_CONTIGUOUS"] and a.dtype in (np.float32, np.uint8)):
+                raise ValueError(f"layer {l} tensor {n} must be contiguous f32 / u8")
+            arr[8 * l + k] = a.ctypes.data
+    return arr
+
+
+def moe_layer_tokens(t, x, norm_w=None, threads=None):
+    """One layer for many independent tokens through tt-lab's own code
+    (rms_norm + GptOssModel::moe + residual, src/model.cpp:590-594), on host
+    threads.  Returns (y [T,2880], idx [T,4], w [T,4], router logits [T,E])."""
+    import os
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, DIM)
+    T = x.shape[0]
+    E = t["router_b"].shape[0]
+    y = np.empty_like(x)
+    idx = np.empty((T, 4), np.int32)
+    w = np.empty((T, 4), np.float32)
+    logits = np.empty((T, E), np.float32)
+    g = None if norm_w is None else np.ascontiguousarray(norm_w, np.float32)
+    tab = _table([t])
+    n = threads or os.cpu_count() or 1
+    _ref_check(ref().tref_moe_layer_tokens(E, tab, _p(g), _p(x), _p(y), T, int(n), _p(idx), _p(w), _p(logits)))
+    return y, idx, w, logits
+
+
+def forward_tokens(layers, x, threads=None, norms=None):
+    """Token-major decode of independent tokens through all `layers` with
+    tt-lab's own code (one worker per host thread, each token as
+    GptOssModel::forward runs it, attention left out).  Returns y [T,2880]."""
+    import os
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, DIM)
+    T = x.shape[0]
+    E = layers[0]["router_b"].shape[0]
+    y = np.empty_like(x)
+    tab = _table(layers)
+    nptr = None
+    if norms is not None:
+        nptr = (ctypes.c_void_p * len(layers))(*[None if g is None else g.ctypes.data for g in norms])
+    n = threads or os.cpu_count() or 1
+    _ref_check(ref().tref_forward_tokens(E, len(layers), tab, nptr, _p(x), _p(y), T, int(n)))
+    return y
 
 
 def compare(a, b):

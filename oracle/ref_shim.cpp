@@ -17,6 +17,7 @@
 // (access checks do not apply to template arguments of an explicit
 // instantiation), which leaves the reference sources untouched.
 #include <algorithm>
+#include <atomic>
 #include <array>
 #include <cmath>
 #include <limits>
@@ -73,6 +74,9 @@ struct TagWeightsSeq {
 struct TagTensors {
     friend auto member(TagTensors);
 };
+struct TagRouter {
+    friend auto member(TagRouter);
+};
 
 } // namespace
 
@@ -84,6 +88,7 @@ template struct Expose<TagWeights, &GptOssModel::expert_weights_>;
 template struct Expose<TagIndicesSeq, &GptOssModel::expert_indices_sequence_>;
 template struct Expose<TagWeightsSeq, &GptOssModel::expert_weights_sequence_>;
 template struct Expose<TagTensors, &GgufFile::tensors_>;
+template struct Expose<TagRouter, &GptOssModel::router_>;
 
 namespace {
 
@@ -142,13 +147,14 @@ uint64_t def_bytes(const TensorDef &t) {
     }
 }
 
-// Writes the metadata-only gpt-oss GGUF for `experts` experts and 24 layers.
-std::string write_fixture(size_t experts) {
+// Writes the metadata-only gpt-oss GGUF for `experts` experts and `layers`
+// layers (24 or 36, the two counts GptOssModel accepts, src/model.cpp:71-74).
+std::string write_fixture(size_t experts, size_t layers = 24) {
     std::vector<TensorDef> defs;
     defs.push_back({"token_embd.weight", {kDim, 201088}, tensor_q8_0});
     defs.push_back({"output_norm.weight", {kDim}, tensor_f32});
     defs.push_back({"output.weight", {kDim, 201088}, tensor_q8_0});
-    for (int i = 0; i < 24; ++i) {
+    for (size_t i = 0; i < layers; ++i) {
         const std::string p = "blk." + std::to_string(i) + ".";
         defs.push_back({p + "attn_norm.weight", {kDim}, tensor_f32});
         defs.push_back({p + "post_attention_norm.weight", {kDim}, tensor_f32});
@@ -173,7 +179,7 @@ std::string write_fixture(size_t experts) {
 
     std::string meta;
     key_str(meta, "general.architecture", "gpt-oss");
-    key_u32(meta, "gpt-oss.block_count", 24);
+    key_u32(meta, "gpt-oss.block_count", uint32_t(layers));
     key_u32(meta, "gpt-oss.context_length", 131072);
     key_u32(meta, "gpt-oss.embedding_length", kDim);
     key_u32(meta, "gpt-oss.feed_forward_length", kDim);
@@ -314,6 +320,74 @@ GgufTensor view(const void *data, std::vector<uint64_t> shape, uint32_t type) {
     t.offset = 0;
     t.data = (const std::byte *)data;
     return t;
+}
+
+// A model of its own for one worker thread (GptOssModel keeps its scratch in
+// members, so threads never share one): `layers` layers, room for one token.
+std::unique_ptr<RefModel> make_model(size_t experts, size_t layers) {
+    auto m = std::make_unique<RefModel>();
+    m->experts = experts;
+    m->capacity = 1;
+    m->path = write_fixture(experts, layers);
+    m->file = std::make_unique<GgufFile>(m->path.c_str());
+    m->model = std::make_unique<GptOssModel>(*m->file, 1, std::string(), 1);
+    return m;
+}
+
+// Aims layer l's MoE tensors at a caller's buffers: eight pointers in the
+// order router_w, router_b, gate_w, gate_b, up_w, up_b, down_w, down_b.
+void bind_layer(RefModel &m, size_t l, const void *const *p) {
+    GgufFile &f = *m.file;
+    const std::string b = "blk." + std::to_string(l) + ".";
+    static const char *const names[8] = {"ffn_gate_inp.weight", "ffn_gate_inp.bias", "ffn_gate_exps.weight",
+                                         "ffn_gate_exps.bias",  "ffn_up_exps.weight", "ffn_up_exps.bias",
+                                         "ffn_down_exps.weight", "ffn_down_exps.bias"};
+    for (int k = 0; k < 8; ++k) {
+        find_tensor(f, b + names[k])->data = (const std::byte *)p[k];
+    }
+}
+
+// One (token, layer) step of GptOssModel::forward without the attention block
+// (src/model.cpp:590-594): normalized = rms_norm(x, norm), out = moe(layer l,
+// normalized), y = x + out; the router logits stay in the model (router_).
+void forward_step(GptOssModel &model, size_t l, const float *norm_w, const float *ones, const float *x, float *y,
+                  float *normalized, float *out) {
+    const GgufTensor g = view(norm_w ? norm_w : ones, {kDim}, tensor_f32);
+    rms_norm(x, g, 1.0e-5f, normalized);
+    auto &layers = model.*member(TagLayers{});
+    (model.*member(TagMoe{}))(layers[l], normalized, out, l, 0);
+    for (size_t j = 0; j < kDim; ++j) {
+        y[j] = x[j] + out[j];
+    }
+}
+
+// Runs body(worker, model) on `threads` threads, each with its own model;
+// rethrows the first failure.
+template <class F> void run_workers(size_t experts, size_t layers, int threads, F &&body) {
+    const int n = std::max(1, threads);
+    std::vector<std::unique_ptr<RefModel>> models;
+    for (int i = 0; i < n; ++i) {
+        models.push_back(make_model(experts, layers));
+    }
+    std::vector<std::string> errors(static_cast<size_t>(n));
+    std::vector<std::thread> pool;
+    for (int i = 0; i < n; ++i) {
+        pool.emplace_back([&, i] {
+            try {
+                body(i, *models[size_t(i)]);
+            } catch (const std::exception &e) {
+                errors[size_t(i)] = e.what();
+            }
+        });
+    }
+    for (std::thread &t : pool) {
+        t.join();
+    }
+    for (const std::string &e : errors) {
+        if (!e.empty()) {
+            throw std::runtime_error(e);
+        }
+    }
 }
 
 } // namespace
@@ -562,6 +636,79 @@ int tref_moe_decode_threaded(size_t experts, const float *router_w, const float 
                 out[i] += weights[sel] * down[sel * kDim + i];
             }
         }
+    });
+}
+
+// One layer for many tokens (the parity tests' checker): for each token t,
+// y[t] = x[t] + moe(rms_norm(x[t], norm_w)) with tt-lab's own rms_norm and
+// GptOssModel::moe, on `threads` host threads (each token's arithmetic is the
+// single-threaded reference's).  layer: the eight tensor pointers of
+// bind_layer; norm_w NULL = ones.  idx/w [T][4] and logits [T][E] optional.
+int tref_moe_layer_tokens(size_t experts, const void *const *layer, const float *norm_w, const float *x, float *y,
+                          size_t tokens, int threads, int32_t *idx, float *w, float *logits) {
+    return guarded([&] {
+        const std::vector<float> ones(kDim, 1.0f);
+        std::atomic<size_t> next{0};
+        run_workers(experts, 24, int(std::min<size_t>(size_t(std::max(threads, 1)), std::max<size_t>(tokens, 1))),
+                    [&](int, RefModel &m) {
+                        bind_layer(m, 0, layer);
+                        GptOssModel &model = *m.model;
+                        std::vector<float> normalized(kDim), out(kDim);
+                        for (size_t t = next++; t < tokens; t = next++) {
+                            forward_step(model, 0, norm_w, ones.data(), x + t * kDim, y + t * kDim,
+                                         normalized.data(), out.data());
+                            const auto &indices = model.*member(TagIndices{});
+                            const auto &weights = model.*member(TagWeights{});
+                            const auto &router = model.*member(TagRouter{});
+                            for (size_t i = 0; i < 4; ++i) {
+                                if (idx) {
+                                    idx[t * 4 + i] = int32_t(indices[i]);
+                                }
+                                if (w) {
+                                    w[t * 4 + i] = weights[i];
+                                }
+                            }
+                            if (logits) {
+                                std::copy(router.begin(), router.begin() + experts, logits + t * experts);
+                            }
+                        }
+                    });
+    });
+}
+
+// Token-major decode of independent tokens, as GptOssModel::forward runs one
+// token through every layer (src/model.cpp:574-597, attention left out): each
+// of `threads` workers takes the next token and runs it through layers
+// [0, layers).  tables: 8 tensor pointers per layer (bind_layer's order);
+// norms: one RMSNorm weight pointer per layer (NULL entries or a NULL array =
+// ones).  y may alias x.
+int tref_forward_tokens(size_t experts, size_t layers, const void *const *tables, const float *const *norms,
+                        const float *x, float *y, size_t tokens, int threads) {
+    return guarded([&] {
+        if (layers == 0 || layers > 36) {
+            throw std::runtime_error("layers must be in 1..36");
+        }
+        const std::vector<float> ones(kDim, 1.0f);
+        std::atomic<size_t> next{0};
+        const size_t fixture_layers = layers > 24 ? 36 : 24;
+        run_workers(experts, fixture_layers,
+                    int(std::min<size_t>(size_t(std::max(threads, 1)), std::max<size_t>(tokens, 1))),
+                    [&](int, RefModel &m) {
+                        for (size_t l = 0; l < layers; ++l) {
+                            bind_layer(m, l, tables + 8 * l);
+                        }
+                        GptOssModel &model = *m.model;
+                        std::vector<float> cur(kDim), nxt(kDim), normalized(kDim), out(kDim);
+                        for (size_t t = next++; t < tokens; t = next++) {
+                            std::copy(x + t * kDim, x + (t + 1) * kDim, cur.begin());
+                            for (size_t l = 0; l < layers; ++l) {
+                                forward_step(model, l, norms ? norms[l] : nullptr, ones.data(), cur.data(),
+                                             nxt.data(), normalized.data(), out.data());
+                                cur.swap(nxt);
+                            }
+                            std::copy(cur.begin(), cur.end(), y + t * kDim);
+                        }
+                    });
     });
 }
 

@@ -82,3 +82,20 @@ def test_zipf_shift_skews_routing():
     assert s.shape == (32,) and np.isclose(np.log(np.exp(s).sum()), 0.0, atol=1e-5)
     order = np.argsort(-s)
     assert len(set(order[:4])) == 4
+
+
+def test_oracle_generator_matches_library():
+    """The checker's own generator (oracle/synth_oracle.c) gives the library's
+    tensors bit for bit, so the CPU side never needs the product library."""
+    from oracle import synth as osynth
+    from ttl_moe import synth
+    a = osynth.layer_host(2, 3, 32, zipf_s=1.1, norm=True)
+    b = synth.layer_host(2, 3, 32, zipf_s=1.1, norm=True)
+    assert a.keys() == b.keys()
+    for k in a:
+        assert np.array_equal(a[k].view(np.uint8), b[k].view(np.uint8)), k
+    assert np.array_equal(osynth.inputs_host(5, 9).view(np.uint32), synth.inputs_host(5, 9).view(np.uint32))
+    # block ranges split over threads give the single-range bytes
+    one = osynth.mxfp4_host(300000, 7, 4, threads=1)
+    many = osynth.mxfp4_host(300000, 7, 4, threads=5)
+    assert np.array_equal(one, many)

@@ -59,7 +59,7 @@ void launch_add(const float *residual, const float *moe, float *out, int n, cuda
 void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream,
                  uint32_t *flags = nullptr);
 
-// ---- persistent decode (decode_stack.cu) ----
+// ---- persistent decode (decode_tc.cu) ----
 // A CUtensorMap, kept opaque here (128 bytes, 64-byte aligned).
 struct alignas(64) TmaDesc {
     unsigned long long w[16];
@@ -154,9 +154,6 @@ size_t decode_tc_smem_bytes();
 void configure_decode_tc();
 cudaError_t launch_decode_tc(const StackArgs &args, int sms, cudaStream_t stream);
 
-size_t stack_smem_bytes();
-void configure_stack_kernel();
-cudaError_t launch_decode_stack(const StackArgs &args, int sms, cudaStream_t stream);
 
 // ---- prefill ----
 struct PrefillWork {

@@ -88,7 +88,6 @@ struct ttl_moe {
     uint64_t launches = 0;
     ncclComm_t comm = nullptr;
     std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;  // exec, kernels per replay
-    bool use_graphs = true;
     // the blocking single-layer decode (ttl_moe_decode): pinned staging of its
     // input and outputs, and one captured graph per layer (copies in, the
     // persistent kernel, copies out with the status word)
@@ -105,8 +104,6 @@ struct ttl_moe {
     int profile_layers = 0;        // layers covered by the recorded events
     std::vector<cudaEvent_t> events;  // [layers][4]
     // persistent decode kernel
-    bool use_stack = true;
-    bool use_tc = true;               // tensor-core persistent kernel (else the CUDA-core one)
     unsigned long long *d_part_gu = nullptr;  // tagged tile partials, [2] x gate/up and down
     unsigned long long *d_part_dn = nullptr;
     double *d_rp = nullptr;           // router sums per down tile
@@ -260,7 +257,7 @@ int allreduce(ttl_moe *h, float *buf, size_t n) {
 // rank's exchange buffer is mapped on every rank (tensor-core kernel only);
 // otherwise decode runs per layer with an NCCL all-reduce.
 bool stack_path(const ttl_moe *h) {
-    return h->use_stack && (h->cfg.world == 1 || (h->use_tc && h->xch_ready));
+    return h->cfg.world == 1 || h->xch_ready;
 }
 
 // Exchange buffers for expert parallelism inside the persistent kernel: this
@@ -483,16 +480,12 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
     }
-    if (h->use_tc) {
-        for (int l = begin; l < end; ++l) {
-            if (!h->host_layers[size_t(l)].tma) {
-                return fail(h, TTL_ERR_STATE, "layer " + std::to_string(l) + " has no tensor maps");
-            }
+    for (int l = begin; l < end; ++l) {
+        if (!h->host_layers[size_t(l)].tma) {
+            return fail(h, TTL_ERR_STATE, "layer " + std::to_string(l) + " has no tensor maps");
         }
-        TTL_TRY_CUDA(h, launch_decode_tc(a, h->sms, h->stream));
-    } else {
-        TTL_TRY_CUDA(h, launch_decode_stack(a, h->sms, h->stream));
     }
+    TTL_TRY_CUDA(h, launch_decode_tc(a, h->sms, h->stream));
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[1], h->stream, cudaEventRecordExternal));
         h->stack_profiled = true;
@@ -795,12 +788,6 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     h->expert_count = int(c.experts / c.world);
     h->expert_begin = int(c.rank) * h->expert_count;
     h->layers.resize(c.layers);
-    const char *no_graph = std::getenv("TTL_MOE_NO_GRAPHS");
-    h->use_graphs = !(no_graph && no_graph[0] == '1');
-    const char *no_stack = std::getenv("TTL_MOE_NO_STACK");
-    h->use_stack = !(no_stack && no_stack[0] == '1');
-    const char *simt = std::getenv("TTL_MOE_SIMT_DECODE");
-    h->use_tc = !(simt && simt[0] == '1');
     h->host_layers.resize(c.layers);
 
     auto bail = [&](int rc) {
@@ -818,7 +805,6 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     configure_decode_kernels();
     configure_prefill_kernels();
     configure_prefill_tc();
-    configure_stack_kernel();
     configure_decode_tc();
     if (cudaEventCreate(&h->stack_ev[0]) != cudaSuccess || cudaEventCreate(&h->stack_ev[1]) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "cudaEventCreate failed"));
@@ -940,11 +926,9 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
             h->comm = nullptr;
             return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + api->GetErrorString(r)));
         }
-        if (h->use_stack && h->use_tc) {
-            const int xrc = setup_exchange(h);
-            if (xrc) {
-                return bail(xrc);
-            }
+        const int xrc = setup_exchange(h);
+        if (xrc) {
+            return bail(xrc);
         }
     }
     *handle_out = h;
@@ -1125,7 +1109,7 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
     if (rc) {
         return rc;
     }
-    if (!stack_path(h) || !h->use_graphs) {
+    if (!stack_path(h)) {
         TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
         rc = stack_path(h) ? enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0)
                            : enqueue_decode_layer(h, layer, h->d_x, 0, nullptr, h->d_y);
@@ -1279,9 +1263,6 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
     }
     if (rc || tokens == 0) {
         return rc;
-    }
-    if (!h->use_graphs) {
-        return enqueue_forward(h, layer_begin, layer_end, x, y, tokens);
     }
     // The token loop is captured once per (buffers, count, layers) and replayed.
     const GraphKey key{x, y, tokens, layer_begin, layer_end};

@@ -174,6 +174,20 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, int x, 
         : "memory");
 }
 
+// Prefetch of one box of `tmap` at (x, y, z) into L2 (no shared-memory
+// destination, no barrier).  No multicast.
+__device__ __forceinline__ void tma_prefetch_3d(const void *tmap, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap), "r"(x), "r"(y),
+                 "r"(z)
+                 : "memory");
+}
+
+// Prefetch of `bytes` contiguous bytes at `src` into L2 (16-byte aligned
+// address, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 policy for data read once: its lines are the first to be evicted.
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t pol;
