@@ -213,6 +213,45 @@ def run_reference(args, world, rank):
     return 0
 
 
+def decode_parity_sample(torch, moe, synth, x_host, y_timed, layers, tokens=16, seed=0):
+    """Parity of the headline launch on a sample, after the timed region: the
+    first `tokens` of the 256 tokens go through the same forward launch again
+    with the step log on (their outputs must equal the timed run's bit for
+    bit: the kernel is deterministic and tokens are independent), and each of
+    their tokens x layers steps is replayed through tt-lab's compiled CPU code
+    on the GPU's own input for it (oracle/parity.py)."""
+    import oracle
+    from oracle import parity
+    steps = tokens * layers
+    ylog = torch.empty((steps, DIM), dtype=torch.float32, device="cuda")
+    ilog = torch.empty((steps, 4), dtype=torch.int32, device="cuda")
+    wlog = torch.empty((steps, 4), dtype=torch.float32, device="cuda")
+    moe.record(steps, ylog, ilog, wlog)
+    xs = torch.from_numpy(np.ascontiguousarray(x_host[:tokens])).cuda()
+    ys = torch.empty_like(xs)
+    moe.forward_async(0, layers, xs, ys, tokens)
+    moe.sync()
+    moe.record(0)
+    same = bool(torch.equal(ys, y_timed[:tokens]))
+    yl = ylog.cpu().numpy().reshape(tokens, layers, DIM)
+    il = ilog.cpu().numpy().reshape(tokens, layers, 4)
+    wl = wlog.cpu().numpy().reshape(tokens, layers, 4)
+
+    def layer_iter():
+        for l in range(layers):
+            t = synth.layer_device(seed, l, 32, device="cuda")
+            yield l, {k: v.cpu().numpy() for k, v in t.items()}
+
+    t0 = time.perf_counter()
+    s = parity.teacher_forced(layer_iter(), x_host[:tokens], yl, il, wl)
+    return {"passed": parity.passed(s) and same, "steps": s["steps"], "max_rel": s["max_rel"],
+            "max_rel_bar": parity.TOL, "top4_mismatches": s["mismatches"], "near_ties": s["near_ties"],
+            "top4_weights_max_rel": s["max_w_rel"], "identical_to_timed_run": same,
+            "sample": f"tokens 0-{tokens - 1} of the 256 x all {layers} layers ({steps} steps), each step replayed "
+                      "through tt-lab's compiled rms_norm + GptOssModel::moe + residual (oracle/_ref) on the "
+                      f"GPU's own input for it; checked in {time.perf_counter() - t0:.1f}s after the timed region"}
+
+
 # Dense FP4 tensor-core peak of one B200 (nominal; MEASURED_PEAKS.json has no FP4 figure).
 FP4_PEAK_TFLOPS = 9000.0
 PREFILL_DIGITS = 6      # radix-8 digit rows per activation (B operand of the prefill MMAs)
@@ -266,7 +305,7 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
         e1.synchronize()
         m.sync()
         ms = e0.elapsed_time(e1) / iters
-        _, idx, _ = m.moe_batch(0, xh)
+        pout, idx, _ = m.moe_batch(0, xh)
         x_pin = torch.from_numpy(xh).pin_memory()
         o_pin = torch.empty_like(x_pin).pin_memory()
         i_pin = torch.empty((T, 4), dtype=torch.int32).pin_memory()
@@ -284,6 +323,21 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
                    "sample": f"GptOssModel::moe_batch on the first {n} cfg2 tokens ({el:.1f}s, 1 thread, {isa} clone)"}
         except Exception as e:  # the reference build is optional on the box
             cpu = {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {e}"}
+    parity = None
+    try:
+        import oracle
+        th = synth.layer_host(2, 0, E, zipf_s=1.1)
+        t0 = time.perf_counter()
+        rout, ridx, _ = oracle.moe_prefill(th, xh, impl="ref")
+        bad = int(np.count_nonzero(np.any(np.asarray(idx) != ridx, axis=1)))
+        good = np.all(np.asarray(idx) == ridx, axis=1)
+        mm = oracle.compare(pout[good], rout[good])
+        parity = {"passed": bad == 0 and mm["max_rel"] <= 1e-3, "tokens": T, "max_rel": mm["max_rel"],
+                  "top4_mismatches": bad,
+                  "sample": f"all {T} tokens against tt-lab's GptOssModel::moe_batch (oracle/_ref, 1 thread, "
+                            f"{time.perf_counter() - t0:.1f}s), after the timed region"}
+    except OSError as e:
+        parity = {"passed": None, "sample": f"unavailable: {e}"}
     counts = np.bincount(np.asarray(idx).ravel(), minlength=E)
     groups = int(sum((c + PREFILL_GROUP - 1) // PREFILL_GROUP for c in counts))
     rows = (DIM + 127) // 128 * 128
@@ -302,6 +356,7 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
         "reference_math_tflops": useful_flop / (ms * 1e-3) / 1e12,
         "tensor_pipe_source": "profiles/prefill_mma_cfg2_T512.md (ncu sm__pipe_tensor_cycles_active)",
         "cpu_baseline": cpu,
+        "parity": parity,
     }
 
 
@@ -417,6 +472,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity sample checked after timing")
     ap.add_argument("--no-120b", action="store_true", help="skip the cfg3 (120b, 36-layer) decode line")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the cfg2 prefill measurement (one JSON line with its figures)")
@@ -527,6 +583,13 @@ def main():
     if dist:
         ms, e2e_s = parallel.max_over_ranks(dist, [ms, e2e_s], device="cuda")
 
+    parity = None
+    if world == 1 and not args.no_parity:
+        try:
+            parity = decode_parity_sample(torch, moe, synth, x_host, y_dev, layers)
+        except OSError as e:  # the checker is not built on this machine
+            parity = {"passed": None, "sample": f"unavailable: {e}"}
+
     ms_step = ms / args.steps
     value = tokens / (ms_step / 1e3)
     e2e_value = tokens * args.steps / e2e_s
@@ -604,6 +667,7 @@ def main():
                 "token_layers_per_launch": kms["steps"],
             },
             "cpu_baseline": cpu,
+            "parity": parity,
             "clocks": clk,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": tokens * DIM * 4,
                     "d2h_bytes_per_step": tokens * DIM * 4},

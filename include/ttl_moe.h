@@ -22,9 +22,14 @@
  *   ttl_ttq_*             the TTQ container writer  src/requant.cpp:23-68,
  *                                                   :415-504; src/requant.h:31-52
  *
- * Memory: device buffers are allocated once in ttl_moe_create and
- * ttl_moe_upload_layer and freed in ttl_moe_destroy ("allocate dynamic memory at
- * startup only", tt-lab AGENTS.md).  Compute calls allocate nothing.
+ * Memory: device buffers, pinned host staging and the blocking decode's
+ * captured graphs are made in ttl_moe_create and ttl_moe_upload_layer and freed
+ * in ttl_moe_destroy ("allocate dynamic memory at startup only", tt-lab
+ * AGENTS.md).  The compute calls allocate nothing, with one exception: the
+ * first ttl_moe_forward / ttl_moe_forward_async call for a new (buffers, token
+ * count, layer range) captures and instantiates a CUDA graph for it (at most 16
+ * are kept, least recently used dropped).  The diagnostic calls
+ * (ttl_moe_profile, ttl_moe_trace, ttl_moe_record) recapture graphs.
  * Threading: one host thread per handle; calls on one handle are serialised on
  * the handle's CUDA stream.
  */
@@ -116,7 +121,8 @@ int ttl_moe_prefill(ttl_moe *handle, int layer, const float *x, size_t tokens, f
  * [layer_begin, layer_end): per layer h = RMSNorm(x) * norm_w, x = x + MoE(h)
  * (src/model.cpp:590-594 with the attention block left out).
  * x: HOST f32 [tokens][2880] residual inputs; y: HOST f32 [tokens][2880]
- * outputs (may alias x).  Blocking. */
+ * outputs (may alias x).  The tokens pass through device staging made at
+ * create (max(max_tokens, 256) rows) in chunks of that size.  Blocking. */
 int ttl_moe_forward(ttl_moe *handle, int layer_begin, int layer_end, const float *x, float *y, size_t tokens);
 
 /* Device-pointer forms of the three calls above: all pointers are device
@@ -165,6 +171,19 @@ int ttl_moe_profile(ttl_moe *handle, int enable);
  * over all CTAs.  With out != NULL, waits and copies steps*10 stamps. */
 int ttl_moe_trace(ttl_moe *handle, int steps, uint64_t *out);
 int ttl_moe_kernel_ms(ttl_moe *handle, float *ms, size_t n);
+
+/* Step log of the persistent decode kernel, for parity checks at full size:
+ * with steps > 0, later ttl_moe_forward* / ttl_moe_decode* calls write, for
+ * each (token, layer) step s = token * (layer_end - layer_begin) +
+ * (layer - layer_begin) below `steps`, the step's output row -- the layer
+ * output x + MoE(RMSNorm(x)) for forward, the MoE output for decode -- to
+ * y_log + 2880 s, and its top-4 experts (rank order) and their weights to
+ * idx_log + 4 s and w_log + 4 s.  Device memory of the handle's GPU, owned by
+ * the caller until the log is turned off (steps = 0).  Per-layer decode (an
+ * expert-parallel handle whose ranks could not map each other's buffers)
+ * writes no log.  Counterpart: tt-lab's --dump-tensors files "output" and
+ * "router" (src/model.cpp:294, :595, :614-645). */
+int ttl_moe_record(ttl_moe *handle, size_t steps, float *y_log, int32_t *idx_log, float *w_log);
 
 /* One expert matrix on the tensor cores: y = bias + W x, tt-lab's
  * matvec_add_mxfp4_2880 (src/tensor.cpp:239-304).  packed: one 2880 x 2880

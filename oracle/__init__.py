@@ -60,6 +60,7 @@ def port():
         L.oref_softmax4.argtypes = [vp, vp, vp]
         L.oref_swiglu.restype = ctypes.c_float
         L.oref_swiglu.argtypes = [ctypes.c_float, ctypes.c_float]
+        L.oref_matvec_add_f32.argtypes = [vp, vp, vp, vp, sz, sz]
         _port = L
     return _port
 
@@ -134,6 +135,19 @@ def moe_prefill(t, x, isa=ISA_V4, impl="port"):
                                           _p(t["gate_w"]), _p(t["gate_b"]), _p(t["up_w"]), _p(t["up_b"]),
                                           _p(t["down_w"]), _p(t["down_b"]), _p(x), T, _p(out), _p(idx), _p(w)))
     return out, idx, w
+
+
+def router_logits(t, x):
+    """tt-lab's router chain for each row of x (matvec_add_f32,
+    src/tensor.cpp:186-200: bias first, products rounded, added in column
+    order; the prefill's matmul_add_f32 keeps the same per-token order).
+    Returns [T, E]."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, DIM)
+    E = t["router_b"].shape[0]
+    out = np.empty((x.shape[0], E), np.float32)
+    for i in range(x.shape[0]):
+        port().oref_matvec_add_f32(_p(t["router_w"]), _p(t["router_b"]), _p(x[i]), _p(out[i]), E, DIM)
+    return out
 
 
 def rms_norm(x, g, eps=1.0e-5, impl="port"):

@@ -31,13 +31,14 @@
 // columns are the per-term partial products, summed in the epilogue.
 //
 // Per step (token x layer), with no grid barrier:
-//   A  select   Every CTA waits for the previous step's 23 down tiles to
-//               count their router sums out, adds them in tile order (so all
-//               CTAs get the same sums -- the RMSNorm scale is a scalar, so
-//               logit_e = b_e + s * sum_c W_ec g_c x_c splits over row slices),
-//               loads the B operand those tiles wrote (digit terms of x*g) and
-//               picks the same top 4.  The first step of a launch splits
-//               h = RMSNorm(x)*g itself.
+//   A  select   Every CTA polls the router sums the previous step's 23 down
+//               tiles published as tagged words, adds them in tile order (so
+//               all CTAs get the same sums -- the RMSNorm scale is a scalar, so
+//               logit_e = b_e + s * sum_c W_ec g_c x_c splits over row slices)
+//               and picks the same top 4; then it loads the B operand those
+//               tiles wrote (digit terms of x*g, counted separately: it is off
+//               the critical path, behind the first weight loads).  The first
+//               step of a launch splits h = RMSNorm(x)*g itself.
 //               Mode 0 (one plain MoE, h given) computes the logits in a
 //               router phase with an error bound instead and re-evaluates
 //               near-ties exactly in the reference's order, so its indices
@@ -54,11 +55,14 @@
 //               down projections accumulate into one tensor (the routing
 //               weights are already in B).  A CTA starts once the gate/up tiles
 //               of the expert slots it reads are all counted.  The last
-//               contributor adds sum_q w_q b_q, the residual, writes the output
-//               rows and (stack mode) the next step's B operand and router
-//               sums for them, then counts the tile.
-// Split-K partials travel as tagged words (value + step tag in one 8-byte
-// store), so a reducer polls the data itself; the tag base lives on the
+//               contributor adds sum_q w_q b_q, the residual, publishes the
+//               next step's router sums over its rows (tagged words), then
+//               writes the output rows and the next step's B operand and
+//               counts the tile.
+// Split-K partials and router sums travel as tagged words (value + step tag
+// in one 8-byte store), so the reader polls the data itself -- no fence on
+// the writer's side, and every poll round keeps all of a thread's missing
+// words in flight together (poll_tagged); the tag base lives on the
 // device and advances per launch, so a replayed graph never matches an old
 // word.  Buffers alternate between even and odd steps: a CTA starts step
 // s + 2 only after every CTA has contributed to step s + 1, so nothing of
@@ -237,27 +241,48 @@ __device__ __forceinline__ bool wait_bar(Smem &s, uint64_t *bar, uint32_t parity
     return true;
 }
 
-// The value of the tagged word at p once it carries `tag` (w: a first load of
-// it).  Bounded: after a timeout or an abort it returns 0 with the status set.
-__device__ __forceinline__ float wait_tagged_slow(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status) {
-    const unsigned long long t0 = tc::now_ns();
-    while (true) {
-        const unsigned long long w = ld_tagged(p);
-        if (uint32_t(w >> 32) == tag) {
-            return __uint_as_float(uint32_t(w));
+// Polls up to N tagged words until each carries `tag`.  Every round issues
+// the loads of all words still missing before checking any of them, so their
+// round trips to L2 overlap (a word-by-word wait would pay one per word).
+// addr(k) is word k's address, `miss` has bit k set for each word to fetch;
+// the f32 halves land in v[k].  Bounded: after a timeout or an abort the
+// missing values stay as they are, with the status set.
+template <int N, bool kSys = false, class F>
+__device__ __forceinline__ void poll_tagged(Smem &s, F addr, uint32_t miss, uint32_t tag, float (&v)[N],
+                                            uint32_t *status) {
+    unsigned long long t0 = 0ull;
+    while (miss != 0u) {
+        unsigned long long w[N];
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            if ((miss >> k) & 1u) {
+                if constexpr (kSys) {
+                    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w[k]) : "l"(addr(k)) : "memory");
+                } else {
+                    w[k] = ld_tagged(addr(k));
+                }
+            } else {
+                w[k] = 0ull;
+            }
         }
-        if (aborted(s)) {
-            return 0.0f;
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+            if (((miss >> k) & 1u) && uint32_t(w[k] >> 32) == tag) {
+                v[k] = __uint_as_float(uint32_t(w[k]));
+                miss &= ~(1u << k);
+            }
         }
-        if (tc::now_ns() - t0 > 2000000000ull) {
+        if (miss == 0u || aborted(s)) {
+            return;
+        }
+        const unsigned long long now = tc::now_ns();
+        if (t0 == 0ull) {
+            t0 = now;
+        } else if (now - t0 > kGridWaitNs) {
             fail_wait(s, status);
-            return 0.0f;
+            return;
         }
     }
-}
-__device__ __forceinline__ float wait_tagged(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status,
-                                             unsigned long long w) {
-    return (uint32_t(w >> 32) == tag) ? __uint_as_float(uint32_t(w)) : wait_tagged_slow(s, p, tag, status);
 }
 
 // ---- expert parallelism: the partial output rows of the ranks ----
@@ -266,28 +291,6 @@ __device__ __forceinline__ float wait_tagged(Smem &s, const unsigned long long *
 __device__ __forceinline__ void st_tagged_sys(unsigned long long *p, unsigned long long w) {
     asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_tagged_sys(const unsigned long long *p) {
-    unsigned long long w;
-    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    return w;
-}
-__device__ __forceinline__ float wait_tagged_sys(Smem &s, const unsigned long long *p, uint32_t tag, uint32_t *status) {
-    const unsigned long long t0 = tc::now_ns();
-    while (true) {
-        const unsigned long long w = ld_tagged_sys(p);
-        if (uint32_t(w >> 32) == tag) {
-            return __uint_as_float(uint32_t(w));
-        }
-        if (aborted(s)) {
-            return 0.0f;
-        }
-        if (tc::now_ns() - t0 > 2000000000ull) {
-            fail_wait(s, status);
-            return 0.0f;
-        }
-    }
-}
-
 // This rank's partial v of output row `row` (the sum over its own selected
 // experts) goes to slot [step parity][rank][row] of every other rank's
 // exchange buffer; the ranks' partials are then added in rank order, so every
@@ -302,10 +305,19 @@ __device__ __forceinline__ float exchange_row(Smem &s, const StackArgs &a, int s
         }
     }
     const unsigned long long *own = a.xch[a.rank] + par + row;
-    float tot = 0.0f;
-    for (int r = 0; r < a.world; ++r) {
-        const float pv = (r == a.rank) ? v : wait_tagged_sys(s, own + size_t(r) * kXchRow, tag, a.status);
-        tot = (r == 0) ? pv : __fadd_rn(tot, pv);
+    float pv[kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+        pv[r] = (r == a.rank) ? v : 0.0f;
+    }
+    const uint32_t others = ((1u << a.world) - 1u) & ~(1u << a.rank);
+    poll_tagged<kMaxWorld, true>(s, [&](int r) { return own + size_t(r) * kXchRow; }, others, tag, pv, a.status);
+    float tot = pv[0];
+#pragma unroll
+    for (int r = 1; r < kMaxWorld; ++r) {
+        if (r < a.world) {
+            tot = __fadd_rn(tot, pv[r]);
+        }
     }
     return tot;
 }
@@ -324,6 +336,12 @@ __device__ __forceinline__ void wait_count(Smem &s, const unsigned *p, unsigned 
             return;
         }
     }
+}
+
+// 4-byte asynchronous global -> shared copy (cp.async; any 4-byte aligned
+// source), completed by cp.async.wait_all of the issuing thread.
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
@@ -648,25 +666,27 @@ __device__ void build_plan(Plan &pl, const Phase &p, uint32_t *status) {
     pl.nseg = min(nseg, kPlanSegs);
 }
 
-// tagged_sum of the gate (p) and up (p + 128) partials together: the loads
-// of both go out at once, four contributors at a time.
+// tagged_sum of the gate (p) and up (p + 128) partials together: four
+// contributors (eight words) per batch, their polls in flight together.
 __device__ __forceinline__ void tagged_sum2(Smem &s, const unsigned long long *p, size_t stride, int nslot, float &g,
                                             float &u, uint32_t tag, uint32_t *status) {
     constexpr int kBatch = 4;
     float sg = 0.0f, su = 0.0f;
     for (int k0 = 0; k0 + 1 < nslot; k0 += kBatch) {
-        unsigned long long wg[kBatch], wu[kBatch];
+        float v[2 * kBatch];
+        uint32_t want = 0u;
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-            const bool in = k0 + j + 1 < nslot;
-            wg[j] = in ? ld_tagged(p + size_t(k0 + j) * stride) : 0ull;
-            wu[j] = in ? ld_tagged(p + 128 + size_t(k0 + j) * stride) : 0ull;
+            v[2 * j] = v[2 * j + 1] = 0.0f;
+            want |= (k0 + j + 1 < nslot) ? (3u << (2 * j)) : 0u;
         }
+        poll_tagged<2 * kBatch>(
+            s, [&](int k) { return p + size_t(k0 + (k >> 1)) * stride + 128 * (k & 1); }, want, tag, v, status);
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
             if (k0 + j + 1 < nslot) {
-                sg += wait_tagged(s, p + size_t(k0 + j) * stride, tag, status, wg[j]);
-                su += wait_tagged(s, p + 128 + size_t(k0 + j) * stride, tag, status, wu[j]);
+                sg += v[2 * j];
+                su += v[2 * j + 1];
             }
         }
     }
@@ -686,21 +706,24 @@ __device__ __forceinline__ unsigned long long *part_base(const StackArgs &a, con
 
 // Sum over the contributors in slot order; this CTA reduces the tile, so its
 // own partial `mine` is the last one.  p: this row's word of slot 0.
-// The loads of up to eight contributors go out together.
+// Eight contributors per batch, their polls in flight together.
 __device__ __forceinline__ float tagged_sum(Smem &s, const unsigned long long *p, size_t stride, int nslot, float mine,
                                             uint32_t tag, uint32_t *status) {
     constexpr int kBatch = 8;
     float sum = 0.0f;
     for (int k0 = 0; k0 + 1 < nslot; k0 += kBatch) {
-        unsigned long long w[kBatch];
+        float v[kBatch];
+        uint32_t want = 0u;
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-            w[j] = (k0 + j + 1 < nslot) ? ld_tagged(p + size_t(k0 + j) * stride) : 0ull;
+            v[j] = 0.0f;
+            want |= (k0 + j + 1 < nslot) ? (1u << j) : 0u;
         }
+        poll_tagged<kBatch>(s, [&](int k) { return p + size_t(k0 + k) * stride; }, want, tag, v, status);
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
             if (k0 + j + 1 < nslot) {
-                sum += wait_tagged(s, p + size_t(k0 + j) * stride, tag, status, w[j]);
+                sum += v[j];
             }
         }
     }
@@ -898,6 +921,9 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             out = exchange_row(s, a, step, row, out, tag);
         }
         yv = (a.mode == 1) ? __fadd_rn(o.resid, out) : out;
+        if (a.ylog && step < a.log_steps) {
+            a.ylog[size_t(step) * kDim + row] = yv;
+        }
     }
     if (!next_router && row < kDim) {
         a.y[size_t(t_token) * kDim + row] = yv;
@@ -947,19 +973,19 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         if (stage_rw && i == 0) {
             ++s.rw_uses;
         }
-        // this tile's router sums for the next step, counted first
-        double *rp = a.rp + (size_t(step & 1) * kTiles + tile) * (kMaxExperts + 1);
+        // this tile's router sums for the next step, first: each f64 as two
+        // tagged f32 words (hi, then the remainder) that every CTA polls
+        unsigned long long *rp = a.rpt + (size_t(step & 1) * kTiles + tile) * (kMaxExperts + 1) * 2;
         for (int e = i; e < E + 1; e += 32 * kEpiWarps) {
             double tot = 0.0;
 #pragma unroll
             for (int k = 0; k < kEpiWarps; ++k) {
                 tot += s.rsum[k][e];
             }
-            rp[e] = tot;
-        }
-        epi_sync();
-        if (i == 0) {
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_r) : "memory");
+            const float hi = __double2float_rn(tot);
+            const float lo = __double2float_rn(tot - double(hi));
+            st_tagged(rp + 2 * e, tagged(tag, hi));
+            st_tagged(rp + 2 * e + 1, tagged(tag, lo));
         }
         // then this tile's output rows and the next step's gate/up B operand
         // (digit terms of x * g; the RMSNorm scale is a scalar applied to the
@@ -977,9 +1003,9 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
                 a.bnext_code[size_t(step & 1) * (kBnextCodeBytes / 2) + kb] = uint8_t(code);
             }
         }
-        epi_sync();
+        epi_sync();  // also: s.rsum is read before this CTA's next tile rewrites it
         if (i == 0) {
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_r + 1) : "memory");
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.cnt_y) : "memory");
         }
     }
 }
@@ -1106,40 +1132,66 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
     }
 }
 
-// Stack mode, step > 0: the router sums of `step` and its gate/up B
-// operand, both written by the down reducers of the previous step.  Every
-// reducer counts its tile in a.cnt_r after writing them; thread 0 waits for
-// the count, then all loads go out together: the B operand (bytes and block
-// codes) into s.bgu / s.gcode, and thread e <= E sums expert e's 23 tile
-// partials in tile order (every CTA gets the same sums) into s.rsum[0][e].
-// Needs a compute_sync before any of it is read.
+// Stack mode, step > 0: the router sums of `step`, written by the down
+// reducers of the previous step as tagged words (two per f64).  The compute
+// threads share the (tile, expert) items -- a few each, their polls in flight
+// together -- and park the values in shared memory (the two B-operand areas,
+// idle between the previous step's last MMA and this step's operand copies);
+// then thread e <= E adds expert e's 23 tile partials in tile
+// order (every CTA gets the same sums) into s.rsum[0][e].  Called by every
+// compute thread; needs a compute_sync before s.rsum is read.
 __device__ __forceinline__ void gather_router_sums(Smem &s, const StackArgs &a, int step, int E) {
+    static_assert(offsetof(Smem, bdown) == offsetof(Smem, bgu) + sizeof(Smem::bgu) &&
+                      sizeof(Smem::bgu) + sizeof(Smem::bdown) >= sizeof(double) * kTiles * (kMaxExperts + 1),
+                  "router scratch: the two B-operand areas, adjacent");
+    constexpr int kItems = 6;
     const int ct = threadIdx.x;
-    if (ct == 0) {
-        wait_count(s, a.cnt_r, unsigned(kTiles) * unsigned(step), a.status);
+    const int per = E + 1;
+    const int items = kTiles * per;
+    const uint32_t tag = step_tag(s, step - 1);
+    const unsigned long long *rp = a.rpt + size_t((step - 1) & 1) * kTiles * (kMaxExperts + 1) * 2;
+    double *rs = reinterpret_cast<double *>(&s.bgu[0][0]);
+    for (int base = 0; base < items; base += kComputeThreads * kItems) {
+        float v[2 * kItems];
+        uint32_t want = 0u;
+#pragma unroll
+        for (int m = 0; m < kItems; ++m) {
+            v[2 * m] = v[2 * m + 1] = 0.0f;
+            want |= (base + ct + kComputeThreads * m < items) ? (3u << (2 * m)) : 0u;
+        }
+        poll_tagged<2 * kItems>(
+            s,
+            [&](int k) {
+                const int i = base + ct + kComputeThreads * (k >> 1);
+                const int t = i / per;
+                return rp + (size_t(t) * (kMaxExperts + 1) + size_t(i - t * per)) * 2 + (k & 1);
+            },
+            want, tag, v, a.status);
+#pragma unroll
+        for (int m = 0; m < kItems; ++m) {
+            const int i = base + ct + kComputeThreads * m;
+            if (i < items) {
+                rs[i] = double(v[2 * m]) + double(v[2 * m + 1]);
+            }
+        }
     }
     compute_sync();
-    const size_t par = size_t((step - 1) & 1);
     if (ct <= E) {
-        const double *rp = a.rp + par * kTiles * (kMaxExperts + 1) + ct;
-        double v[kTiles];
-#pragma unroll
-        for (int t = 0; t < kTiles; ++t) {
-            v[t] = __ldcg(rp + t * (kMaxExperts + 1));
-        }
         double sum = 0.0;
-#pragma unroll
         for (int t = 0; t < kTiles; ++t) {
-            sum += v[t];
+            sum += rs[t * per + ct];
         }
         s.rsum[0][ct] = sum;
     }
+    // the areas' next writers: the gate/up operand copy, then the down
+    // operand's bulk copies (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void gather_next_operand(Smem &s, const StackArgs &a, int step) {
     const int ct = threadIdx.x;
     if (ct == 0) {
-        wait_count(s, a.cnt_r + 1, unsigned(kTiles) * unsigned(step), a.status);
+        wait_count(s, a.cnt_y, unsigned(kTiles) * unsigned(step), a.status);
     }
     compute_sync();
     const size_t par = size_t((step - 1) & 1);
@@ -1284,13 +1336,15 @@ __device__ __forceinline__ void check_top4(Smem &s, int experts) {
     }
 }
 
-// B-operand scales of one operand's 24 chunks into tensor memory: chunk c at
-// columns 4c..4c+3, of which the MMA reads column 4c (lane n = row n of B,
-// byte k = K-block 4c + k); four chunks per store.  Warp-collective, this
-// warp's lane quadrant.
+// B-operand scales of one operand's chunks (kCols / 4 of them) into tensor
+// memory: chunk c at columns 4c..4c+3, of which the MMA reads column 4c (lane
+// n = row n of B, byte k = K-block 4c + k); four chunks per store.
+// Warp-collective, this warp's lane quadrant.
+template <uint32_t kCols = kSfbCols>
 __device__ __forceinline__ void store_sfb(const uint8_t *codes, uint32_t taddr, int lane) {
+    static_assert(kCols % 16 == 0, "whole stores");
 #pragma unroll
-    for (int g4 = 0; g4 < int(kSfbCols / 16); ++g4) {
+    for (int g4 = 0; g4 < int(kCols / 16); ++g4) {
         uint32_t v[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) {
@@ -1306,7 +1360,7 @@ __device__ __forceinline__ void store_sfb(const uint8_t *codes, uint32_t taddr, 
 // experts, by warp 0 (lane q handles selection q; the maximum and the sum
 // run in rank order as in the reference), then published to the load warp.
 // Called by all 32 lanes of warp 0 after s.sel is visible to them.
-__device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, bool export_top) {
+__device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, bool export_top, int step) {
     const int lane = threadIdx.x & 31;
     const int q = lane & 3;
     const int e = s.sel[q];
@@ -1339,6 +1393,10 @@ __device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, b
         if (export_top) {
             a.top_idx[q] = e;
             a.top_w[q] = __fdiv_rn(wq, sum);
+        }
+        if (a.ilog && blockIdx.x == 0 && step < a.log_steps) {
+            a.ilog[size_t(step) * kTopK + q] = e;
+            a.wlog[size_t(step) * kTopK + q] = __fdiv_rn(wq, sum);
         }
     }
     if (lane == 0) {
@@ -1483,19 +1541,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 // The gate/up B operand: digit terms of x * g (mode 1) or of h
                 // (mode 0).  From the second step of a stack on, the previous
                 // step's down epilogues have written it (a.bnext): one bulk
-                // copy.  Otherwise it is split here; its loads go out first
-                // (warp w takes K-blocks w + 9 i).
+                // copy.  Otherwise it is split here from x (and g) staged in
+                // shared memory by asynchronous copies issued now, before the
+                // selection (the down-operand area is idle in such a step);
+                // the split loop is not unrolled: it runs once per launch, so
+                // its code is fetched cold, and unrolled it would miss the
+                // instruction cache once per pass.
                 const bool split_here = (a.mode == 0) || (step == 0);
                 constexpr int kPasses = kBlocks / kComputeWarps;  // 10
                 static_assert(kPasses * kComputeWarps == kBlocks, "split passes");
-                float xr[kPasses], gr[kPasses];
+                static_assert(sizeof(Smem::bdown) >= 2 * kDim * sizeof(float), "split staging");
+                float *xs = reinterpret_cast<float *>(&s.bdown[0][0][0]);
+                float *gs = xs + kDim;
                 if (split_here) {
-#pragma unroll
-                    for (int pi = 0; pi < kPasses; ++pi) {
-                        const int k = (warp + pi * kComputeWarps) * 32 + lane;
-                        xr[pi] = __ldcg(xcur + k);
-                        gr[pi] = (a.mode == 1) ? __ldg(L.norm_w + k) : 1.0f;
+#pragma unroll 1
+                    for (int k = ct; k < kDim; k += kComputeThreads) {
+                        cp_async4(xs + k, xcur + k);
+                        if (a.mode == 1) {
+                            cp_async4(gs + k, L.norm_w + k);
+                        }
                     }
+                    asm volatile("cp.async.commit_group;" ::: "memory");
                 }
                 float scale = 1.0f;
                 // ---------------- A: selection ----------------
@@ -1522,7 +1588,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     if (warp == 0) {
                         warp_top4(s, E);
                         __syncwarp();
-                        publish_selection(s, a, export_top);
+                        publish_selection(s, a, export_top, step);
                     }
                 } else {
                     // CTA e < E: expert e's logit and the bound on the reference's f32 chain.
@@ -1628,7 +1694,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                         compute_sync();
                     }
                     if (warp == 0) {
-                        publish_selection(s, a, export_top);
+                        publish_selection(s, a, export_top, step);
                     }
                 }
                 stamp(a, step, 1);
@@ -1636,10 +1702,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     s.nscale = scale;
                 }
                 if (split_here) {
-#pragma unroll
+                    asm volatile("cp.async.wait_all;" ::: "memory");
+                    compute_sync();
+#pragma unroll 1
                     for (int pi = 0; pi < kPasses; ++pi) {
                         const int kb = warp + pi * kComputeWarps;
-                        const float h = (a.mode == 1) ? __fmul_rn(xr[pi], gr[pi]) : xr[pi];
+                        const int k = kb * 32 + lane;
+                        const float h = (a.mode == 1) ? __fmul_rn(xs[k], gs[k]) : xs[k];
                         const uint32_t code = tc::digit_split_store(h, &s.bgu[kb][0], lane);
                         if (lane == 0) {
                             s.gcode[kb] = uint8_t(code);

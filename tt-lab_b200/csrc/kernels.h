@@ -115,16 +115,24 @@ struct StackArgs {
                                    //     advances [0] by the launch's steps and clears [1])
     unsigned long long *part_gu;   // [2][4 * 23 tiles][16 slots][256] gate/up tile partials, tagged
     unsigned long long *part_dn;   // [2][23 tiles][16 slots][128] down tile partials, tagged
-    double *rp;                    // [2][23 tiles][129] next step's router sums per down tile
+    unsigned long long *rpt;       // [2][23 tiles][129][2] next step's router sums per down tile (the sum of
+                                   // squares at index E), each f64 as two tagged f32 words (hi, then lo)
     unsigned *cnt_b;               // [4] gate/up tiles reduced per expert slot (zeroed by the host)
-    unsigned *cnt_r;               // [2] down tiles whose router sums are written, and whose output rows and
-                                   // next B operand are (zeroed by the host)
+    unsigned *cnt_y;               // down tiles whose output rows and next B operand are written (zeroed
+                                   // by the host)
     uint8_t *bdown;                // [2][4][90 K-blocks][2][8][16] down B operand: digit terms of w * hidden
     uint8_t *sfb_down;             // [2][4][96] their block codes (90 + padding, 127)
     uint8_t *bnext;                // [2][90 K-blocks][2][8][16] next step's gate/up B operand: digit terms of x * g
     uint8_t *bnext_code;           // [2][96] their block codes (90 + padding, 127)
     unsigned long long *trace; // optional: [steps][kTracePoints] %globaltimer stamps of CTA 0 (+ CTA-max phase ends)
     int trace_steps;
+    // optional step log: step s < log_steps writes its output row (the layer
+    // output in mode 1, the MoE output in mode 0) to ylog[s][2880] and its
+    // top-4 (rank order) to ilog[s][4] / wlog[s][4]
+    float *ylog;
+    int32_t *ilog;
+    float *wlog;
+    int log_steps;
     // Expert parallelism inside the launch (world > 1): a device array of
     // every rank's exchange buffer as this GPU addresses it (its own, and the
     // peers' mapped over NVLink), each [2 step parities][world][kXchRow]
@@ -144,7 +152,7 @@ constexpr int kTracePoints = 10;
 // Sizes of the tensor-core decode workspace (StackArgs), in elements.
 constexpr size_t kPartGuWords = size_t(2) * 4 * 23 * 16 * 256;
 constexpr size_t kPartDnWords = size_t(2) * 23 * 16 * 128;
-constexpr size_t kRpWords = size_t(2) * 23 * 129;
+constexpr size_t kRptWords = size_t(2) * 23 * 129 * 2;
 constexpr size_t kBdownBytes = size_t(2) * 4 * 90 * 256;
 constexpr size_t kSfbDownBytes = size_t(2) * 4 * 96;
 constexpr size_t kBnextBytes = size_t(2) * 90 * 256;

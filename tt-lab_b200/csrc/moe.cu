@@ -51,6 +51,9 @@ struct LayerStore {
     float *down_b = nullptr;
 };
 
+constexpr size_t kMaxForwardGraphs = 16;       // captured forward graphs kept per handle
+constexpr size_t kForwardStagingTokens = 256;  // ttl_moe_forward's device rows (at least)
+
 struct GraphKey {
     const void *x;
     const void *y;
@@ -80,34 +83,47 @@ struct ttl_moe {
     PrefillWork pw{};
     float *d_x = nullptr;        // [max(1, max_tokens)][2880]
     float *d_y = nullptr;
-    float *d_fwd = nullptr;      // forward staging for host calls [fwd_cap][2880]
+    float *d_fwd = nullptr;      // forward staging for host calls [fwd_cap][2880], allocated at create
     size_t fwd_cap = 0;
     float *d_ones = nullptr;
     uint32_t *d_status = nullptr;
     unsigned long long *d_counters = nullptr;
     uint64_t launches = 0;
     ncclComm_t comm = nullptr;
-    std::map<GraphKey, std::pair<cudaGraphExec_t, uint64_t>> graphs;  // exec, kernels per replay
+    struct ForwardGraph {
+        cudaGraphExec_t exec;
+        uint64_t kernels;   // kernels per replay
+        uint64_t last_use;  // graph_clock of the last replay
+    };
+    std::map<GraphKey, ForwardGraph> graphs;  // at most kMaxForwardGraphs, least recently used evicted
+    uint64_t graph_clock = 0;
     // the blocking single-layer decode (ttl_moe_decode): pinned staging of its
     // input and outputs, and one captured graph per layer (copies in, the
     // persistent kernel, copies out with the status word)
-    struct DecodePin {
-        float x[kDim];
+    // (the device copy of DecodeBlock holds the handle's status word, so one
+    // copy brings back the output, the top-4 and the status)
+    struct DecodeBlock {
         float y[kDim];
         int32_t idx[4];
         float w[4];
         uint32_t status;
+        uint32_t pad[3];
     };
-    DecodePin *pin = nullptr;
-    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> decode_graphs;
+    struct DecodePin {
+        float x[kDim];
+        DecodeBlock out;
+    };
+    DecodePin *pin = nullptr;        // pinned host staging, allocated at create
+    DecodeBlock *d_dblk = nullptr;   // device side
+    std::map<int, std::pair<cudaGraphExec_t, uint64_t>> decode_graphs;  // per layer, captured at upload
     bool profile = false;
     int profile_layers = 0;        // layers covered by the recorded events
     std::vector<cudaEvent_t> events;  // [layers][4]
     // persistent decode kernel
     unsigned long long *d_part_gu = nullptr;  // tagged tile partials, [2] x gate/up and down
     unsigned long long *d_part_dn = nullptr;
-    double *d_rp = nullptr;           // router sums per down tile
-    unsigned *d_cnt = nullptr;        // [6] gate/up tiles reduced per expert slot, down tiles with router sums, and with y
+    unsigned long long *d_rpt = nullptr;  // tagged router sums per down tile
+    unsigned *d_cnt = nullptr;        // [5] gate/up tiles reduced per expert slot, down tiles with y and B written
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
     uint8_t *d_bnext = nullptr;       // next step's gate/up B operand (written by the down epilogues)
@@ -147,6 +163,10 @@ struct ttl_moe {
     int stack_steps = 0;              // (token, layer) steps of the profiled launch
     unsigned long long *d_trace = nullptr;  // phase stamps (ttl_moe_trace)
     int trace_steps = 0;
+    float *log_y = nullptr;           // step log (ttl_moe_record): caller's device buffers
+    int32_t *log_idx = nullptr;
+    float *log_w = nullptr;
+    int log_steps = 0;
 };
 
 namespace ttl {
@@ -461,21 +481,25 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.xch = h->d_xch_peers;
     a.part_gu = h->d_part_gu;
     a.part_dn = h->d_part_dn;
-    a.rp = h->d_rp;
+    a.rpt = h->d_rpt;
     a.cnt_b = h->d_cnt;
-    a.cnt_r = h->d_cnt + 4;
+    a.cnt_y = h->d_cnt + 4;
     a.bdown = h->d_bdown;
     a.sfb_down = h->d_sfb_down;
     a.bnext = h->d_bnext;
     a.bnext_code = h->d_bnext_code;
     a.trace = h->d_trace;
     a.trace_steps = h->trace_steps;
+    a.ylog = h->log_y;
+    a.ilog = h->log_idx;
+    a.wlog = h->log_w;
+    a.log_steps = h->log_steps;
     if (h->d_trace) {
         TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_trace, 0, size_t(h->trace_steps) * kTracePoints * 8, h->stream));
     }
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_acc, 0, 2 * (kMaxExperts + 1) * sizeof(double), h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_barrier, 0, sizeof(unsigned), h->stream));
-    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, 6 * sizeof(unsigned), h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_cnt, 0, 5 * sizeof(unsigned), h->stream));
     const bool prof = h->profile && mode == 1;
     if (prof) {
         TTL_TRY_CUDA(h, cudaEventRecordWithFlags(h->stack_ev[0], h->stream, cudaEventRecordExternal));
@@ -492,6 +516,61 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
         h->stack_steps = int(tokens) * (end - begin);
     }
     h->launches += 1;
+    return TTL_OK;
+}
+
+// The graph ttl_moe_decode replays for `layer`: the input row from pinned
+// staging, one persistent-kernel step, the output block back.  Captured at
+// upload and again whenever launch settings change (trace, step log), so the
+// blocking call allocates nothing.
+int capture_decode_graph(ttl_moe *h, int layer) {
+    if (!stack_path(h) || !h->layers[size_t(layer)].uploaded) {
+        return TTL_OK;
+    }
+    auto old = h->decode_graphs.find(layer);
+    if (old != h->decode_graphs.end()) {
+        cudaGraphExecDestroy(old->second.first);
+        h->decode_graphs.erase(old);
+    }
+    cudaGraph_t graph = nullptr;
+    TTL_TRY_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    const uint64_t launches = h->launches;
+    cudaMemcpyAsync(h->d_x, h->pin->x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream);
+    int rc = enqueue_stack(h, layer, layer + 1, h->d_x, h->d_dblk->y, 1, 0);
+    cudaMemcpyAsync(&h->pin->out, h->d_dblk, sizeof(h->pin->out), cudaMemcpyDeviceToHost, h->stream);
+    const cudaError_t end = cudaStreamEndCapture(h->stream, &graph);
+    h->launches = launches;
+    if (rc || end != cudaSuccess) {
+        if (graph) {
+            cudaGraphDestroy(graph);
+        }
+        return rc ? rc : fail(h, TTL_ERR_CUDA, std::string("stream capture: ") + cudaGetErrorString(end));
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (inst != cudaSuccess) {
+        return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
+    }
+    h->decode_graphs.emplace(layer, std::make_pair(exec, uint64_t(1)));
+    return TTL_OK;
+}
+
+// Launch settings changed (profiling events, trace, step log): captured
+// forward graphs are dropped (recaptured on their next call) and the decode
+// graphs recaptured now.
+int refresh_graphs(ttl_moe *h) {
+    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    for (auto &g : h->graphs) {
+        cudaGraphExecDestroy(g.second.exec);
+    }
+    h->graphs.clear();
+    for (int l = 0; l < int(h->cfg.layers); ++l) {
+        const int rc = capture_decode_graph(h, l);
+        if (rc) {
+            return rc;
+        }
+    }
     return TTL_OK;
 }
 
@@ -813,14 +892,25 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     const size_t E = c.experts;
     const size_t T = std::max<uint32_t>(c.max_tokens, 1u);
     int rc = TTL_OK;
-    rc = rc ? rc : alloc_n(h, &h->d_status, 1);
+    rc = rc ? rc : alloc_n(h, &h->d_dblk, 1);
+    if (!rc) {
+        h->d_status = &h->d_dblk->status;
+        h->dw.top_idx = h->d_dblk->idx;
+        h->dw.top_w = h->d_dblk->w;
+    }
+    // host-call staging: the blocking decode's pinned block and the forward
+    // call's device rows (ttl_moe_forward works through them in chunks)
+    h->fwd_cap = std::max<size_t>(c.max_tokens, kForwardStagingTokens);
+    rc = rc ? rc : alloc_n(h, &h->d_fwd, h->fwd_cap * kDim);
+    if (!rc && cudaHostAlloc(reinterpret_cast<void **>(&h->pin), sizeof(*h->pin), cudaHostAllocDefault) != cudaSuccess) {
+        h->pin = nullptr;
+        rc = fail(h, TTL_ERR_CUDA, "cudaHostAlloc of the decode staging failed");
+    }
     rc = rc ? rc : alloc_n(h, &h->d_counters, 4);
     rc = rc ? rc : alloc_n(h, &h->d_ones, kDim);
     rc = rc ? rc : alloc_n(h, &h->dw.h, kDim);
     rc = rc ? rc : alloc_n(h, &h->dw.logits, 2 * size_t(kMaxExperts));
     rc = rc ? rc : alloc_n(h, &h->dw.bounds, 2 * size_t(kMaxExperts));
-    rc = rc ? rc : alloc_n(h, &h->dw.top_idx, 4);
-    rc = rc ? rc : alloc_n(h, &h->dw.top_w, 4);
     rc = rc ? rc : alloc_n(h, &h->dw.hidden, 4 * size_t(kDim));
     rc = rc ? rc : alloc_n(h, &h->dw.partial, kDim);
     rc = rc ? rc : alloc_n(h, &h->dw.arrive, 1);
@@ -833,8 +923,8 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_barrier, 2);
     rc = rc ? rc : alloc_n(h, &h->d_part_gu, kPartGuWords);
     rc = rc ? rc : alloc_n(h, &h->d_part_dn, kPartDnWords);
-    rc = rc ? rc : alloc_n(h, &h->d_rp, kRpWords);
-    rc = rc ? rc : alloc_n(h, &h->d_cnt, 6);
+    rc = rc ? rc : alloc_n(h, &h->d_rpt, kRptWords);
+    rc = rc ? rc : alloc_n(h, &h->d_cnt, 5);
     rc = rc ? rc : alloc_n(h, &h->d_seq, 2);
     rc = rc ? rc : alloc_n(h, &h->d_bdown, kBdownBytes);
     rc = rc ? rc : alloc_n(h, &h->d_sfb_down, kSfbDownBytes);
@@ -901,11 +991,11 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->dw.top_idx, 0, 4 * sizeof(int32_t)) != cudaSuccess ||
         cudaMemset(h->dw.top_w, 0, 4 * sizeof(float)) != cudaSuccess ||
         cudaMemset(h->d_barrier, 0, 2 * sizeof(unsigned)) != cudaSuccess ||
-        cudaMemset(h->d_cnt, 0, 6 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->d_cnt, 0, 5 * sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(h->d_seq, 0, 2 * sizeof(uint32_t)) != cudaSuccess ||
         cudaMemset(h->d_part_gu, 0, kPartGuWords * 8) != cudaSuccess ||
         cudaMemset(h->d_part_dn, 0, kPartDnWords * 8) != cudaSuccess ||
-        cudaMemset(h->d_rp, 0, kRpWords * 8) != cudaSuccess ||
+        cudaMemset(h->d_rpt, 0, kRptWords * 8) != cudaSuccess ||
         cudaMemset(h->d_bdown, 0, kBdownBytes) != cudaSuccess ||
         cudaMemset(h->d_sfb_down, 0x7f, kSfbDownBytes) != cudaSuccess ||
         cudaMemset(h->d_bnext, 0, kBnextBytes) != cudaSuccess ||
@@ -944,7 +1034,7 @@ void ttl_moe_destroy(ttl_moe *h) {
         cudaStreamSynchronize(h->stream);
     }
     for (auto &g : h->graphs) {
-        cudaGraphExecDestroy(g.second.first);
+        cudaGraphExecDestroy(g.second.exec);
     }
     h->graphs.clear();
     for (auto &g : h->decode_graphs) {
@@ -1047,7 +1137,8 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
         }
     }
     s.uploaded = true;
-    return push_layer_descriptor(h, layer);
+    const int prc = push_layer_descriptor(h, layer);
+    return prc ? prc : capture_decode_graph(h, layer);
 }
 
 int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
@@ -1127,52 +1218,26 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
         }
         return sync_and_check(h);
     }
-    // one launch of a captured graph per call: the input from pinned staging,
-    // the persistent kernel, the output, top-4 and status word back to it
-    if (!h->pin) {
-        TTL_TRY_CUDA(h, cudaHostAlloc(reinterpret_cast<void **>(&h->pin), sizeof(*h->pin), cudaHostAllocDefault));
-    }
+    // one launch of the layer's graph (captured at upload): the input from
+    // pinned staging, the persistent kernel, one copy of the output block
+    // (output, top-4, status word) back to it
     auto found = h->decode_graphs.find(layer);
     if (found == h->decode_graphs.end()) {
-        cudaGraph_t graph = nullptr;
-        TTL_TRY_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-        const uint64_t launches = h->launches;
-        cudaMemcpyAsync(h->d_x, h->pin->x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream);
-        rc = enqueue_stack(h, layer, layer + 1, h->d_x, h->d_y, 1, 0);
-        cudaMemcpyAsync(h->pin->y, h->d_y, kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
-        cudaMemcpyAsync(h->pin->idx, h->dw.top_idx, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, h->stream);
-        cudaMemcpyAsync(h->pin->w, h->dw.top_w, 4 * sizeof(float), cudaMemcpyDeviceToHost, h->stream);
-        cudaMemcpyAsync(&h->pin->status, h->d_status, sizeof(uint32_t), cudaMemcpyDeviceToHost, h->stream);
-        const cudaError_t end = cudaStreamEndCapture(h->stream, &graph);
-        if (rc || end != cudaSuccess) {
-            if (graph) {
-                cudaGraphDestroy(graph);
-            }
-            return rc ? rc : fail(h, TTL_ERR_CUDA, std::string("stream capture: ") + cudaGetErrorString(end));
-        }
-        cudaGraphExec_t exec = nullptr;
-        const cudaError_t inst = cudaGraphInstantiate(&exec, graph, 0);
-        cudaGraphDestroy(graph);
-        if (inst != cudaSuccess) {
-            return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
-        }
-        const uint64_t per_replay = h->launches - launches;
-        h->launches = launches;
-        found = h->decode_graphs.emplace(layer, std::make_pair(exec, per_replay)).first;
+        return fail(h, TTL_ERR_STATE, "layer " + std::to_string(layer) + " has no decode graph");
     }
     std::memcpy(h->pin->x, x, kDim * sizeof(float));
     TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.first, h->stream));
     h->launches += found->second.second;
     TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
-    if (h->pin->status) {
+    if (h->pin->out.status) {
         return check_status(h);  // reads, clears and reports the device status word
     }
-    std::memcpy(out, h->pin->y, kDim * sizeof(float));
+    std::memcpy(out, h->pin->out.y, kDim * sizeof(float));
     if (top4_idx) {
-        std::memcpy(top4_idx, h->pin->idx, 4 * sizeof(int32_t));
+        std::memcpy(top4_idx, h->pin->out.idx, 4 * sizeof(int32_t));
     }
     if (top4_w) {
-        std::memcpy(top4_w, h->pin->w, 4 * sizeof(float));
+        std::memcpy(top4_w, h->pin->out.w, 4 * sizeof(float));
     }
     return TTL_OK;
 }
@@ -1264,10 +1329,21 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
     if (rc || tokens == 0) {
         return rc;
     }
-    // The token loop is captured once per (buffers, count, layers) and replayed.
+    // The token loop is captured once per (buffers, count, layers) and
+    // replayed; the cache keeps the kMaxForwardGraphs most recently used.
     const GraphKey key{x, y, tokens, layer_begin, layer_end};
     auto found = h->graphs.find(key);
     if (found == h->graphs.end()) {
+        if (h->graphs.size() >= kMaxForwardGraphs) {
+            auto oldest = h->graphs.begin();
+            for (auto it = h->graphs.begin(); it != h->graphs.end(); ++it) {
+                if (it->second.last_use < oldest->second.last_use) {
+                    oldest = it;
+                }
+            }
+            cudaGraphExecDestroy(oldest->second.exec);
+            h->graphs.erase(oldest);
+        }
         cudaGraph_t graph = nullptr;
         TTL_TRY_CUDA(h, cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
         const uint64_t launches = h->launches;
@@ -1290,10 +1366,11 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
         }
         const uint64_t per_replay = h->launches - launches;
         h->launches = launches;  // counted per replay below
-        found = h->graphs.emplace(key, std::make_pair(exec, per_replay)).first;
+        found = h->graphs.emplace(key, ttl_moe::ForwardGraph{exec, per_replay, 0}).first;
     }
-    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.first, h->stream));
-    h->launches += found->second.second;
+    found->second.last_use = ++h->graph_clock;
+    TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.exec, h->stream));
+    h->launches += found->second.kernels;
     return TTL_OK;
 }
 
@@ -1308,22 +1385,19 @@ int ttl_moe_forward(ttl_moe *h, int layer_begin, int layer_end, const float *x, 
     if (rc || tokens == 0) {
         return rc;
     }
-    if (tokens > h->fwd_cap) {
-        // Grows the staging buffer; the first call with a larger count pays it.
-        float *p = nullptr;
-        rc = alloc_n(h, &p, tokens * kDim);
+    // the tokens are independent, so they go through the staging rows (made
+    // at create) in chunks of its capacity
+    for (size_t t0 = 0; t0 < tokens; t0 += h->fwd_cap) {
+        const size_t n = std::min(h->fwd_cap, tokens - t0);
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_fwd, x + t0 * kDim, n * kDim * sizeof(float), cudaMemcpyHostToDevice,
+                                        h->stream));
+        rc = ttl_moe_forward_async(h, layer_begin, layer_end, h->d_fwd, h->d_fwd, n);
         if (rc) {
             return rc;
         }
-        h->d_fwd = p;
-        h->fwd_cap = tokens;
+        TTL_TRY_CUDA(h, cudaMemcpyAsync(y + t0 * kDim, h->d_fwd, n * kDim * sizeof(float), cudaMemcpyDeviceToHost,
+                                        h->stream));
     }
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_fwd, x, tokens * kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
-    rc = ttl_moe_forward_async(h, layer_begin, layer_end, h->d_fwd, h->d_fwd, tokens);
-    if (rc) {
-        return rc;
-    }
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(y, h->d_fwd, tokens * kDim * sizeof(float), cudaMemcpyDeviceToHost, h->stream));
     return sync_and_check(h);
 }
 
@@ -1341,7 +1415,10 @@ int ttl_moe_profile(ttl_moe *h, int enable) {
             TTL_TRY_CUDA(h, cudaEventCreate(&e));
         }
     }
-    h->profile = enable != 0;
+    if (h->profile != (enable != 0)) {
+        h->profile = enable != 0;
+        return refresh_graphs(h);
+    }
     return TTL_OK;
 }
 
@@ -1359,12 +1436,42 @@ int ttl_moe_trace(ttl_moe *h, int steps, uint64_t *out) {
             return rc;
         }
         h->trace_steps = steps;
+        rc = refresh_graphs(h);
+        if (rc) {
+            return rc;
+        }
     }
     if (out && h->d_trace) {
         TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
         TTL_TRY_CUDA(h, cudaMemcpy(out, h->d_trace, size_t(h->trace_steps) * kTracePoints * 8, cudaMemcpyDeviceToHost));
     }
     return TTL_OK;
+}
+
+int ttl_moe_record(ttl_moe *h, size_t steps, float *y_log, int32_t *idx_log, float *w_log) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (steps > 0 && (!y_log || !idx_log || !w_log)) {
+        return fail(h, TTL_ERR_ARGUMENT, "step log needs its three buffers");
+    }
+    if (steps > size_t(1) << 30) {
+        return fail(h, TTL_ERR_ARGUMENT, "step log too long");
+    }
+    for (const void *p : {(const void *)y_log, (const void *)idx_log, (const void *)w_log}) {
+        if (steps > 0 && !is_device_pointer(p)) {
+            return fail(h, TTL_ERR_ARGUMENT, "step log buffers must be device memory");
+        }
+    }
+    int rc = set_device(h);
+    if (rc) {
+        return rc;
+    }
+    h->log_steps = int(steps);
+    h->log_y = steps ? y_log : nullptr;
+    h->log_idx = steps ? idx_log : nullptr;
+    h->log_w = steps ? w_log : nullptr;
+    return refresh_graphs(h);
 }
 
 int ttl_moe_kernel_ms(ttl_moe *h, float *ms, size_t n) {

@@ -87,6 +87,7 @@ def lib():
         "ttl_moe_profile": (i32, [vp, i32]),
         "ttl_moe_trace": (i32, [vp, i32, ctypes.POINTER(u64)]),
         "ttl_moe_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_float), sz]),
+        "ttl_moe_record": (i32, [vp, sz, vp, vp, vp]),
         "ttl_matvec_mxfp4": (i32, [vp, vp, vp, vp, i32]),
         "ttl_matvec_mxfp4_noalloc": (i32, [vp, vp, vp, vp, sz, i32]),
         "ttl_packed_bytes": (sz, [sz]),
@@ -249,6 +250,12 @@ class MoE:
         out = (ctypes.c_uint64 * (n * 10))()
         self._check(lib().ttl_moe_trace(self.h, 0, out))
         return np.frombuffer(out, dtype=np.uint64).reshape(n, 10).astype(np.int64)
+
+    def record(self, steps, y_log=None, idx_log=None, w_log=None):
+        """Step log of later forward/decode launches into caller-owned device
+        buffers (y_log [steps, 2880] f32, idx_log / w_log [steps, 4]);
+        steps = 0 turns it off."""
+        self._check(lib().ttl_moe_record(self.h, steps, _ptr(y_log), _ptr(idx_log), _ptr(w_log)))
 
     def counters(self):
         out = (ctypes.c_uint64 * 4)()
