@@ -360,6 +360,74 @@ def prefill_cfg2(torch, ttl_moe, synth, device, iters=20, cpu_seconds=0.0):
     }
 
 
+VOCAB = 201088
+HEAD_BYTES = VOCAB * 90 * 34 + VOCAB * 4 + 2 * DIM * 4  # Q8_0 output.weight, logits out, x + norm in
+
+
+def logits_head(torch, ttl_moe, synth, hbm_peak, iters=20, cpu_seconds=6.0):
+    """SURVEY 8(f) rank 2, the output head of GptOssModel::forward: rms_norm
+    with output_norm.weight, matvec_q8_0 over the 201,088 x 2880 Q8_0
+    output.weight (615 MB, far above L2) and greedy, on seeded synthetic
+    weights.  Device time per call (CUDA events on the head's stream, x and
+    the logits in HBM), the host call end to end (x in, logits and token out),
+    tt-lab's own rms_norm + matvec_q8_0 + greedy on one host thread, and the
+    logits of two inputs checked bit for bit against it."""
+    import oracle
+    t = synth.head_device(0, VOCAB)
+    xs = synth.inputs_host(9, 4)
+    with ttl_moe.Head(vocab=VOCAB, device=torch.cuda.current_device()) as h:
+        h.upload(t["output_w"], t["output_norm"])
+        wh = t["output_w"].cpu().numpy()
+        gh = t["output_norm"].cpu().numpy()
+        del t
+        torch.cuda.empty_cache()
+        xd = torch.from_numpy(xs).cuda()
+        ld = torch.empty(VOCAB, dtype=torch.float32, device="cuda")
+        td = torch.empty(1, dtype=torch.int32, device="cuda")
+        st = torch.cuda.ExternalStream(h.stream())
+        for i in range(3):
+            h.forward_async(xd[i % 4], ld, td)
+        h.sync()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(iters):
+            h.forward_async(xd[i % 4], ld, td)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        h.forward(xs[0])
+        t0 = time.perf_counter()
+        for i in range(iters):
+            logits, tok = h.forward(xs[i % 4])
+        e2e_ms = (time.perf_counter() - t0) / iters * 1e3
+        checks = []
+        for i in range(2):
+            gl, gt = h.forward(xs[i])
+            rl, rt = oracle.head(wh, gh, xs[i], VOCAB, impl="ref")
+            nan = np.isnan(rl)
+            checks.append(bool(np.array_equal(np.isnan(gl), nan) and
+                               np.array_equal(gl[~nan].view(np.uint32), rl[~nan].view(np.uint32)) and gt == rt))
+    oracle.head(wh, gh, xs[0], VOCAB, impl="ref")
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < cpu_seconds or n == 0:
+        oracle.head(wh, gh, xs[n % 4], VOCAB, impl="ref")
+        n += 1
+    cpu_ms = (time.perf_counter() - t0) / n * 1e3
+    gbs = HEAD_BYTES / (ms * 1e-3) / 1e9
+    return {"workload": "output head: rms_norm + matvec_q8_0 (201088 x 2880 Q8_0, 615 MB) + greedy, one token",
+            "ms_per_call": ms, "tokens_per_s": 1e3 / ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "bytes_per_call": HEAD_BYTES,
+                         "kernels": "head_norm_kernel + head_matvec_kernel, CUDA events around both"},
+            "e2e": {"ms_per_call": e2e_ms, "h2d_bytes_per_step": DIM * 4, "d2h_bytes_per_step": VOCAB * 4 + 4},
+            "cpu_baseline": {"value": 1e3 / cpu_ms, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                             "sample": f"{n} calls of tt-lab's rms_norm + matvec_q8_0 + greedy (oracle/_ref, 1 "
+                                       f"thread), {cpu_ms:.1f} ms each"},
+            "parity": {"passed": all(checks), "inputs": len(checks),
+                       "what": "logits bit-equal to tt-lab's (NaN positions equal) and the same greedy token"}}
+
+
 # Algorithmic bytes of one gpt-oss-120b decode token-layer (E = 128): router W
 # + bias, 12 expert matrices + their biases, x / out.
 LAYER_BYTES_120B = 128 * DIM * 4 + 128 * 4 + 12 * GGUF_MATRIX + 12 * BIAS + 2 * DIM * 4
@@ -473,6 +541,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the parity sample checked after timing")
+    ap.add_argument("--no-head", action="store_true", help="skip the output-head (logits) measurement")
     ap.add_argument("--no-120b", action="store_true", help="skip the cfg3 (120b, 36-layer) decode line")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the cfg2 prefill measurement (one JSON line with its figures)")
@@ -618,6 +687,15 @@ def main():
             prefill = prefill_cfg2(torch, ttl_moe, synth, local,
                                    cpu_seconds=0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 6.0))
         prefill_ep = prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist)
+    head = None
+    if world == 1 and not args.no_head:
+        moe.close()
+        torch.cuda.empty_cache()
+        try:
+            head = logits_head(torch, ttl_moe, synth, peaks()[0],
+                               cpu_seconds=0.0 if args.no_cpu_baseline else 6.0)
+        except OSError as e:  # the checker is not built on this machine
+            head = {"unavailable": str(e)}
     decode_120b = None
     if not args.no_120b:
         moe.close()
@@ -677,6 +755,7 @@ def main():
                                     "blocking call on host buffers, wall clock, max over ranks"},
             "prefill": prefill,
             "prefill_ep": prefill_ep,
+            "logits_head": head,
             "decode_120b": decode_120b,
         }
         print(json.dumps(line))

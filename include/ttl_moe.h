@@ -21,6 +21,8 @@
  *                                                   src/requant.cpp:258-277
  *   ttl_ttq_*             the TTQ container writer  src/requant.cpp:23-68,
  *                                                   :415-504; src/requant.h:31-52
+ *   ttl_head_*            the output head of GptOssModel::forward: rms_norm,
+ *                         matvec_q8_0 and greedy    src/model.cpp:598-612
  *
  * Memory: device buffers, pinned host staging and the blocking decode's
  * captured graphs are made in ttl_moe_create and ttl_moe_upload_layer and freed
@@ -199,7 +201,9 @@ int ttl_matvec_mxfp4(const void *packed, const float *bias, const float *x, floa
  * allocate (a fixed memory budget, a pool-owning host).  The first call on a
  * device looks the array up (cudaGetSymbolAddress) with that device current;
  * make it before any stream capture.  The array is shared by all calls on a
- * device, so overlapping calls from several threads or streams race.
+ * device, so overlapping calls from several threads or streams race.  The
+ * looked-up address is kept for the life of the process: resetting the device
+ * (cudaDeviceReset) while using this entry is not supported.
  * Synchronous, on the device's legacy default stream.  No counterpart in
  * tt-lab. */
 int ttl_matvec_mxfp4_noalloc(const void *packed, const float *bias, const float *x, float *y, size_t matrices,
@@ -235,6 +239,35 @@ int ttl_ttq_finish(ttl_ttq_writer *writer);
 /* Frees the writer; an unfinished file is removed. */
 void ttl_ttq_close(ttl_ttq_writer *writer);
 
+/* ---- output head (logits) ---------------------------------------------- */
+
+/* The last step of GptOssModel::forward / prefill (src/model.cpp:598-612):
+ * normalized = rms_norm(x, output_norm.weight), logits = matvec_q8_0(
+ * output.weight, normalized), token = greedy(logits) (src/tensor.cpp:202-218,
+ * :568-580), computed on the GPU with tt-lab's exact arithmetic, so logits and
+ * token equal the reference's bit for bit.  One handle holds one output
+ * matrix of `vocab` rows x 2880 columns (201088 rows for gpt-oss). */
+typedef struct ttl_head ttl_head;
+
+int ttl_head_create(int device, uint32_t vocab, ttl_head **handle_out);
+void ttl_head_destroy(ttl_head *handle);
+/* Message of the last failed call on `handle` (NULL: of the calling thread). */
+const char *ttl_head_last_error(const ttl_head *handle);
+/* q8_0: output.weight in GGUF Q8_0 blocks [vocab][90][34 B] (half scale, 32
+ * int8); norm_w: output_norm.weight f32 [2880].  Host or device pointers;
+ * repacked on the device to aligned rows.  Synchronous. */
+int ttl_head_upload(ttl_head *handle, const void *q8_0, const float *norm_w);
+/* The uploaded matrix back in GGUF bytes (host or device), for checks. */
+int ttl_head_unpack(ttl_head *handle, void *gguf_out);
+/* x: HOST f32 [2880] (the residual stream after the last layer); logits:
+ * optional HOST f32 [vocab]; token: optional HOST int32 (at least one of
+ * the two).  Blocking. */
+int ttl_head_forward(ttl_head *handle, const float *x, float *logits, int32_t *token);
+/* Device-pointer form on the handle's stream (logits, token optional). */
+int ttl_head_forward_async(ttl_head *handle, const float *x, float *logits, int32_t *token);
+int ttl_head_sync(ttl_head *handle);
+void *ttl_head_stream(ttl_head *handle);
+
 /* ---- synthetic inputs (benchmarks and tests) ---------------------------- */
 
 /* Fills GGUF-layout MXFP4 blocks from (seed, stream): quant bytes uniform,
@@ -242,6 +275,9 @@ void ttl_ttq_close(ttl_ttq_writer *writer);
  * device. */
 int ttl_synth_mxfp4(void *dst, size_t blocks, uint64_t seed, uint64_t stream, uint32_t scale_lo,
                     uint32_t scale_count);
+/* Fills GGUF-layout Q8_0 blocks from (seed, stream): half scales in
+ * [2^-11, 2^-9), int8 quants uniform.  dst host or device. */
+int ttl_synth_q8_0(void *dst, size_t blocks, uint64_t seed, uint64_t stream);
 /* Fills n f32 values sigma * IrwinHall12(seed, stream) + mean.  dst host or device. */
 int ttl_synth_normal(float *dst, size_t n, uint64_t seed, uint64_t stream, float sigma, float mean);
 

@@ -61,6 +61,11 @@ def port():
         L.oref_swiglu.restype = ctypes.c_float
         L.oref_swiglu.argtypes = [ctypes.c_float, ctypes.c_float]
         L.oref_matvec_add_f32.argtypes = [vp, vp, vp, vp, sz, sz]
+        L.oref_matvec_q8_0.argtypes = [vp, vp, vp, sz]
+        L.oref_greedy.argtypes = [vp, sz]
+        L.oref_greedy.restype = ctypes.c_int32
+        L.oref_half_to_float.argtypes = [ctypes.c_uint16]
+        L.oref_half_to_float.restype = ctypes.c_float
         _port = L
     return _port
 
@@ -88,6 +93,8 @@ def ref():
         L.tref_moe_decode_threaded.argtypes = [sz] + [vp] * 10 + [i32]
         L.tref_moe_layer_tokens.argtypes = [sz, vp, vp, vp, vp, sz, i32, vp, vp, vp]
         L.tref_forward_tokens.argtypes = [sz, sz, vp, vp, vp, vp, sz, i32]
+        L.tref_matvec_q8_0.argtypes = [vp, sz, vp, vp, vp]
+        L.tref_greedy.argtypes = [vp, vp]
         _ref = L
     return _ref
 
@@ -135,6 +142,41 @@ def moe_prefill(t, x, isa=ISA_V4, impl="port"):
                                           _p(t["gate_w"]), _p(t["gate_b"]), _p(t["up_w"]), _p(t["up_b"]),
                                           _p(t["down_w"]), _p(t["down_b"]), _p(x), T, _p(out), _p(idx), _p(w)))
     return out, idx, w
+
+
+VOCAB = 201088
+
+
+def matvec_q8_0(w, x, rows, impl="port"):
+    """tt-lab's matvec_q8_0 (src/tensor.cpp:202-218) of `rows` GGUF Q8_0 rows
+    (uint8 [rows * 3060]) with x [2880].  Returns f32 [rows]."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(rows, np.float32)
+    if impl == "port":
+        port().oref_matvec_q8_0(_p(w), _p(x), _p(y), rows)
+    else:
+        _ref_check(ref().tref_matvec_q8_0(_p(w), rows, _p(x), _p(y), None))
+    return y
+
+
+def greedy(logits, impl="port"):
+    """GptOssModel::greedy (src/model.cpp:604-612)."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    if impl == "port":
+        return int(port().oref_greedy(_p(logits), logits.size))
+    if logits.size != VOCAB:
+        raise ValueError("the reference's greedy reads the full vocabulary")
+    tok = np.zeros(1, np.int32)
+    _ref_check(ref().tref_greedy(_p(logits), _p(tok)))
+    return int(tok[0])
+
+
+def head(w, norm_w, x, rows, impl="port"):
+    """The output head of GptOssModel::forward (src/model.cpp:598-612):
+    rms_norm(x, norm_w) -> matvec_q8_0 -> greedy.  Returns (logits, token)."""
+    h = rms_norm(x, norm_w, impl=impl)
+    logits = matvec_q8_0(w, h, rows, impl=impl)
+    return logits, greedy(logits, impl="port" if rows != VOCAB else impl)
 
 
 def router_logits(t, x):

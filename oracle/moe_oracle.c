@@ -368,3 +368,81 @@ done:
     free(xt);
     return rc;
 }
+
+/* ---- output head: rms_norm -> matvec_q8_0 -> greedy ----------------------- */
+
+/* IEEE half -> float, exact (src/tensor.cpp:163-165 converts through
+ * _Float16).  Subnormal halves are normalised; inf and NaN keep their class. */
+static float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t exp = (h >> 10) & 31u;
+    uint32_t mant = h & 1023u;
+    uint32_t bits;
+    if (exp == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            int e = -1;
+            do {
+                ++e;
+                mant <<= 1;
+            } while ((mant & 1024u) == 0);
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((mant & 1023u) << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (mant << 13);
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (mant << 13);
+    }
+    float out;
+    memcpy(&out, &bits, sizeof(out));
+    return out;
+}
+
+float oref_half_to_float(uint16_t h) {
+    return half_to_float(h);
+}
+
+/* matvec_q8_0 (src/tensor.cpp:202-218 with q8_0_vector_fma_block :90-114):
+ * a Q8_0 block is a half scale and 32 int8 quants (34 B).  Two 16-lane
+ * accumulators take elements 0..15 and 16..31 of every block in block order,
+ * each term rounded as (q * scale) * x, then lane-wise acc0 + acc1, then the
+ * 16 lanes summed in order from 0.  rows x 2880 columns. */
+void oref_matvec_q8_0(const uint8_t *w, const float *x, float *y, size_t rows) {
+    const size_t blocks = OREF_DIM / 32;
+    for (size_t r = 0; r < rows; ++r) {
+        const uint8_t *row = w + r * blocks * 34;
+        float acc0[16] = {0}, acc1[16] = {0};
+        for (size_t b = 0; b < blocks; ++b) {
+            const uint8_t *src = row + b * 34;
+            const float scale = half_to_float((uint16_t)(src[0] | (src[1] << 8)));
+            for (int i = 0; i < 16; ++i) {
+                const float q0 = (float)(int8_t)src[2 + i] * scale;
+                const float q1 = (float)(int8_t)src[18 + i] * scale;
+                const float p0 = q0 * x[b * 32 + i];
+                const float p1 = q1 * x[b * 32 + 16 + i];
+                acc0[i] = acc0[i] + p0;
+                acc1[i] = acc1[i] + p1;
+            }
+        }
+        float sum = 0.0f;
+        for (int i = 0; i < 16; ++i) {
+            const float a = acc0[i] + acc1[i];
+            sum = sum + a;
+        }
+        y[r] = sum;
+    }
+}
+
+/* GptOssModel::greedy (src/model.cpp:604-612): the first index whose logit
+ * is greater than every earlier one's, starting from index 0 (a NaN is never
+ * greater, so NaNs are passed over, and a NaN at index 0 is never replaced). */
+int32_t oref_greedy(const float *logits, size_t n) {
+    size_t best = 0;
+    for (size_t i = 1; i < n; ++i) {
+        if (logits[i] > logits[best]) {
+            best = i;
+        }
+    }
+    return (int32_t)best;
+}

@@ -70,6 +70,13 @@ void oref_moe_decode(const oref_layer *layer, const float *x, float *out, int32_
 int oref_moe_prefill(const oref_layer *layer, const float *x, size_t tokens, float *out, int32_t *idx, float *w,
                      int isa);
 
+/* Output head (src/model.cpp:598-612): y = matvec_q8_0(w, x) over `rows`
+ * rows of 2880 columns (src/tensor.cpp:202-218), greedy argmax, and the exact
+ * half -> float conversion the Q8_0 scales use (src/tensor.cpp:163-165). */
+void oref_matvec_q8_0(const uint8_t *w, const float *x, float *y, size_t rows);
+int32_t oref_greedy(const float *logits, size_t n);
+float oref_half_to_float(uint16_t h);
+
 #ifdef __cplusplus
 }
 #endif

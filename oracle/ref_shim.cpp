@@ -712,4 +712,26 @@ int tref_forward_tokens(size_t experts, size_t layers, const void *const *tables
     });
 }
 
+// tt-lab's output head on caller buffers: matvec_q8_0 (src/tensor.cpp:202-218)
+// over `rows` rows of a Q8_0 matrix, then, when rows is the model's vocabulary,
+// GptOssModel::greedy (src/model.cpp:604-612) on the result.
+int tref_matvec_q8_0(const uint8_t *w, size_t rows, const float *x, float *y, int32_t *token) {
+    return guarded([&] {
+        const GgufTensor m = view(w, {kDim, rows}, tensor_q8_0);
+        matvec_q8_0(m, x, y);
+        if (token) {
+            if (rows != 201088) {
+                throw std::runtime_error("greedy needs the full vocabulary (201088 rows)");
+            }
+            *token = get_model(32, 1).model->greedy(y);
+        }
+    });
+}
+
+// GptOssModel::greedy (src/model.cpp:604-612) on a caller's full-vocabulary
+// logit vector (201088 floats).
+int tref_greedy(const float *logits, int32_t *token) {
+    return guarded([&] { *token = get_model(32, 1).model->greedy(logits); });
+}
+
 } // extern "C"

@@ -41,6 +41,8 @@ def _lib():
         L.oref_synth_mxfp4.restype = None
         L.oref_synth_mxfp4_range.argtypes = [vp, sz, sz, u64, u64, ctypes.c_uint32, ctypes.c_uint32]
         L.oref_synth_mxfp4_range.restype = None
+        L.oref_synth_q8_0_range.argtypes = [vp, sz, sz, u64, u64]
+        L.oref_synth_q8_0_range.restype = None
         L._synth_bound = True
     return L
 
@@ -71,6 +73,36 @@ def mxfp4_host(blocks, seed, stream_id, scale_lo=SCALE_LO, scale_count=SCALE_COU
         with ThreadPoolExecutor(n) as ex:
             list(ex.map(part, range(n)))
     return out
+
+
+def q8_0_host(blocks, seed, stream_id, threads=None) -> np.ndarray:
+    """GGUF Q8_0 blocks (34 B: half scale in [2^-11, 2^-9), 32 int8 quants)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty(blocks * 34, np.uint8)
+    L = _lib()
+    n = max(1, min(threads or os.cpu_count() or 1, 64, blocks // 65536 + 1))
+    cuts = [blocks * i // n for i in range(n + 1)]
+
+    def part(i):
+        b0, b1 = cuts[i], cuts[i + 1]
+        L.oref_synth_q8_0_range(out.ctypes.data + 34 * b0, b0, b1 - b0, seed, stream_id)
+
+    if n == 1:
+        part(0)
+    else:
+        with ThreadPoolExecutor(n) as ex:
+            list(ex.map(part, range(n)))
+    return out
+
+
+HEAD_STREAM = 1 << 36
+
+
+def head_host(seed, rows):
+    """The output matrix (Q8_0, rows x 2880) and output_norm.weight ~ N(1, 0.02)."""
+    return {"output_w": q8_0_host(rows * (DIM // 32), seed, HEAD_STREAM),
+            "output_norm": normal_host(DIM, seed, HEAD_STREAM + 1, 0.02, 1.0)}
 
 
 def zipf_shift(seed, experts, s, beta=1.0) -> np.ndarray:

@@ -22,6 +22,9 @@
  *   MXFP4 block b (GGUF layout, 17 bytes): byte 0 = lo + ((hi32(draw(k, 3b + 2))
  *                * count) >> 32); bytes 1..8 and 9..16 = the little-endian bytes
  *                of draw(k, 3b) and draw(k, 3b + 1)
+ *   Q8_0 block b (GGUF layout, 34 bytes): bytes 0..1 = the half bits 0x1000 +
+ *                ((draw(k, 5b + 4) >> 40) & 0x7FF), little-endian; bytes 2..33 =
+ *                the little-endian bytes of draw(k, 5b) .. draw(k, 5b + 3)
  */
 #include <stddef.h>
 #include <stdint.h>
@@ -81,4 +84,22 @@ void oref_synth_mxfp4_range(uint8_t *dst, size_t b0, size_t blocks, uint64_t see
 
 void oref_synth_mxfp4(uint8_t *dst, size_t blocks, uint64_t seed, uint64_t stream, uint32_t lo, uint32_t count) {
     oref_synth_mxfp4_range(dst, 0, blocks, seed, stream, lo, count);
+}
+
+/* GGUF Q8_0 blocks b0 .. b0 + blocks - 1. */
+void oref_synth_q8_0_range(uint8_t *dst, size_t b0, size_t blocks, uint64_t seed, uint64_t stream) {
+    const uint64_t k = stream_key(seed, stream);
+    for (size_t b = b0; b < b0 + blocks; ++b) {
+        uint8_t *o = dst + (b - b0) * 34;
+        const uint64_t hs = draw(k, (uint64_t)b * 5ull + 4ull);
+        const uint32_t bits = 0x1000u + (uint32_t)((hs >> 40) & 0x7FFull);
+        o[0] = (uint8_t)bits;
+        o[1] = (uint8_t)(bits >> 8);
+        for (int d = 0; d < 4; ++d) {
+            const uint64_t h = draw(k, (uint64_t)b * 5ull + (uint64_t)d);
+            for (int j = 0; j < 8; ++j) {
+                o[2 + 8 * d + j] = (uint8_t)(h >> (8 * j));
+            }
+        }
+    }
 }

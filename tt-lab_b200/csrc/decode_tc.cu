@@ -167,7 +167,8 @@ struct alignas(1024) Smem {
     uint64_t sel_full;            // the step's selection is published
     uint64_t setup;               // the down B operands of the step landed
     uint64_t rwbar;               // a down reducer's staged router weights landed
-    uint32_t rw_uses;             // stagings so far (its parity), written by thread 0 only
+    uint32_t rw_uses;             // stagings consumed so far (its parity), written by thread 0 only
+    uint32_t rw_issued;           // stagings issued so far, written by thread 0 only
     uint64_t fin;
     uint32_t tmem;
     int go;      // grid-barrier / end-of-step verdict, written by thread 0 only
@@ -872,6 +873,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     if (stage_rw && i == 0) {
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const uint32_t rb = uint32_t(min(128, kDim - 128 * tile)) * 4u;
+        ++s.rw_issued;
         tc::mbar_expect_tx(&s.rwbar, uint32_t(E - kPreE) * rb);
         float *dst = reinterpret_cast<float *>(&s.a[0][0][0][0]);
         for (int e = kPreE; e < E; ++e) {
@@ -943,7 +945,8 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             } else if (kWideRouter) {
                 if (b == kPreE / 16) {
                     // every thread waits for the staged weights (bounded, and
-                    // not cut short by an abort: no copy is in flight at exit)
+                    // not cut short by an abort; a wait that gives up leaves
+                    // the copies to the drain before the CTA exits)
                     if (!tc::mbar_wait(&s.rwbar, rw_parity)) {
                         fail_wait(s, a.status);
                     }
@@ -1476,6 +1479,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         tc::mbar_init(&s.setup, 1);
         tc::mbar_init(&s.rwbar, 1);
         s.rw_uses = 0;
+        s.rw_issued = 0;
         tc::mbar_init(&s.fin, kIssuers);
         tc::fence_mbar_init();
     }
@@ -1834,6 +1838,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         if (warp >= kIssuerWarp0 && warp < kIssuerWarp0 + kIssuers && lane == 0) {
             tc::mma_commit(&s.fin);
             tc::mbar_wait(&s.fin, 0);
+        }
+        // a router-weight staging whose wait gave up (the launch is aborting)
+        // still has its copies in flight: wait for them once more (bounded)
+        // before the shared memory is released
+        if (kWideRouter && threadIdx.x == 0 && s.rw_issued != s.rw_uses) {
+            if (!tc::mbar_wait(&s.rwbar, s.rw_uses & 1u)) {
+                set_status(a.status, kStatusWaitTimeout);
+            }
         }
     }
     tc::fence_before_sync();

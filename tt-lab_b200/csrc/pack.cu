@@ -98,6 +98,15 @@ __global__ void synth_mxfp4_kernel(uint8_t *dst, size_t blocks, uint64_t key, ui
     }
 }
 
+__global__ void synth_q8_0_kernel(uint8_t *dst, size_t blocks, uint64_t key) {
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < blocks; i += size_t(gridDim.x) * blockDim.x) {
+        uint8_t *out = dst + i * 34;
+        for (uint32_t o = 0; o < 34; ++o) {
+            out[o] = ttl_synth_q8_0_byte(key, i, o);
+        }
+    }
+}
+
 __global__ void synth_normal_kernel(float *dst, size_t n, uint64_t key, float sigma, float mean) {
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
         dst[i] = __fadd_rn(__fmul_rn(ttl_synth_normal(key, i), sigma), mean);
@@ -236,6 +245,26 @@ extern "C" int ttl_synth_mxfp4(void *dst, size_t blocks, uint64_t seed, uint64_t
         for (int q = 0; q < 8; ++q) {
             b[1 + q] = (uint8_t)(h0 >> (8 * q));
             b[9 + q] = (uint8_t)(h1 >> (8 * q));
+        }
+    }
+    return TTL_OK;
+}
+
+extern "C" int ttl_synth_q8_0(void *dst, size_t blocks, uint64_t seed, uint64_t stream) {
+    if (!dst && blocks) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null buffer");
+    }
+    const uint64_t key = ttl_synth_key(seed, stream);
+    if (is_device_pointer(dst)) {
+        synth_q8_0_kernel<<<grid_for(blocks), 256>>>((uint8_t *)dst, blocks, key);
+        TTL_TRY_CUDA(nullptr, cudaGetLastError());
+        TTL_TRY_CUDA(nullptr, cudaDeviceSynchronize());
+        return TTL_OK;
+    }
+    uint8_t *out = (uint8_t *)dst;
+    for (size_t i = 0; i < blocks; ++i) {
+        for (uint32_t o = 0; o < 34; ++o) {
+            out[i * 34 + o] = ttl_synth_q8_0_byte(key, i, o);
         }
     }
     return TTL_OK;

@@ -10,6 +10,10 @@
 //     and :149-153 of tt-lab): 16 quant bytes uniform over 0..255 (so both
 //     nibbles are uniform over the 16 E2M1 codes) and one E8M0 scale byte
 //     uniform over [scale_lo, scale_lo + scale_count).
+//   - Q8_0 tensors in GGUF layout (34-byte blocks, src/tensor.cpp:90-114): a
+//     half scale with bits 0x1000 + 11 random bits (2^-11 <= scale < 2^-9,
+//     the range of a gpt-oss output matrix), then 32 int8 quants uniform over
+//     -128..127 (five draws per block).
 //   - "Normal" f32 values: Irwin-Hall with twelve 24-bit uniforms,
 //     sum - 6 (mean 0, variance 1, bounded by +-6), times sigma.  The sum is
 //     formed in integers and converted once, so it rounds identically everywhere.
@@ -60,5 +64,17 @@ TTL_HD uint8_t ttl_synth_mxfp4_byte(uint64_t key, uint64_t block, uint32_t offse
     }
     const uint32_t q = offset - 1;
     const uint64_t h = ttl_synth_draw(key, block * 3ull + (q >> 3));
+    return (uint8_t)(h >> (8 * (q & 7)));
+}
+
+// Byte `offset` (0..33) of block `block` of a Q8_0 tensor in GGUF layout.
+TTL_HD uint8_t ttl_synth_q8_0_byte(uint64_t key, uint64_t block, uint32_t offset) {
+    if (offset < 2) {
+        const uint64_t h = ttl_synth_draw(key, block * 5ull + 4ull);
+        const uint32_t bits = 0x1000u + (uint32_t)((h >> 40) & 0x7FFull);
+        return (uint8_t)(bits >> (8 * offset));
+    }
+    const uint32_t q = offset - 2;
+    const uint64_t h = ttl_synth_draw(key, block * 5ull + (q >> 3));
     return (uint8_t)(h >> (8 * (q & 7)));
 }

@@ -198,17 +198,21 @@ extern "C" int ttl_matvec_mxfp4(const void *packed, const float *bias, const flo
     }
     uint32_t *status = nullptr;
     TTL_TRY_CUDA(nullptr, cudaMalloc(&status, sizeof(uint32_t)));
-    cudaMemset(status, 0, sizeof(uint32_t));
     const int smem = int(sizeof(MatvecSmem));
-    cudaFuncSetAttribute(tc_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    tc_matvec_kernel<<<(kDim + 127) / 128, 128, smem>>>((const uint8_t *)packed, bias, x, y, status);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = cudaMemset(status, 0, sizeof(uint32_t));
+    if (e == cudaSuccess) {
+        e = cudaFuncSetAttribute(tc_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    }
+    if (e == cudaSuccess) {
+        tc_matvec_kernel<<<(kDim + 127) / 128, 128, smem>>>((const uint8_t *)packed, bias, x, y, status);
+        e = cudaGetLastError();
+    }
     if (e == cudaSuccess) {
         e = cudaDeviceSynchronize();
     }
     uint32_t st = 0;
     if (e == cudaSuccess) {
-        cudaMemcpy(&st, status, sizeof(st), cudaMemcpyDeviceToHost);
+        e = cudaMemcpy(&st, status, sizeof(st), cudaMemcpyDeviceToHost);
     }
     cudaFree(status);
     if (e != cudaSuccess) {
@@ -222,7 +226,10 @@ extern "C" int ttl_matvec_mxfp4(const void *packed, const float *bias, const flo
 
 // ---- allocation-free variant ----
 // Status words of ttl_matvec_mxfp4_noalloc live in this file-scope array
-// instead of a per-call cudaMalloc: one word per matrix of a call.
+// instead of a per-call cudaMalloc: one word per matrix of a call.  The
+// array's device address is looked up once per device ordinal and kept for
+// the life of the process, so a device reset (cudaDeviceReset, or a context
+// torn down and made again) is not supported for callers of this entry.
 namespace {
 constexpr size_t kNoAllocMaxMatrices = 256;  // 1 KB of scratch per device
 static __device__ __align__(256) uint32_t g_noalloc_status[kNoAllocMaxMatrices];

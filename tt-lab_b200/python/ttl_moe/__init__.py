@@ -99,6 +99,16 @@ def lib():
         "ttl_ttq_close": (None, [vp]),
         "ttl_synth_mxfp4": (i32, [vp, sz, u64, u64, u32, u32]),
         "ttl_synth_normal": (i32, [vp, sz, u64, u64, ctypes.c_float, ctypes.c_float]),
+        "ttl_synth_q8_0": (i32, [vp, sz, u64, u64]),
+        "ttl_head_create": (i32, [i32, u32, ctypes.POINTER(vp)]),
+        "ttl_head_destroy": (None, [vp]),
+        "ttl_head_last_error": (ctypes.c_char_p, [vp]),
+        "ttl_head_upload": (i32, [vp, vp, fp]),
+        "ttl_head_unpack": (i32, [vp, vp]),
+        "ttl_head_forward": (i32, [vp, fp, fp, vp]),
+        "ttl_head_forward_async": (i32, [vp, fp, fp, vp]),
+        "ttl_head_sync": (i32, [vp]),
+        "ttl_head_stream": (vp, [vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -294,6 +304,64 @@ def unpack_mxfp4(packed, matrices, gguf=None, device=0):
         gguf = np.empty(matrices * GGUF_MATRIX_BYTES, np.uint8)
     check(lib().ttl_unpack_mxfp4(_ptr(packed), matrices, _ptr(gguf), device))
     return gguf
+
+
+class Head:
+    """One ttl_head handle: the output head of GptOssModel::forward (rms_norm
+    with output_norm.weight, matvec_q8_0 with output.weight, greedy)."""
+
+    def __init__(self, vocab=201088, device=-1):
+        h = ctypes.c_void_p()
+        check(lib().ttl_head_create(device, vocab, ctypes.byref(h)))
+        self.h = h
+        self.vocab = vocab
+
+    def _check(self, rc):
+        if rc != TTL_OK:
+            msg = lib().ttl_head_last_error(self.h)
+            raise RuntimeError(f"cuda head ({rc}): {msg.decode() if msg else ''}")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().ttl_head_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def upload(self, q8_0, norm_w):
+        self._check(lib().ttl_head_upload(self.h, _ptr(q8_0), _ptr(norm_w)))
+
+    def unpack(self):
+        out = np.empty(self.vocab * (DIM // 32) * 34, np.uint8)
+        self._check(lib().ttl_head_unpack(self.h, _ptr(out)))
+        return out
+
+    def forward(self, x, want_logits=True):
+        """Host x [2880] -> (logits [vocab] or None, token)."""
+        x = np.ascontiguousarray(x, np.float32)
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        tok = np.zeros(1, np.int32)
+        self._check(lib().ttl_head_forward(self.h, _ptr(x), _ptr(logits), _ptr(tok)))
+        return logits, int(tok[0])
+
+    def forward_async(self, x, logits=None, token=None):
+        self._check(lib().ttl_head_forward_async(self.h, _ptr(x), _ptr(logits), _ptr(token)))
+
+    def sync(self):
+        self._check(lib().ttl_head_sync(self.h))
+
+    def stream(self) -> int:
+        return lib().ttl_head_stream(self.h) or 0
 
 
 class TtqWriter:

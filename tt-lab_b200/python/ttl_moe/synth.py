@@ -106,6 +106,26 @@ def layer_device(seed, layer, experts, device="cuda", zipf_s=None, scale_lo=SCAL
     return t
 
 
+HEAD_STREAM = 1 << 36
+
+
+def head_device(seed, rows, device="cuda"):
+    """The output matrix (Q8_0, rows x 2880) and output_norm.weight ~ N(1,
+    0.02) in device memory (torch tensors)."""
+    import torch
+    w = torch.empty(rows * (DIM // 32) * 34, dtype=torch.uint8, device=device)
+    _check(_lib().ttl_synth_q8_0(w.data_ptr(), rows * (DIM // 32), seed, HEAD_STREAM))
+    g = torch.empty(DIM, dtype=torch.float32, device=device)
+    _check(_lib().ttl_synth_normal(g.data_ptr(), DIM, seed, HEAD_STREAM + 1, ctypes.c_float(0.02), ctypes.c_float(1.0)))
+    return {"output_w": w, "output_norm": g}
+
+
+def q8_0_host(blocks, seed, stream_id) -> np.ndarray:
+    out = np.empty(blocks * 34, np.uint8)
+    _check(_lib().ttl_synth_q8_0(out.ctypes.data, blocks, seed, stream_id))
+    return out
+
+
 def inputs_host(seed, tokens, batch=0, sigma=1.0) -> np.ndarray:
     """Activations [tokens, 2880] ~ N(0, sigma)."""
     return normal_host(tokens * DIM, seed, INPUT_STREAM_BASE + batch, sigma).reshape(tokens, DIM)
