@@ -100,6 +100,16 @@ int ttl_moe_upload_layer(ttl_moe *handle, int layer, const float *router_w, cons
                          const void *gate_w, const float *gate_b, const void *up_w, const float *up_b,
                          const void *down_w, const float *down_b);
 
+/* ttl_moe_upload_layer with the expert matrices already in the GPU layout:
+ * gate/up/down_packed are TTL_TTQ_FORMAT_MXFP4_GPU payloads of all E experts
+ * (ttl_packed_bytes(E) bytes each, as ttl_requant_gpu writes them); the rest
+ * as for ttl_moe_upload_layer.  A scale byte of 255 is refused the same way.
+ * Counterpart: the expert-weight binding from tt-lab's TtqFile
+ * (src/tt_backend.cpp:315-445).  Synchronous. */
+int ttl_moe_upload_layer_packed(ttl_moe *handle, int layer, const float *router_w, const float *router_b,
+                                const void *gate_packed, const float *gate_b, const void *up_packed,
+                                const float *up_b, const void *down_packed, const float *down_b);
+
 /* Post-attention RMSNorm weights (blk.N.post_attention_norm.weight, f32 [2880])
  * applied by ttl_moe_forward before layer `layer`'s MoE.  Default: all ones. */
 int ttl_moe_upload_norm(ttl_moe *handle, int layer, const float *norm_w);
@@ -224,6 +234,7 @@ int ttl_unpack_mxfp4(const void *packed, size_t matrices, void *gguf, int device
 /* ---- TTQ container (TTLBQNT1, src/requant.h:31-52) ----------------------- */
 
 #define TTL_TTQ_FORMAT_MXFP4_GPU 6 /* new format id next to tt-lab's 1..5 */
+#define TTL_TTQ_FORMAT_F32 7       /* an f32 tensor exactly as the GGUF stores it */
 
 typedef struct ttl_ttq_writer ttl_ttq_writer;
 
@@ -238,6 +249,16 @@ int ttl_ttq_add(ttl_ttq_writer *writer, const char *name, uint32_t format, uint3
 int ttl_ttq_finish(ttl_ttq_writer *writer);
 /* Frees the writer; an unfinished file is removed. */
 void ttl_ttq_close(ttl_ttq_writer *writer);
+
+/* requant --cuda: reads a gpt-oss GGUF (v3) and writes, atomically, a TTQ
+ * file with the MoE tensors of layers [layer_begin, layer_end) (layer_end -1:
+ * all): per layer ffn_gate_inp.{weight,bias} and ffn_{gate,up,down}_exps.bias
+ * as TTL_TTQ_FORMAT_F32 records under their GGUF names, and the three expert
+ * matrices packed on `device` as TTL_TTQ_FORMAT_MXFP4_GPU records named
+ * "<GGUF name>.mxfp4gpu".  The header carries the model (20 / 120), layer and
+ * expert counts, dim and vocab, so tt-lab's TtqFile reads the file.
+ * Counterpart: write_requant (src/requant.cpp:415-504). */
+int ttl_requant_gpu(const char *gguf_path, const char *ttq_path, int layer_begin, int layer_end, int device);
 
 /* ---- output head (logits) ---------------------------------------------- */
 

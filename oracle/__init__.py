@@ -284,3 +284,63 @@ def compare(a, b):
         "rel_rms": float(np.sqrt(np.mean(err * err)) / max(rms_b, 1e-30)),
         "cosine": float(np.dot(a, b) / max(np.sqrt(np.dot(a, a) * np.dot(b, b)), 1e-30)),
     }
+
+
+# ---- tt-lab's TTQ reader (TtqFile, src/tt_backend.cpp:315-445) ----
+TTQ_PATH = HERE / "_ref" / "libttlttq.so"
+_ttq = None
+
+
+def ttq_available() -> bool:
+    return TTQ_PATH.exists()
+
+
+def _ttq_lib():
+    global _ttq
+    if _ttq is None:
+        if not TTQ_PATH.exists():
+            raise OSError(f"TTQ reader not built: {TTQ_PATH} (make -C oracle ttq)")
+        L = ctypes.CDLL(str(TTQ_PATH))
+        vp, sz = ctypes.c_void_p, ctypes.c_size_t
+        L.tref_ttq_last_error.restype = ctypes.c_char_p
+        L.tref_ttq_open.restype = vp
+        L.tref_ttq_open.argtypes = [ctypes.c_char_p]
+        L.tref_ttq_close.argtypes = [vp]
+        L.tref_ttq_count.restype = sz
+        L.tref_ttq_count.argtypes = [vp]
+        L.tref_ttq_layers.restype = sz
+        L.tref_ttq_layers.argtypes = [vp]
+        L.tref_ttq_record.argtypes = [vp, sz, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                                      ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
+        _ttq = L
+    return _ttq
+
+
+def ttq_read(path):
+    """Every record of a TTQ file as tt-lab's TtqFile parses it: a list of
+    dicts (name, format, shape, payload as a read-only numpy view).  The file
+    stays mapped while the returned object lives."""
+    L = _ttq_lib()
+    f = L.tref_ttq_open(str(path).encode())
+    if not f:
+        raise RuntimeError("TtqFile: " + L.tref_ttq_last_error().decode())
+
+    class Mapped(list):
+        def __del__(self):
+            L.tref_ttq_close(f)
+
+    out = Mapped()
+    out.layers = int(L.tref_ttq_layers(f))
+    name = ctypes.create_string_buffer(128)
+    fmt, rank = ctypes.c_uint32(), ctypes.c_uint32()
+    shape = (ctypes.c_uint64 * 4)()
+    data, size = ctypes.c_void_p(), ctypes.c_uint64()
+    for i in range(int(L.tref_ttq_count(f))):
+        L.tref_ttq_record(f, i, name, ctypes.byref(fmt), ctypes.byref(rank), shape, ctypes.byref(data),
+                          ctypes.byref(size))
+        buf = (ctypes.c_uint8 * size.value).from_address(data.value) if size.value else (ctypes.c_uint8 * 0)()
+        out.append({"name": name.value.decode(), "format": fmt.value,
+                    "shape": [int(shape[d]) for d in range(rank.value)],
+                    "payload": np.frombuffer(buf, np.uint8)})
+    return out

@@ -58,6 +58,8 @@ void launch_add(const float *residual, const float *moe, float *out, int n, cuda
 // a scale byte is 255.
 void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, cudaStream_t stream,
                  uint32_t *flags = nullptr);
+// Sets bit 0 of *flags when a scale byte of `matrices` packed matrices is 255.
+void launch_scan_scales(const uint8_t *packed_dev, size_t matrices, cudaStream_t stream, uint32_t *flags);
 
 // ---- persistent decode (decode_tc.cu) ----
 // A CUtensorMap, kept opaque here (128 bytes, 64-byte aligned).

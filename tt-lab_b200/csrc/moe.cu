@@ -1069,9 +1069,15 @@ void ttl_moe_destroy(ttl_moe *h) {
     delete h;
 }
 
-int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const float *router_b, const void *gate_w,
-                         const float *gate_b, const void *up_w, const float *up_b, const void *down_w,
-                         const float *down_b) {
+} // extern "C"
+
+namespace {
+
+// Both uploads: GGUF blocks are packed on the device; packed payloads
+// (TTL_TTQ_FORMAT_MXFP4_GPU) are copied and only their scales checked.
+int upload_layer(ttl_moe *h, int layer, const float *router_w, const float *router_b, const void *gate_w,
+                 const float *gate_b, const void *up_w, const float *up_b, const void *down_w, const float *down_b,
+                 bool packed) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
@@ -1101,7 +1107,7 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
             return rc;
         }
     }
-    const size_t expert_gguf = size_t(kDim) * kGgufRowBytes;
+    const size_t expert_gguf = packed ? kPackedMatrixBytes : size_t(kDim) * kGgufRowBytes;
     const size_t first = size_t(h->expert_begin);
     TTL_TRY_CUDA(h, cudaMemcpy(s.router_w, router_w, E * kDim * sizeof(float), cudaMemcpyDefault));
     TTL_TRY_CUDA(h, cudaMemcpy(s.router_b, router_b, E * sizeof(float), cudaMemcpyDefault));
@@ -1114,7 +1120,8 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
         const uint8_t *src = (const uint8_t *)srcs[m] + first * expert_gguf;
         if (!is_device_pointer(srcs[m])) {
             if (!h->staging) {
-                h->staging_bytes = El * expert_gguf;
+                // sized for either input layout, so GGUF and packed uploads can be mixed on one handle
+                h->staging_bytes = El * std::max(kPackedMatrixBytes, size_t(kDim) * kGgufRowBytes);
                 rc = alloc(h, reinterpret_cast<void **>(&h->staging), h->staging_bytes);
                 if (rc) {
                     return rc;
@@ -1124,7 +1131,12 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
             src = h->staging;
         }
         TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_pack_flags, 0, sizeof(uint32_t), h->stream));
-        launch_pack(src, dsts[m], El, h->stream, h->d_pack_flags);
+        if (packed) {
+            TTL_TRY_CUDA(h, cudaMemcpyAsync(dsts[m], src, El * kPackedMatrixBytes, cudaMemcpyDefault, h->stream));
+            launch_scan_scales(dsts[m], El, h->stream, h->d_pack_flags);
+        } else {
+            launch_pack(src, dsts[m], El, h->stream, h->d_pack_flags);
+        }
         TTL_TRY_CUDA(h, cudaGetLastError());
         uint32_t flags = 0;
         TTL_TRY_CUDA(h, cudaMemcpyAsync(&flags, h->d_pack_flags, sizeof(flags), cudaMemcpyDeviceToHost, h->stream));
@@ -1140,6 +1152,24 @@ int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const flo
     const int prc = push_layer_descriptor(h, layer);
     return prc ? prc : capture_decode_graph(h, layer);
 }
+
+} // namespace
+
+extern "C" {
+
+int ttl_moe_upload_layer(ttl_moe *h, int layer, const float *router_w, const float *router_b, const void *gate_w,
+                         const float *gate_b, const void *up_w, const float *up_b, const void *down_w,
+                         const float *down_b) {
+    return upload_layer(h, layer, router_w, router_b, gate_w, gate_b, up_w, up_b, down_w, down_b, false);
+}
+
+int ttl_moe_upload_layer_packed(ttl_moe *h, int layer, const float *router_w, const float *router_b,
+                                const void *gate_packed, const float *gate_b, const void *up_packed, const float *up_b,
+                                const void *down_packed, const float *down_b) {
+    return upload_layer(h, layer, router_w, router_b, gate_packed, gate_b, up_packed, up_b, down_packed, down_b, true);
+}
+
+
 
 int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
     if (!h) {

@@ -89,6 +89,17 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ packed, uint8_t *__res
     }
 }
 
+__global__ void scan_scales_kernel(const uint8_t *packed, size_t matrices, uint32_t *flags) {
+    const size_t per = kPackedMatrixBytes - kNibbleBytes;  // the scale region of a matrix
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < matrices * per;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const size_t m = i / per;
+        if (packed[m * kPackedMatrixBytes + kNibbleBytes + (i - m * per)] == 255u) {
+            atomicOr(flags, 1u);
+        }
+    }
+}
+
 __global__ void synth_mxfp4_kernel(uint8_t *dst, size_t blocks, uint64_t key, uint32_t lo, uint32_t count) {
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < blocks; i += size_t(gridDim.x) * blockDim.x) {
         uint8_t *out = dst + i * 17;
@@ -215,6 +226,15 @@ void launch_pack(const uint8_t *gguf_dev, uint8_t *packed_dev, size_t matrices, 
         // scale padding (K-blocks 90, 91; rows 2880..2943; the region's tail) is zero
         cudaMemset2DAsync(packed_dev + kNibbleBytes, kPackedMatrixBytes, 0, kScaleBytes, matrices, stream);
         pack_kernel<<<grid_for(blocks), 256, 0, stream>>>(gguf_dev, packed_dev, blocks, flags);
+    }
+}
+} // namespace ttl
+
+namespace ttl {
+void launch_scan_scales(const uint8_t *packed_dev, size_t matrices, cudaStream_t stream, uint32_t *flags) {
+    const size_t n = matrices * (kPackedMatrixBytes - kNibbleBytes);
+    if (n) {
+        scan_scales_kernel<<<grid_for(n), 256, 0, stream>>>(packed_dev, matrices, flags);
     }
 }
 } // namespace ttl

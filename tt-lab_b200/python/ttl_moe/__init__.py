@@ -26,6 +26,7 @@ BLOCK_BYTES = 17
 GGUF_MATRIX_BYTES = DIM * (DIM // 32) * BLOCK_BYTES  # 4,406,400
 NCCL_ID_BYTES = 128
 TTQ_FORMAT_MXFP4_GPU = 6
+TTQ_FORMAT_F32 = 7
 
 TTL_OK = 0
 TTL_ERR_ARGUMENT = -1
@@ -75,6 +76,8 @@ def lib():
         "ttl_moe_destroy": (None, [vp]),
         "ttl_moe_upload_layer": (i32, [vp, i32, fp, fp, vp, fp, vp, fp, vp, fp]),
         "ttl_moe_upload_norm": (i32, [vp, i32, fp]),
+        "ttl_moe_upload_layer_packed": (i32, [vp, i32, fp, fp, vp, fp, vp, fp, vp, fp]),
+        "ttl_requant_gpu": (i32, [ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]),
         "ttl_moe_decode": (i32, [vp, i32, fp, fp, vp, fp]),
         "ttl_moe_prefill": (i32, [vp, i32, fp, sz, fp, vp, fp]),
         "ttl_moe_forward": (i32, [vp, i32, i32, fp, fp, sz]),
@@ -192,6 +195,15 @@ class MoE:
         if t.get("norm_w") is not None:
             self._check(lib().ttl_moe_upload_norm(self.h, layer, _ptr(t["norm_w"])))
 
+    def upload_layer_packed(self, layer, t):
+        """Binds layer `layer` from GPU-layout expert payloads (keys gate_p,
+        up_p, down_p: TTQ format-6 bytes of all experts) and the f32 tensors."""
+        self._check(lib().ttl_moe_upload_layer_packed(
+            self.h, layer, _ptr(t["router_w"]), _ptr(t["router_b"]), _ptr(t["gate_p"]), _ptr(t["gate_b"]),
+            _ptr(t["up_p"]), _ptr(t["up_b"]), _ptr(t["down_p"]), _ptr(t["down_b"])))
+        if t.get("norm_w") is not None:
+            self._check(lib().ttl_moe_upload_norm(self.h, layer, _ptr(t["norm_w"])))
+
     def moe(self, layer, x):
         """GptOssModel::moe on host f32 [2880]; returns (out, top4 idx, top4 weights)."""
         x = np.ascontiguousarray(x, dtype=np.float32)
@@ -284,6 +296,11 @@ def pack_mxfp4(gguf, matrices, packed=None, device=0):
         packed = np.empty(packed_bytes(matrices), np.uint8)
     check(lib().ttl_pack_mxfp4(_ptr(gguf), matrices, _ptr(packed), device))
     return packed
+
+
+def requant_gpu(gguf_path, ttq_path, layer_begin=0, layer_end=-1, device=0):
+    """requant --cuda: a gpt-oss GGUF to a TTQ file with GPU-layout experts."""
+    check(lib().ttl_requant_gpu(str(gguf_path).encode(), str(ttq_path).encode(), layer_begin, layer_end, device))
 
 
 def matvec_mxfp4(packed, bias, x, y, device=0):
