@@ -428,6 +428,99 @@ def logits_head(torch, ttl_moe, synth, hbm_peak, iters=20, cpu_seconds=6.0):
                        "what": "logits bit-equal to tt-lab's (NaN positions equal) and the same greedy token"}}
 
 
+# Algorithmic bytes of one attention block at a given number of attended
+# positions: Q8_0 Q / K / V (4096 + 512 + 512 rows of 2880) and output (2880
+# rows of 4096), their biases, attn_norm and sinks, x in / residual out, the
+# new K / V row written, and K / V of every attended position read (f32).
+ATTN_WEIGHT_BYTES = (4096 + 512 + 512) * 90 * 34 + DIM * 128 * 34 + (4096 + 512 + 512 + DIM) * 4 + DIM * 4 + 64 * 4
+
+
+def attn_bytes(attended):
+    return ATTN_WEIGHT_BYTES + 2 * DIM * 4 + 2 * 512 * 4 + attended * 2 * 512 * 4
+
+
+def attention_decode(torch, ttl_moe, synth, hbm_peak, context=1024, layers=24, iters=10):
+    """the attention block of a 20b decode layer on the
+    GPU (ttl_attn), on seeded synthetic weights, at `context` positions
+    already in the KV cache: device time per layer (CUDA events on the
+    handle's stream over all `layers` layers of one token; even layers attend
+    to 128 positions, odd ones to all), and a whole GPU-resident decode token
+    -- per layer attention then the MoE half (rms_norm -> moe -> residual,
+    ttl_moe_forward) on one stream, then the output head -- in tokens/s.
+    Parity of the attention block: tests/test_gpu_attn.py."""
+    dev = torch.cuda.current_device()
+    attn_t = [synth.attention_layer_host(5, l) for l in range(layers)]
+    with ttl_moe.MoE(experts=32, layers=layers, device=dev) as m, \
+            ttl_moe.Attention(layers=layers, token_capacity=context + iters + 8, device=dev, stream=m.stream()) as a, \
+            ttl_moe.Head(vocab=VOCAB, device=dev) as h:
+        for l in range(layers):
+            a.upload_layer(l, attn_t[l])
+            t = synth.layer_device(0, l, 32, device="cuda")
+            m.upload_layer(l, t)
+            del t
+        ht = synth.head_device(0, VOCAB)
+        h.upload(ht["output_w"], ht["output_norm"])
+        del ht
+        torch.cuda.empty_cache()
+        xs = torch.from_numpy(synth.inputs_host(11, 8)).cuda()
+        buf = torch.empty((2, DIM), dtype=torch.float32, device="cuda")
+        logits = torch.empty(VOCAB, dtype=torch.float32, device="cuda")
+        tok = torch.empty(1, dtype=torch.int32, device="cuda")
+        # fill the caches to `context` positions (attention only)
+        for p in range(context):
+            for l in range(layers):
+                a.forward_async(l, p, xs[p % 8], buf[0])
+        a.sync()
+        st = torch.cuda.ExternalStream(m.stream())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p = context
+        e0.record(st)
+        for i in range(iters):
+            for l in range(layers):
+                a.forward_async(l, p, xs[i % 8], buf[0])
+            p += 1
+        e1.record(st)
+        e1.synchronize()
+        attn_ms = e0.elapsed_time(e1) / (iters * layers)
+        # whole tokens: attention -> MoE half per layer, then the head (on
+        # its own stream, after an event of the MoE stream)
+        hst = torch.cuda.ExternalStream(h.stream())
+        ev = torch.cuda.Event()
+
+        def token(p):
+            x = xs[p % 8]
+            for l in range(layers):
+                a.forward_async(l, p, x, buf[0])
+                m.forward_async(l, l + 1, buf[0], buf[1], 1)
+                x = buf[1]
+            ev.record(st)
+            hst.wait_event(ev)
+            h.forward_async(x, logits, tok)
+        token(p)
+        p += 1
+        h.sync()
+        m.sync()
+        t0 = time.perf_counter()
+        for i in range(iters):
+            token(p)
+            p += 1
+            h.sync()  # the head runs on its own stream; the next token's input waits for it
+        tok_ms = (time.perf_counter() - t0) / iters * 1e3
+        del hst
+    avg_attended = (128 + context) / 2
+    gbs = attn_bytes(avg_attended) / (attn_ms * 1e-3) / 1e9
+    return {"workload": f"gpt-oss-20b attention block, {layers} layers, context {context} (even layers: window "
+                        f"128), synthetic Q8_0 weights",
+            "ms_per_layer": attn_ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "bytes_per_layer": attn_bytes(avg_attended),
+                         "kernels": "attn_qkv_kernel + attn_decode_kernel + attn_out_kernel, CUDA events"},
+            "decode_token": {"ms_per_token": tok_ms, "tokens_per_s": 1e3 / tok_ms,
+                             "what": "one token through 24 x (attention + rms_norm -> MoE -> residual) and the "
+                                     "output head, all on the GPU (wall clock per token, host waits for the "
+                                     "greedy token)"}}
+
+
 # Algorithmic bytes of one gpt-oss-120b decode token-layer (E = 128): router W
 # + bias, 12 expert matrices + their biases, x / out.
 LAYER_BYTES_120B = 128 * DIM * 4 + 128 * 4 + 12 * GGUF_MATRIX + 12 * BIAS + 2 * DIM * 4
@@ -543,6 +636,8 @@ def main():
     ap.add_argument("--no-parity", action="store_true", help="skip the parity sample checked after timing")
     ap.add_argument("--no-head", action="store_true", help="skip the output-head (logits) measurement")
     ap.add_argument("--no-120b", action="store_true", help="skip the cfg3 (120b, 36-layer) decode line")
+    ap.add_argument("--no-attention", action="store_true",
+                    help="skip the attention block / GPU-resident decode token measurement")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the cfg2 prefill measurement (one JSON line with its figures)")
     args = ap.parse_args()
@@ -696,6 +791,11 @@ def main():
                                cpu_seconds=0.0 if args.no_cpu_baseline else 6.0)
         except OSError as e:  # the checker is not built on this machine
             head = {"unavailable": str(e)}
+    attention = None
+    if world == 1 and not args.no_attention:
+        moe.close()
+        torch.cuda.empty_cache()
+        attention = attention_decode(torch, ttl_moe, synth, peaks()[0])
     decode_120b = None
     if not args.no_120b:
         moe.close()
@@ -756,6 +856,7 @@ def main():
             "prefill": prefill,
             "prefill_ep": prefill_ep,
             "logits_head": head,
+            "attention": attention,
             "decode_120b": decode_120b,
         }
         print(json.dumps(line))

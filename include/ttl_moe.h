@@ -29,7 +29,7 @@
  * in ttl_moe_destroy ("allocate dynamic memory at startup only", tt-lab
  * AGENTS.md).  The compute calls allocate nothing, with one exception: the
  * first ttl_moe_forward / ttl_moe_forward_async call for a new (buffers, token
- * count, layer range) captures and instantiates a CUDA graph for it (at most 16
+ * count, layer range) captures and instantiates a CUDA graph for it (at most 64
  * are kept, least recently used dropped).  The diagnostic calls
  * (ttl_moe_profile, ttl_moe_trace, ttl_moe_record) recapture graphs.
  * Threading: one host thread per handle; calls on one handle are serialised on
@@ -152,6 +152,22 @@ int ttl_moe_forward_async(ttl_moe *handle, int layer_begin, int layer_end, const
 /* Waits for the handle's stream, then checks the device status word that the
  * kernels set on a bounds or bounded-wait failure (TTL_ERR_DEVICE). */
 int ttl_moe_sync(ttl_moe *handle);
+
+/* Expert parallelism (world > 1): failures and recovery.
+ * Every compute call is collective: each rank makes the same calls in the
+ * same order.  After any call on a multi-rank handle returns an error (on
+ * this rank: a rejected argument, a failed launch, a device timeout waiting
+ * for a peer), the handle refuses compute calls with TTL_ERR_STATE until
+ * every rank has called ttl_moe_resync, which brings the ranks' kernel tag
+ * bases and peer-memory flags back into agreement (two NCCL collectives).
+ * The kernels' waits on peers are bounded on the device (2 s, then
+ * TTL_ERR_DEVICE).  The communicator is nonblocking and every host wait on it
+ * or on the handle's stream is bounded by the handle's timeout (default
+ * 60000 ms); past it the communicator is aborted (TTL_ERR_NCCL), after which
+ * the handle refuses everything but ttl_moe_destroy.  World 1:
+ * ttl_moe_resync waits for the stream and clears the status word. */
+int ttl_moe_resync(ttl_moe *handle);
+int ttl_moe_set_timeout(ttl_moe *handle, uint32_t milliseconds);
 
 /* The handle's cudaStream_t, as void *. */
 void *ttl_moe_stream(ttl_moe *handle);

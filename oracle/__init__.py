@@ -66,6 +66,9 @@ def port():
         L.oref_greedy.restype = ctypes.c_int32
         L.oref_half_to_float.argtypes = [ctypes.c_uint16]
         L.oref_half_to_float.restype = ctypes.c_float
+        L.oref_attention_step.argtypes = [ctypes.POINTER(_AttnLayer), sz, sz, vp, vp, sz, vp, vp, vp]
+        L.oref_attention_step.restype = i32
+        L.oref_rope_frequencies.argtypes = [vp]
         _port = L
     return _port
 
@@ -95,8 +98,48 @@ def ref():
         L.tref_forward_tokens.argtypes = [sz, sz, vp, vp, vp, vp, sz, i32]
         L.tref_matvec_q8_0.argtypes = [vp, sz, vp, vp, vp]
         L.tref_greedy.argtypes = [vp, vp]
+        L.tref_attention_steps.argtypes = [ctypes.POINTER(vp), i32, sz, vp, vp, vp]
         _ref = L
     return _ref
+
+
+class _AttnLayer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b",
+                                               "sinks")]
+
+
+ATTN_TENSORS = ("attn_norm", "q_w", "q_b", "k_w", "k_b", "v_w", "v_b", "o_w", "o_b", "sinks")
+
+
+def attention_steps(t, layer_index, x, impl="port"):
+    """The attention block of GptOssModel::forward (src/model.cpp:578-590)
+    for positions 0 .. P-1 of one layer (even index: sliding window), x
+    [P][2880] one row per position.  Returns (residual [P][2880], attended
+    [P][4096]).  impl "port": the C restatement (attn_oracle.c); "ref": tt-lab's
+    own code (tref_attention_steps)."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, DIM)
+    P = x.shape[0]
+    res = np.empty((P, DIM), np.float32)
+    att = np.empty((P, 4096), np.float32)
+    if impl == "ref":
+        ptrs = (ctypes.c_void_p * 10)(*[t[n].ctypes.data for n in ATTN_TENSORS])
+        _ref_check(ref().tref_attention_steps(ptrs, layer_index, P, _p(x), _p(res), _p(att)))
+        return res, att
+    L = _AttnLayer(*[t[n].ctypes.data for n in ATTN_TENSORS])
+    kc = np.zeros((P, 512), np.float32)
+    vc = np.zeros((P, 512), np.float32)
+    for p in range(P):
+        rc = port().oref_attention_step(ctypes.byref(L), layer_index, p, _p(kc), _p(vc), P, _p(x[p]), _p(res[p]),
+                                        _p(att[p]))
+        if rc != 0:
+            raise RuntimeError("oref_attention_step failed")
+    return res, att
+
+
+def rope_frequencies():
+    f = np.empty(32, np.float32)
+    port().oref_rope_frequencies(_p(f))
+    return f
 
 
 def _ref_check(rc):

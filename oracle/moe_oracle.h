@@ -77,6 +77,34 @@ void oref_matvec_q8_0(const uint8_t *w, const float *x, float *y, size_t rows);
 int32_t oref_greedy(const float *logits, size_t n);
 float oref_half_to_float(uint16_t h);
 
+/* Attention block (oracle/attn_oracle.c; src/model.cpp:578-590 with the
+ * constants of src/model.h:36-50). */
+enum {
+    OREF_HEAD_SIZE = 64,
+    OREF_QUERY_HEADS = 64,
+    OREF_KV_HEADS = 8,
+    OREF_QUERY_WIDTH = 4096,
+    OREF_KV_WIDTH = 512,
+    OREF_SLIDING_WINDOW = 128
+};
+typedef struct {
+    const float *attn_norm;                 /* [2880] attn_norm.weight */
+    const uint8_t *q_w; const float *q_b;   /* Q8_0 [4096 rows][90 blocks][34 B]; [4096] */
+    const uint8_t *k_w; const float *k_b;   /* [512 rows]; [512] */
+    const uint8_t *v_w; const float *v_b;   /* [512 rows]; [512] */
+    const uint8_t *o_w; const float *o_b;   /* Q8_0 [2880 rows][128 blocks][34 B]; [2880] */
+    const float *sinks;                     /* [64] attn_sinks.weight */
+} oref_attn_layer;
+
+void oref_matvec_add_q8_0(const uint8_t *w, const float *bias, const float *x, float *y, size_t rows,
+                          size_t cols);
+void oref_rope_frequencies(float freq[OREF_HEAD_SIZE / 2]);
+void oref_apply_rope(float *v, size_t heads, size_t position, const float freq[OREF_HEAD_SIZE / 2]);
+void oref_attention(size_t layer_index, size_t position, const float *q, const float *k_cache, const float *v_cache,
+                    const float *sinks, float *scores, float *out);
+int oref_attention_step(const oref_attn_layer *layer, size_t layer_index, size_t position, float *k_cache,
+                        float *v_cache, size_t capacity, const float *x, float *residual, float *attended);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,6 +77,15 @@ struct TagTensors {
 struct TagRouter {
     friend auto member(TagRouter);
 };
+struct TagRope {
+    friend auto member(TagRope);
+};
+struct TagStoreKv {
+    friend auto member(TagStoreKv);
+};
+struct TagAttend {
+    friend auto member(TagAttend);
+};
 
 } // namespace
 
@@ -89,6 +98,9 @@ template struct Expose<TagIndicesSeq, &GptOssModel::expert_indices_sequence_>;
 template struct Expose<TagWeightsSeq, &GptOssModel::expert_weights_sequence_>;
 template struct Expose<TagTensors, &GgufFile::tensors_>;
 template struct Expose<TagRouter, &GptOssModel::router_>;
+template struct Expose<TagRope, &GptOssModel::apply_rope>;
+template struct Expose<TagStoreKv, &GptOssModel::store_kv>;
+template struct Expose<TagAttend, &GptOssModel::attention_from_cache>;
 
 namespace {
 
@@ -408,6 +420,55 @@ void matmul_default(const GgufTensor &, const GgufTensor &, const float *, const
 
 
 extern "C" {
+
+// The attention block of GptOssModel::forward (src/model.cpp:578-590) for
+// positions 0 .. positions-1 of layer `layer_index` (even: a sliding-window
+// layer, odd: a full one), through tt-lab's own code: rms_norm,
+// matvec_add_q8_0 for Q / K / V, the model's apply_rope, store_kv and
+// attention_from_cache, matvec_add_q8_0 for the output, residual add.  The
+// layer's attention tensors are aimed at the caller's ten buffers (attn_norm,
+// q_w, q_b, k_w, k_b, v_w, v_b, o_w, o_b, sinks).  x and residual are
+// [positions][2880]; attended (optional) [positions][4096].
+int tref_attention_steps(const void *const *tensors, int layer_index, size_t positions, const float *x,
+                         float *residual, float *attended) {
+    return guarded([&] {
+        if (layer_index < 0 || layer_index > 1 || positions == 0) {
+            throw std::runtime_error("layer_index must be 0 or 1 and positions > 0");
+        }
+        const std::string path = write_fixture(32);
+        GgufFile file(path.c_str());
+        static const char *const names[10] = {"attn_norm.weight", "attn_q.weight",      "attn_q.bias",
+                                              "attn_k.weight",    "attn_k.bias",        "attn_v.weight",
+                                              "attn_v.bias",      "attn_output.weight", "attn_output.bias",
+                                              "attn_sinks.weight"};
+        const std::string b = "blk." + std::to_string(layer_index) + ".";
+        for (int k = 0; k < 10; ++k) {
+            find_tensor(file, b + names[k])->data = (const std::byte *)tensors[k];
+        }
+        GptOssModel model(file, positions, std::string(), 1);
+        auto &layer = (model.*member(TagLayers{}))[size_t(layer_index)];
+        std::vector<float> normalized(kDim), q(4096), k(512), v(512), att(4096), proj(kDim);
+        for (size_t p = 0; p < positions; ++p) {
+            const float *xp = x + p * kDim;
+            rms_norm(xp, *layer.attention_norm, 1.0e-5f, normalized.data());
+            matvec_add_q8_0(*layer.query_weight, *layer.query_bias, normalized.data(), q.data());
+            matvec_add_q8_0(*layer.key_weight, *layer.key_bias, normalized.data(), k.data());
+            matvec_add_q8_0(*layer.value_weight, *layer.value_bias, normalized.data(), v.data());
+            (model.*member(TagRope{}))(q.data(), 64, p);
+            (model.*member(TagRope{}))(k.data(), 8, p);
+            (model.*member(TagStoreKv{}))(layer, p, k.data(), v.data());
+            (model.*member(TagAttend{}))(layer, size_t(layer_index), p, q.data(), att.data());
+            matvec_add_q8_0(*layer.attention_output_weight, *layer.attention_output_bias, att.data(), proj.data());
+            for (size_t j = 0; j < kDim; ++j) {
+                residual[p * kDim + j] = xp[j] + proj[j];
+            }
+            if (attended) {
+                std::memcpy(attended + p * 4096, att.data(), 4096 * sizeof(float));
+            }
+        }
+        unlink(path.c_str());
+    });
+}
 
 const char *tref_last_error() {
     return g_error.c_str();

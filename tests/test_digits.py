@@ -1,7 +1,8 @@
 """The prefill B operand's digit encoding (tt-lab_b200/csrc/prefill_tc.cu),
 restated in numpy and checked exhaustively on CPU.
 
-A K-block value with magnitude m (17 bits, |v| * 2^(16 - e) truncated) is
+A K-block value with magnitude m = |v| * 2^(16 - e) rounded to nearest (e the
+exponent of the block's largest |v|, so 0 <= m <= 2^17) is
 written as six balanced radix-8 digits c_d in [-4, 4], m = sum_d c_d 8^d,
 each an exact E2M1 value with the sign of v applied, digit row d scaled by
 2^(e - 16 + 3d).  radix8_codes computes the six E2M1 codes per nibble
@@ -12,7 +13,7 @@ both signs, and the reconstruction to m exactly.
 import numpy as np
 
 E2M1 = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], np.float64)
-ALL = np.arange(1 << 17, dtype=np.int64)
+ALL = np.arange((1 << 17) + 1, dtype=np.int64)  # every magnitude, 2^17 included
 
 
 def digits_loop(m):
@@ -90,3 +91,18 @@ def test_digit_scales():
         # a normal block (code = e + 127) gives row d the scale 2^(e - 16 + 3d)
         e = np.arange(-100, 100)
         assert np.array_equal(np.maximum(e + 127 - (16 - 3 * d), 0) - 127, e - 16 + 3 * d)
+
+
+def test_rounded_magnitudes_stay_within_the_digits_and_half_a_step():
+    """m = rint(|v| 2^(16-e)) for the block maximum's exponent e: m <= 2^17
+    (what six balanced digits hold), and |v - m 2^(e-16)| <= 2^(e-17)."""
+    rng = np.random.default_rng(5)
+    v = rng.standard_normal((4096, 32)).astype(np.float32) * np.float32(2.0) ** rng.integers(-60, 60, (4096, 1))
+    v[0, :] = np.nextafter(np.float32(2.0), np.float32(0))  # the largest value below a power of two rounds up to 2^17
+    mb = np.abs(v).max(axis=1, keepdims=True)
+    e = np.floor(np.log2(mb.astype(np.float64)))
+    m = np.rint(np.abs(v).astype(np.float64) * 2.0 ** (16 - e))
+    assert m.max() == 1 << 17
+    c = digits_loop(m.astype(np.int64).ravel())
+    assert c[:, 5].max() <= 4
+    assert np.all(np.abs(np.abs(v) - m * 2.0 ** (e - 16)) <= 2.0 ** (e - 17))

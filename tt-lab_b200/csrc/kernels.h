@@ -184,6 +184,11 @@ struct PrefillWork {
     uint8_t *bdig_dn;         // the down B operand (SwiGLU output per slot), same layout, written by
     uint8_t *bsfb_dn;         //   the gate/up epilogue, and its scale blocks
     uint32_t *status;
+    // expert parallelism: the rows are [world][seg_rows] (one region per
+    // source rank), row t live iff t % seg_rows < seg_count[t / seg_rows];
+    // seg_count == nullptr: every row is live
+    const int32_t *seg_count;
+    int seg_rows;
 };
 
 struct PrefillShape {
@@ -215,19 +220,59 @@ constexpr size_t kPrefillUnitBytes = size_t(96) * 192 * 16;
 constexpr size_t kPrefillUnitScaleBytes = size_t(24) * 2 * 512;
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream);
 
-// Expert-parallel prefill (prefill_ep.cu): dispatch plan, pack, return and
-// owner combine around the expert pipeline.  Row offsets per rank, by value.
-struct EpOffsets {
-    int v[kMaxWorld];
+// Expert-parallel prefill over peer memory (prefill_ep.cu).  Every rank
+// holds one receive block (an IPC allocation mapped by every peer), laid out
+// identically on all ranks for a given (world, cap):
+struct EpInbox {
+    float *x;                  // [world][cap][2880] token rows, by source rank
+    int32_t *idx;              // [world][cap][4] their top-4 expert ids
+    float *w;                  // [world][cap][4] and weights
+    int32_t *src;              // [world][cap] each row's token index on its source rank
+    float *back;               // [cap][4][2880] w * down of this rank's own tokens, by (token, rank q)
+    unsigned long long *cnt;   // [world] tagged (call tag, rows sent) from each source rank
+    unsigned long long *done;  // [world] tagged (call tag, 0): each rank has written its rows back
 };
-void launch_ep_plan(const int32_t *idx, int tokens, int world, int per_rank, int32_t *tok_off, int32_t *pair_off,
-                    int32_t *cnt, cudaStream_t stream);
-void launch_ep_pack(const float *x, const int32_t *idx, const float *wts, int tokens, int world,
-                    const int32_t *tok_off, const EpOffsets &send_off, float *sendx, int32_t *send_idx,
-                    float *send_w, cudaStream_t stream);
-void launch_ep_return(const PrefillWork &w, int tokens, int rank, int per_rank, int32_t *ret_off, float *ret,
-                      cudaStream_t stream);
-void launch_ep_combine(const int32_t *idx, int tokens, int world, int per_rank, const int32_t *pair_off,
-                       const EpOffsets &back_off, const float *back, float *out, cudaStream_t stream);
+__host__ __device__ constexpr size_t ep_align256(size_t v) {
+    return (v + 255) & ~size_t(255);
+}
+inline size_t ep_inbox_bytes(int world, int cap) {
+    const size_t rows = size_t(world) * size_t(cap);
+    return ep_align256(rows * kDim * 4) + ep_align256(rows * 16) + ep_align256(rows * 16) + ep_align256(rows * 4) +
+           ep_align256(size_t(cap) * 4 * kDim * 4) + ep_align256(size_t(world) * 8) + ep_align256(size_t(world) * 8);
+}
+__host__ __device__ inline EpInbox ep_inbox_at(void *base, int world, int cap) {
+    const size_t rows = size_t(world) * size_t(cap);
+    uint8_t *p = static_cast<uint8_t *>(base);
+    EpInbox in{};
+    in.x = reinterpret_cast<float *>(p);
+    p += ep_align256(rows * kDim * 4);
+    in.idx = reinterpret_cast<int32_t *>(p);
+    p += ep_align256(rows * 16);
+    in.w = reinterpret_cast<float *>(p);
+    p += ep_align256(rows * 16);
+    in.src = reinterpret_cast<int32_t *>(p);
+    p += ep_align256(rows * 4);
+    in.back = reinterpret_cast<float *>(p);
+    p += ep_align256(size_t(cap) * 4 * kDim * 4);
+    in.cnt = reinterpret_cast<unsigned long long *>(p);
+    p += ep_align256(size_t(world) * 8);
+    in.done = reinterpret_cast<unsigned long long *>(p);
+    return in;
+}
+
+struct EpPeers {
+    void *base[kMaxWorld];  // every rank's receive block as this GPU addresses it (own included)
+};
+
+void launch_ep_plan(const int32_t *idx, int tokens, int world, int per_rank, int32_t *tok_off, int32_t *cnt,
+                    cudaStream_t stream);
+void launch_ep_send(const float *x, const int32_t *idx, const float *wts, int tokens, int world, int rank, int cap,
+                    const int32_t *tok_off, const int32_t *cnt, const EpPeers &peers, uint32_t tag,
+                    unsigned *arrive, int sms, cudaStream_t stream);
+void launch_ep_wait(const unsigned long long *flags, int world, uint32_t tag, int cap, int32_t *counts,
+                    uint32_t *status, cudaStream_t stream);
+void launch_ep_back(const PrefillWork &w, const EpInbox &in, int world, int rank, int per_rank, int cap,
+                    const EpPeers &peers, uint32_t tag, unsigned *arrive, int sms, cudaStream_t stream);
+void launch_ep_combine(const int32_t *idx, int tokens, const float *back, float *out, cudaStream_t stream);
 
 } // namespace ttl

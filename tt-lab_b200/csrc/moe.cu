@@ -15,11 +15,13 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <vector>
 
@@ -51,7 +53,7 @@ struct LayerStore {
     float *down_b = nullptr;
 };
 
-constexpr size_t kMaxForwardGraphs = 16;       // captured forward graphs kept per handle
+constexpr size_t kMaxForwardGraphs = 64;       // captured forward graphs kept per handle
 constexpr size_t kForwardStagingTokens = 256;  // ttl_moe_forward's device rows (at least)
 
 struct GraphKey {
@@ -89,7 +91,17 @@ struct ttl_moe {
     uint32_t *d_status = nullptr;
     unsigned long long *d_counters = nullptr;
     uint64_t launches = 0;
-    ncclComm_t comm = nullptr;
+    ncclComm_t comm = nullptr;   // nonblocking: every wait on it is bounded by timeout_ms
+    // Expert-parallel fault state.  The ranks' kernels meet on tags derived
+    // from per-rank bases (d_seq, ep.seq), so after any failed call on a
+    // multi-rank handle the ranks may disagree about them: ep_fault is set,
+    // and compute calls are refused until every rank has run ttl_moe_resync.
+    // comm_dead: the communicator was aborted (a collective missed its deadline).
+    bool ep_fault = false;
+    bool comm_dead = false;
+    uint32_t timeout_ms = 60000;     // host-side bound on waits for the stream and for NCCL
+    cudaEvent_t wait_ev = nullptr;   // recorded for the bounded stream wait (world > 1)
+    uint32_t *d_sync = nullptr;      // [4] resync scratch (world > 1)
     struct ForwardGraph {
         cudaGraphExec_t exec;
         uint64_t kernels;   // kernels per replay
@@ -135,22 +147,21 @@ struct ttl_moe {
     void *xch_open[kMaxWorld] = {};              // the peers' buffers, opened from their IPC handles
     bool xch_ready = false;                      // every rank mapped every buffer
     // expert-parallel prefill (world > 1): the own tokens' routing, the
-    // dispatch plan, and the send / receive / return row buffers
+    // dispatch plan, and the receive blocks every rank maps (prefill_ep.cu)
     struct {
         int32_t *own_idx = nullptr;    // [T][4] top-4 of this rank's own tokens
         float *own_w = nullptr;        // [T][4]
         float *own_logits = nullptr;   // [T][E]
-        int32_t *tok_off = nullptr;    // [T][world] send index of each own token per destination (-1: none)
-        int32_t *pair_off = nullptr;   // [T][world] pairs to the destination before the token
-        int32_t *cnt = nullptr;        // [2 world] tokens, then pairs, sent to each rank
-        int32_t *cnt_all = nullptr;    // [world][2 world] every rank's cnt
-        float *sendx = nullptr;        // [min(world, 4) T] token rows, by destination
-        int32_t *send_idx = nullptr;   // [min(world, 4) T][4]
-        float *send_w = nullptr;
-        float *recvx = nullptr;        // [world T] the received token rows (the expert pipeline's input)
-        int32_t *ret_off = nullptr;    // [world T]
-        float *ret = nullptr;          // [4 world T] rows w * down returned to the senders
-        float *back = nullptr;         // [4 T] rows returned to this rank
+        int32_t *tok_off = nullptr;    // [T][world] row of each own token in each destination's region (-1: none)
+        int32_t *cnt = nullptr;        // [world] rows sent to each rank
+        int32_t *rcnt = nullptr;       // [world] rows received from each rank (this call)
+        unsigned *arrive = nullptr;    // [2] grid arrival counters of the send and back kernels
+        void *inbox = nullptr;         // this rank's receive block (IPC allocation), ep_inbox_bytes
+        int cap = 0;                   // rows per source region = max_tokens
+        EpPeers peers{};               // every rank's block as this GPU addresses it
+        void *open[kMaxWorld] = {};    // the peers' blocks, opened from their IPC handles
+        bool mapped = false;           // every rank mapped every block
+        uint32_t seq = 0;              // tag of the last call (agreed by every rank)
     } ep;
     StackLayer *d_layers = nullptr;   // [layers]
     TmaDesc *d_tma = nullptr;         // [layers][kTmaCount] tensor maps of the packed matrices
@@ -179,6 +190,9 @@ std::string &thread_error() {
 int fail(ttl_moe *handle, int code, const std::string &message) {
     if (handle) {
         handle->error = message;
+        if (handle->cfg.world > 1) {
+            handle->ep_fault = true;
+        }
     } else {
         thread_error() = message;
     }
@@ -256,10 +270,110 @@ int set_device(ttl_moe *h) {
     return TTL_OK;
 }
 
+using Clock = std::chrono::steady_clock;
+
+// Aborts the communicator; the handle then refuses every compute call and
+// must be destroyed.
+int abort_comm(ttl_moe *h, const std::string &why) {
+    if (h->comm) {
+        nccl(nullptr)->CommAbort(h->comm);
+        h->comm = nullptr;
+    }
+    h->comm_dead = true;
+    return fail(h, TTL_ERR_NCCL, why + "; the communicator was aborted (destroy the handle)");
+}
+
+// The communicator is nonblocking: a call that answers ncclInProgress has
+// completed once ncclCommGetAsyncError stops answering it.  Bounded by the
+// handle's deadline; an asynchronous error or the deadline aborts it.
+int comm_settle(ttl_moe *h, const char *what) {
+    const NcclApi *api = nccl(nullptr);
+    const auto deadline = Clock::now() + std::chrono::milliseconds(h->timeout_ms);
+    for (;;) {
+        ncclResult_t state = ncclSuccess;
+        const ncclResult_t r = api->CommGetAsyncError(h->comm, &state);
+        if (r != ncclSuccess) {
+            state = r;
+        }
+        if (state == ncclSuccess) {
+            return TTL_OK;
+        }
+        if (state != ncclInProgress) {
+            return abort_comm(h, std::string(what) + ": " + api->GetErrorString(state));
+        }
+        if (Clock::now() > deadline) {
+            return abort_comm(h, std::string(what) + ": not complete after " + std::to_string(h->timeout_ms) + " ms");
+        }
+        std::this_thread::yield();
+    }
+}
+
 int nccl_check(ttl_moe *h, ncclResult_t r, const char *what) {
+    if (r == ncclInProgress) {
+        return comm_settle(h, what);
+    }
     if (r != ncclSuccess) {
         const NcclApi *api = nccl(nullptr);
         return fail(h, TTL_ERR_NCCL, std::string(what) + ": " + (api ? api->GetErrorString(r) : "nccl unavailable"));
+    }
+    return TTL_OK;
+}
+
+// Waits for everything enqueued on the handle's stream.  A multi-rank handle
+// waits by polling an event, bounded by its deadline, and watches its
+// communicator meanwhile: an NCCL error or the deadline aborts it, after
+// which the stream gets one more deadline to drain.  The kernels' own waits
+// on peers are bounded on the device (2 s) and end in a status word.
+int stream_wait(ttl_moe *h) {
+    if (h->cfg.world == 1 || !h->wait_ev) {
+        TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+        return TTL_OK;
+    }
+    TTL_TRY_CUDA(h, cudaEventRecord(h->wait_ev, h->stream));
+    const NcclApi *api = nccl(nullptr);
+    auto deadline = Clock::now() + std::chrono::milliseconds(h->timeout_ms);
+    int rc = TTL_OK;
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(h->wait_ev);
+        if (q == cudaSuccess) {
+            return rc;
+        }
+        if (q != cudaErrorNotReady) {
+            return fail(h, TTL_ERR_CUDA, std::string("stream wait: ") + cudaGetErrorString(q));
+        }
+        if (h->comm) {
+            ncclResult_t state = ncclSuccess;
+            if (api->CommGetAsyncError(h->comm, &state) == ncclSuccess && state != ncclSuccess &&
+                state != ncclInProgress) {
+                rc = abort_comm(h, std::string("NCCL: ") + api->GetErrorString(state));
+                deadline = Clock::now() + std::chrono::milliseconds(h->timeout_ms);
+            }
+        }
+        if (Clock::now() > deadline) {
+            if (!h->comm) {
+                return rc ? rc : fail(h, TTL_ERR_NCCL, "the stream did not drain within the deadline");
+            }
+            rc = abort_comm(h, "stream not finished after " + std::to_string(h->timeout_ms) + " ms");
+            deadline = Clock::now() + std::chrono::milliseconds(h->timeout_ms);
+        }
+        std::this_thread::yield();
+    }
+}
+
+// Compute calls on a multi-rank handle are refused after a failure until the
+// ranks have agreed again (ttl_moe_resync), or for good once the
+// communicator was aborted.
+int ep_ready(ttl_moe *h) {
+    if (h->cfg.world == 1) {
+        return TTL_OK;
+    }
+    if (h->comm_dead) {
+        return fail(h, TTL_ERR_NCCL, "the communicator was aborted after a failure; destroy the handle");
+    }
+    if (h->ep_fault) {
+        return fail(h, TTL_ERR_STATE,
+                    "an earlier call failed on this expert-parallel handle; every rank must call ttl_moe_resync "
+                    "before the next compute call");
     }
     return TTL_OK;
 }
@@ -280,12 +394,14 @@ bool stack_path(const ttl_moe *h) {
     return h->cfg.world == 1 || h->xch_ready;
 }
 
-// Exchange buffers for expert parallelism inside the persistent kernel: this
-// rank's buffer, the IPC handles of all ranks gathered over NCCL, the peers'
-// buffers opened (peer access over NVLink), and a table of all of them on the
-// device.  The ranks then agree (NCCL min) that every one of them succeeded,
-// so all take the same decode path.  Returns TTL_OK either way; a rank that
-// could not map stays on the per-layer path together with the others.
+// Peer memory for expert parallelism: this rank's exchange buffer (the
+// persistent decode kernel's partial rows) and, with a prefill capacity, its
+// receive block (prefill_ep.cu); the IPC handles of all ranks gathered over
+// NCCL, the peers' allocations opened (peer access over NVLink), and tables
+// of them on the device.  The ranks then agree (NCCL min) that every one of
+// them succeeded, so all take the same paths.  Returns TTL_OK either way; if
+// any rank could not map, decode runs per layer with an NCCL all-reduce on
+// every rank and prefill is refused.
 int setup_exchange(ttl_moe *h) {
     const int W = int(h->cfg.world);
     const int R = int(h->cfg.rank);
@@ -293,52 +409,67 @@ int setup_exchange(ttl_moe *h) {
     int ok = 1;
     uint8_t *d_handles = nullptr;
     int *d_ok = nullptr;
+    constexpr size_t kHandle = sizeof(cudaIpcMemHandle_t);
     int rc = alloc_n(h, &h->d_xch, xch_words(W));
     rc = rc ? rc : alloc_n(h, &h->d_xch_peers, size_t(W));
-    rc = rc ? rc : alloc_n(h, &d_handles, size_t(W) * sizeof(cudaIpcMemHandle_t));
+    rc = rc ? rc : alloc_n(h, &d_handles, size_t(W) * 2 * kHandle);
     rc = rc ? rc : alloc_n(h, &d_ok, 1);
     if (rc) {
         return rc;
     }
-    cudaIpcMemHandle_t mine{};
+    cudaIpcMemHandle_t mine[2] = {};
     if (cudaMemset(h->d_xch, 0, xch_words(W) * sizeof(unsigned long long)) != cudaSuccess ||
-        cudaIpcGetMemHandle(&mine, h->d_xch) != cudaSuccess) {
+        cudaIpcGetMemHandle(&mine[0], h->d_xch) != cudaSuccess ||
+        (h->ep.inbox && cudaIpcGetMemHandle(&mine[1], h->ep.inbox) != cudaSuccess)) {
         ok = 0;
         cudaGetLastError();
     }
-    TTL_TRY_CUDA(h, cudaMemcpy(d_handles + size_t(R) * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice));
-    rc = nccl_check(h, api->AllGather(d_handles + size_t(R) * sizeof(mine), d_handles, sizeof(mine), ncclUint8,
+    TTL_TRY_CUDA(h, cudaMemcpy(d_handles + size_t(R) * 2 * kHandle, mine, 2 * kHandle, cudaMemcpyHostToDevice));
+    rc = nccl_check(h, api->AllGather(d_handles + size_t(R) * 2 * kHandle, d_handles, 2 * kHandle, ncclUint8,
                                       h->comm, h->stream),
                     "ncclAllGather");
+    rc = rc ? rc : stream_wait(h);
     if (rc) {
         return rc;
     }
-    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
-    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(W));
-    TTL_TRY_CUDA(h, cudaMemcpy(all.data(), d_handles, size_t(W) * sizeof(mine), cudaMemcpyDeviceToHost));
+    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(2 * W));
+    TTL_TRY_CUDA(h, cudaMemcpy(all.data(), d_handles, size_t(W) * 2 * kHandle, cudaMemcpyDeviceToHost));
     std::vector<unsigned long long *> ptrs(static_cast<size_t>(W), nullptr);
     for (int r = 0; r < W && ok; ++r) {
         if (r == R) {
             ptrs[size_t(r)] = h->d_xch;
+            h->ep.peers.base[r] = h->ep.inbox;
             continue;
         }
         void *p = nullptr;
-        if (cudaIpcOpenMemHandle(&p, all[size_t(r)], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        if (cudaIpcOpenMemHandle(&p, all[size_t(2 * r)], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
             ok = 0;
             cudaGetLastError();
             break;
         }
         h->xch_open[r] = p;
         ptrs[size_t(r)] = static_cast<unsigned long long *>(p);
+        if (h->ep.inbox) {
+            void *q = nullptr;
+            if (cudaIpcOpenMemHandle(&q, all[size_t(2 * r + 1)], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                ok = 0;
+                cudaGetLastError();
+                break;
+            }
+            h->ep.open[r] = q;
+            h->ep.peers.base[r] = q;
+        }
     }
     TTL_TRY_CUDA(h, cudaMemcpy(h->d_xch_peers, ptrs.data(), size_t(W) * sizeof(void *), cudaMemcpyHostToDevice));
     TTL_TRY_CUDA(h, cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice));
     rc = nccl_check(h, api->AllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, h->comm, h->stream), "ncclAllReduce");
+    rc = rc ? rc : stream_wait(h);
     if (rc) {
         return rc;
     }
     TTL_TRY_CUDA(h, cudaMemcpy(&ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost));
     h->xch_ready = ok != 0;
+    h->ep.mapped = ok != 0 && h->ep.inbox != nullptr;
     return TTL_OK;
 }
 
@@ -624,129 +755,52 @@ int check_status(ttl_moe *h) {
 }
 
 int sync_and_check(ttl_moe *h) {
-    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
-    return check_status(h);
+    const int rc = stream_wait(h);
+    return rc ? rc : check_status(h);
 }
 
-// Expert-parallel prefill of this rank's own tokens (prefill_ep.cu has the
-// steps): router, dispatch plan, counts all-gathered (one host sync: NCCL
-// takes the sizes from the host), token rows out by grouped NCCL send/recv,
-// the expert pipeline on the received tokens, rows w * down back, owner
-// combine.  A rank's block to itself is a device copy.
+// Expert-parallel prefill of this rank's own tokens over peer memory
+// (prefill_ep.cu has the steps): router, plan, rows written into the
+// experts' owners' receive blocks, the expert pipeline on the rows received
+// from every rank, rows w * down written back into the tokens' owners'
+// blocks, owner combine.  All on the stream: no host round trip, no NCCL;
+// every wait on a peer is bounded on the device.
 int enqueue_prefill_ep(ttl_moe *h, int layer, const float *x, size_t tokens, float *out) {
     const int W = int(h->cfg.world);
     const int R = int(h->cfg.rank);
     const int P = h->expert_count;
-    const NcclApi *api = nccl(nullptr);
+    if (!h->ep.mapped) {
+        return fail(h, TTL_ERR_UNSUPPORTED, "expert-parallel prefill needs every rank's receive block mapped");
+    }
     const LayerDev L = layer_view(h, layer);
     const TmaDesc *tma = h->host_layers[size_t(layer)].tma;
     if (!tma) {
         return fail(h, TTL_ERR_STATE, "layer " + std::to_string(layer) + " has no tensor maps");
     }
     auto &ep = h->ep;
+    const uint32_t tag = ++ep.seq;
+    const EpInbox in = ep_inbox_at(ep.inbox, W, ep.cap);
     PrefillWork own = h->pw;
     own.logits = ep.own_logits;
     own.top_idx = ep.own_idx;
     own.top_w = ep.own_w;
+    own.seg_count = nullptr;
     PrefillShape so{int(h->cfg.experts), h->expert_begin, h->expert_count, int(tokens), h->sms};
     launch_prefill_router(L, own, so, x, h->stream);
-    launch_ep_plan(ep.own_idx, int(tokens), W, P, ep.tok_off, ep.pair_off, ep.cnt, h->stream);
-    int rc = nccl_check(h, api->AllGather(ep.cnt, ep.cnt_all, size_t(2 * W), ncclInt32, h->comm, h->stream),
-                        "ncclAllGather");
-    if (rc) {
-        return rc;
-    }
-    std::vector<int32_t> cnt(size_t(2 * W * W));
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(cnt.data(), ep.cnt_all, cnt.size() * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                                    h->stream));
-    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
-    auto sent = [&](int from, int to) { return cnt[size_t(from) * 2 * W + to]; };          // tokens
-    auto pairs = [&](int from, int to) { return cnt[size_t(from) * 2 * W + W + to]; };    // pairs
-    EpOffsets send_off{}, recv_off{}, ret_off{}, back_off{};
-    int ns = 0, nr = 0, nret = 0, nback = 0;
-    for (int d = 0; d < W; ++d) {
-        send_off.v[d] = ns;
-        ns += sent(R, d);
-        recv_off.v[d] = nr;  // from rank d
-        nr += sent(d, R);
-        ret_off.v[d] = nret;  // to rank d
-        nret += pairs(d, R);
-        back_off.v[d] = nback;  // from rank d
-        nback += pairs(R, d);
-    }
-    // ns <= min(W, 4) * tokens and nr <= W * max_tokens by construction (each
-    // rank sends each own token at most once per destination), so the buffers
-    // hold them; no rank leaves here alone, which would strand the others in
-    // the send/recv below
-    launch_ep_pack(x, ep.own_idx, ep.own_w, int(tokens), W, ep.tok_off, send_off, ep.sendx, ep.send_idx, ep.send_w,
-                   h->stream);
-    // token rows and their top-4 to the experts' owners
-    auto rows = [&](float *base, int row) { return base + size_t(row) * kDim; };
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(rows(ep.recvx, recv_off.v[R]), rows(ep.sendx, send_off.v[R]),
-                                    size_t(sent(R, R)) * kDim * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->pw.top_idx + 4 * size_t(recv_off.v[R]), ep.send_idx + 4 * size_t(send_off.v[R]),
-                                    size_t(sent(R, R)) * 4 * sizeof(int32_t), cudaMemcpyDeviceToDevice, h->stream));
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->pw.top_w + 4 * size_t(recv_off.v[R]), ep.send_w + 4 * size_t(send_off.v[R]),
-                                    size_t(sent(R, R)) * 4 * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
-    api->GroupStart();
-    for (int d = 0; d < W && !rc; ++d) {
-        if (d == R) {
-            continue;
-        }
-        if (sent(R, d) > 0) {
-            rc = rc ? rc : nccl_check(h, api->Send(rows(ep.sendx, send_off.v[d]), size_t(sent(R, d)) * kDim,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
-            rc = rc ? rc : nccl_check(h, api->Send(ep.send_idx + 4 * size_t(send_off.v[d]), size_t(sent(R, d)) * 4,
-                                                   ncclInt32, d, h->comm, h->stream), "ncclSend");
-            rc = rc ? rc : nccl_check(h, api->Send(ep.send_w + 4 * size_t(send_off.v[d]), size_t(sent(R, d)) * 4,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
-        }
-        if (sent(d, R) > 0) {
-            rc = rc ? rc : nccl_check(h, api->Recv(rows(ep.recvx, recv_off.v[d]), size_t(sent(d, R)) * kDim,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
-            rc = rc ? rc : nccl_check(h, api->Recv(h->pw.top_idx + 4 * size_t(recv_off.v[d]), size_t(sent(d, R)) * 4,
-                                                   ncclInt32, d, h->comm, h->stream), "ncclRecv");
-            rc = rc ? rc : nccl_check(h, api->Recv(h->pw.top_w + 4 * size_t(recv_off.v[d]), size_t(sent(d, R)) * 4,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
-        }
-    }
-    const int grc = nccl_check(h, api->GroupEnd(), "ncclGroupEnd");
-    rc = rc ? rc : grc;
-    if (rc) {
-        return rc;
-    }
-    // the experts of this rank on the received tokens
-    if (nr > 0) {
-        PrefillShape sp{int(h->cfg.experts), h->expert_begin, h->expert_count, nr, h->sms};
-        launch_prefill_route(h->pw, sp, h->stream);
-        launch_prefill_gateup(L, tma, h->pw, sp, ep.recvx, h->stream);
-        launch_prefill_down(L, tma, h->pw, sp, h->stream);
-        launch_ep_return(h->pw, nr, R, P, ep.ret_off, ep.ret, h->stream);
-    }
-    // rows w * down back to the tokens' owners
-    TTL_TRY_CUDA(h, cudaMemcpyAsync(rows(ep.back, back_off.v[R]), rows(ep.ret, ret_off.v[R]),
-                                    size_t(pairs(R, R)) * kDim * sizeof(float), cudaMemcpyDeviceToDevice, h->stream));
-    api->GroupStart();
-    for (int d = 0; d < W && !rc; ++d) {
-        if (d == R) {
-            continue;
-        }
-        if (pairs(d, R) > 0) {
-            rc = rc ? rc : nccl_check(h, api->Send(rows(ep.ret, ret_off.v[d]), size_t(pairs(d, R)) * kDim,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclSend");
-        }
-        if (pairs(R, d) > 0) {
-            rc = rc ? rc : nccl_check(h, api->Recv(rows(ep.back, back_off.v[d]), size_t(pairs(R, d)) * kDim,
-                                                   ncclFloat32, d, h->comm, h->stream), "ncclRecv");
-        }
-    }
-    const int grc2 = nccl_check(h, api->GroupEnd(), "ncclGroupEnd");
-    rc = rc ? rc : grc2;
-    if (rc) {
-        return rc;
-    }
-    launch_ep_combine(ep.own_idx, int(tokens), W, P, ep.pair_off, back_off, ep.back, out, h->stream);
-    h->launches += (nr > 0) ? 10 : 4;  // router, plan, pack, combine (+ route, split, 2 MMA, 2 return)
+    launch_ep_plan(ep.own_idx, int(tokens), W, P, ep.tok_off, ep.cnt, h->stream);
+    TTL_TRY_CUDA(h, cudaMemsetAsync(ep.arrive, 0, 2 * sizeof(unsigned), h->stream));
+    launch_ep_send(x, ep.own_idx, ep.own_w, int(tokens), W, R, ep.cap, ep.tok_off, ep.cnt, ep.peers, tag, ep.arrive,
+                   h->sms, h->stream);
+    launch_ep_wait(in.cnt, W, tag, ep.cap, ep.rcnt, h->d_status, h->stream);
+    // this rank's experts on the rows received from every rank
+    PrefillShape sp{int(h->cfg.experts), h->expert_begin, h->expert_count, W * ep.cap, h->sms};
+    launch_prefill_route(h->pw, sp, h->stream);
+    launch_prefill_gateup(L, tma, h->pw, sp, in.x, h->stream);
+    launch_prefill_down(L, tma, h->pw, sp, h->stream);
+    launch_ep_back(h->pw, in, W, R, P, ep.cap, ep.peers, tag, ep.arrive + 1, h->sms, h->stream);
+    launch_ep_wait(in.done, W, tag, ep.cap, nullptr, h->d_status, h->stream);
+    launch_ep_combine(ep.own_idx, int(tokens), in.back, out, h->stream);
+    h->launches += 11;  // router, plan, send, wait, route, split, gate/up, down, back, wait, combine
     TTL_TRY_CUDA(h, cudaGetLastError());
     return TTL_OK;
 }
@@ -941,21 +995,18 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         const size_t Tp = size_t(c.world) * T;
         if (c.world > 1) {
             const size_t W = c.world;
-            const size_t Ts = std::min<size_t>(W, 4) * T;
             rc = rc ? rc : alloc_n(h, &h->ep.own_idx, 4 * T);
             rc = rc ? rc : alloc_n(h, &h->ep.own_w, 4 * T);
             rc = rc ? rc : alloc_n(h, &h->ep.own_logits, T * E);
             rc = rc ? rc : alloc_n(h, &h->ep.tok_off, T * W);
-            rc = rc ? rc : alloc_n(h, &h->ep.pair_off, T * W);
-            rc = rc ? rc : alloc_n(h, &h->ep.cnt, 2 * W);
-            rc = rc ? rc : alloc_n(h, &h->ep.cnt_all, 2 * W * W);
-            rc = rc ? rc : alloc_n(h, &h->ep.sendx, Ts * kDim);
-            rc = rc ? rc : alloc_n(h, &h->ep.send_idx, 4 * Ts);
-            rc = rc ? rc : alloc_n(h, &h->ep.send_w, 4 * Ts);
-            rc = rc ? rc : alloc_n(h, &h->ep.recvx, Tp * kDim);
-            rc = rc ? rc : alloc_n(h, &h->ep.ret_off, Tp);
-            rc = rc ? rc : alloc_n(h, &h->ep.ret, 4 * Tp * kDim);
-            rc = rc ? rc : alloc_n(h, &h->ep.back, 4 * T * kDim);
+            rc = rc ? rc : alloc_n(h, &h->ep.cnt, W);
+            rc = rc ? rc : alloc_n(h, &h->ep.rcnt, W);
+            rc = rc ? rc : alloc_n(h, &h->ep.arrive, 2);
+            h->ep.cap = int(T);
+            rc = rc ? rc : alloc(h, &h->ep.inbox, ep_inbox_bytes(int(W), int(T)));
+            if (!rc && cudaMemset(h->ep.inbox, 0, ep_inbox_bytes(int(W), int(T))) != cudaSuccess) {
+                rc = fail(h, TTL_ERR_CUDA, "cannot clear the receive block");
+            }
         }
         const size_t pairs = 4 * Tp;
         rc = rc ? rc : alloc_n(h, &h->pw.logits, Tp * E);
@@ -979,6 +1030,15 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         rc = rc ? rc : alloc_n(h, &h->pw.bdig_dn, units * kPrefillUnitBytes);
         rc = rc ? rc : alloc_n(h, &h->pw.bsfb_dn, units * kPrefillUnitScaleBytes);
         h->pw.status = h->d_status;
+        if (!rc && c.world > 1) {
+            // the expert pipeline runs on the received rows: [world][T] by
+            // source rank, the ids and weights sent with them
+            const EpInbox in = ep_inbox_at(h->ep.inbox, int(c.world), int(T));
+            h->pw.top_idx = in.idx;
+            h->pw.top_w = in.w;
+            h->pw.seg_count = h->ep.rcnt;
+            h->pw.seg_rows = int(T);
+        }
         if (rc) {
             return bail(rc);
         }
@@ -1009,14 +1069,21 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         if (!api) {
             return bail(fail(h, TTL_ERR_NCCL, std::string("NCCL unavailable: ") + why));
         }
+        if (alloc_n(h, &h->d_sync, 4) != TTL_OK ||
+            cudaEventCreateWithFlags(&h->wait_ev, cudaEventDisableTiming) != cudaSuccess) {
+            return bail(fail(h, TTL_ERR_CUDA, "cannot allocate the resync scratch"));
+        }
         ncclUniqueId id;
         std::memcpy(&id, c.nccl_id, sizeof(id));
-        const ncclResult_t r = api->CommInitRank(&h->comm, int(c.world), id, int(c.rank));
-        if (r != ncclSuccess) {
+        ncclConfig_t nc = NCCL_CONFIG_INITIALIZER;
+        nc.blocking = 0;  // every wait on the communicator is bounded on the host
+        const ncclResult_t r = api->CommInitRankConfig(&h->comm, int(c.world), id, int(c.rank), &nc);
+        if (r != ncclSuccess && r != ncclInProgress) {
             h->comm = nullptr;
-            return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRank: ") + api->GetErrorString(r)));
+            return bail(fail(h, TTL_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + api->GetErrorString(r)));
         }
-        const int xrc = setup_exchange(h);
+        int xrc = comm_settle(h, "ncclCommInitRankConfig");
+        xrc = xrc ? xrc : setup_exchange(h);
         if (xrc) {
             return bail(xrc);
         }
@@ -1031,7 +1098,7 @@ void ttl_moe_destroy(ttl_moe *h) {
     }
     cudaSetDevice(h->device);
     if (h->stream) {
-        cudaStreamSynchronize(h->stream);
+        stream_wait(h);  // bounded for a multi-rank handle
     }
     for (auto &g : h->graphs) {
         cudaGraphExecDestroy(g.second.exec);
@@ -1057,8 +1124,24 @@ void ttl_moe_destroy(ttl_moe *h) {
             cudaIpcCloseMemHandle(p);
         }
     }
+    for (void *p : h->ep.open) {
+        if (p) {
+            cudaIpcCloseMemHandle(p);
+        }
+    }
     if (h->comm) {
-        nccl(nullptr)->CommDestroy(h->comm);
+        // finalize (flushes this rank's NCCL work), bounded; abort past the deadline
+        const NcclApi *api = nccl(nullptr);
+        const ncclResult_t f = api->CommFinalize(h->comm);
+        if ((f == ncclSuccess || f == ncclInProgress) && comm_settle(h, "ncclCommFinalize") == TTL_OK) {
+            api->CommDestroy(h->comm);
+        } else if (h->comm) {
+            api->CommAbort(h->comm);
+        }
+        h->comm = nullptr;
+    }
+    if (h->wait_ev) {
+        cudaEventDestroy(h->wait_ev);
     }
     for (void *p : h->allocations) {
         cudaFree(p);
@@ -1194,6 +1277,9 @@ int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int3
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int frc = ep_ready(h)) {
+        return frc;
+    }
     if (!x || !out) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
     }
@@ -1221,6 +1307,9 @@ int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int3
 int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int frc = ep_ready(h)) {
+        return frc;
     }
     if (!x || !out) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
@@ -1258,7 +1347,10 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
     std::memcpy(h->pin->x, x, kDim * sizeof(float));
     TTL_TRY_CUDA(h, cudaGraphLaunch(found->second.first, h->stream));
     h->launches += found->second.second;
-    TTL_TRY_CUDA(h, cudaStreamSynchronize(h->stream));
+    rc = stream_wait(h);
+    if (rc) {
+        return rc;
+    }
     if (h->pin->out.status) {
         return check_status(h);  // reads, clears and reports the device status word
     }
@@ -1276,6 +1368,9 @@ int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, 
                           float *top4_w) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int frc = ep_ready(h)) {
+        return frc;
     }
     if (!x || !out) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
@@ -1311,6 +1406,9 @@ int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int frc = ep_ready(h)) {
+        return frc;
+    }
     if (!x || !out) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
     }
@@ -1345,6 +1443,9 @@ int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
 int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const float *x, float *y, size_t tokens) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int frc = ep_ready(h)) {
+        return frc;
     }
     if (!x || !y) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
@@ -1407,6 +1508,9 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
 int ttl_moe_forward(ttl_moe *h, int layer_begin, int layer_end, const float *x, float *y, size_t tokens) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int frc = ep_ready(h)) {
+        return frc;
     }
     if (!x || !y) {
         return fail(h, TTL_ERR_ARGUMENT, "null input or output");
@@ -1538,6 +1642,82 @@ int ttl_moe_sync(ttl_moe *h) {
     }
     int rc = set_device(h);
     return rc ? rc : sync_and_check(h);
+}
+
+int ttl_moe_set_timeout(ttl_moe *h, uint32_t ms) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (ms == 0) {
+        return fail(h, TTL_ERR_ARGUMENT, "timeout must be at least 1 ms");
+    }
+    h->timeout_ms = ms;
+    return TTL_OK;
+}
+
+// Collective over the ranks of a multi-rank handle, after a failed call on
+// any of them: (1) drain this rank's stream; (2) NCCL max of the ranks' tag
+// bases (the persistent kernel's, on the device, and the prefill call tag) --
+// a barrier, so every rank's kernels have ended when it returns; (3) this
+// rank's exchange buffer, receive-block flags, tagged partials and status
+// cleared and the agreed bases installed; (4) a second barrier, so no rank
+// launches (and writes into a peer's memory) before every rank has cleared
+// its own.  Stale words of a failed launch cannot then match a new tag.
+int ttl_moe_resync(ttl_moe *h) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    int rc = set_device(h);
+    if (rc) {
+        return rc;
+    }
+    if (h->cfg.world == 1) {
+        rc = stream_wait(h);
+        TTL_TRY_CUDA(h, cudaMemset(h->d_status, 0, sizeof(uint32_t)));
+        return rc;
+    }
+    if (h->comm_dead) {
+        return fail(h, TTL_ERR_NCCL, "the communicator was aborted after a failure; destroy the handle");
+    }
+    const NcclApi *api = nccl(nullptr);
+    rc = stream_wait(h);
+    if (rc) {
+        return rc;
+    }
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_sync, h->d_seq, sizeof(uint32_t), cudaMemcpyDeviceToDevice, h->stream));
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_sync + 1, &h->ep.seq, sizeof(uint32_t), cudaMemcpyHostToDevice, h->stream));
+    rc = nccl_check(h, api->AllReduce(h->d_sync, h->d_sync, 2, ncclUint32, ncclMax, h->comm, h->stream),
+                    "ncclAllReduce (resync)");
+    rc = rc ? rc : stream_wait(h);
+    if (rc) {
+        return rc;
+    }
+    uint32_t agreed[2] = {0, 0};
+    TTL_TRY_CUDA(h, cudaMemcpy(agreed, h->d_sync, sizeof(agreed), cudaMemcpyDeviceToHost));
+    h->ep.seq = agreed[1];
+    TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_seq, h->d_sync, sizeof(uint32_t), cudaMemcpyDeviceToDevice, h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_seq + 1, 0, sizeof(uint32_t), h->stream));
+    if (h->d_xch) {
+        TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_xch, 0, xch_words(int(h->cfg.world)) * sizeof(unsigned long long),
+                                        h->stream));
+    }
+    if (h->ep.inbox) {
+        const EpInbox in = ep_inbox_at(h->ep.inbox, int(h->cfg.world), h->ep.cap);
+        TTL_TRY_CUDA(h, cudaMemsetAsync(in.cnt, 0, h->cfg.world * sizeof(unsigned long long), h->stream));
+        TTL_TRY_CUDA(h, cudaMemsetAsync(in.done, 0, h->cfg.world * sizeof(unsigned long long), h->stream));
+    }
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_part_gu, 0, kPartGuWords * 8, h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_part_dn, 0, kPartDnWords * 8, h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_rpt, 0, kRptWords * 8, h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_status, 0, sizeof(uint32_t), h->stream));
+    rc = nccl_check(h, api->AllReduce(h->d_sync, h->d_sync + 2, 1, ncclUint32, ncclMax, h->comm, h->stream),
+                    "ncclAllReduce (resync barrier)");
+    rc = rc ? rc : stream_wait(h);
+    if (rc) {
+        return rc;
+    }
+    h->ep_fault = false;
+    return TTL_OK;
 }
 
 void *ttl_moe_stream(ttl_moe *h) {

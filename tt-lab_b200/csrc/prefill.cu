@@ -218,11 +218,17 @@ __global__ void prefill_router_kernel(LayerDev L, PrefillWork w, int experts, in
     }
 }
 
+__device__ __forceinline__ bool row_live(const PrefillWork &w, int t) {
+    return !w.seg_count || t % w.seg_rows < w.seg_count[t / w.seg_rows];
+}
+
 // One CTA per local expert le (src/model.cpp:380-394): every CTA counts the
 // routed pairs of all local experts (the same counts in every CTA), takes
 // le's first slot, first group and first unit from the counts of the experts
 // before it, writes le's groups, units and padding slots, and places le's
 // pairs in its slots in token order (a block-wide scan over the tokens).
+// Rows outside the live part of their segment (expert parallelism) are
+// skipped.
 // CTA 0 also writes the totals and marks pairs of experts that are not local.
 __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int experts, int expert_begin,
                                                              int expert_count, int tokens) {
@@ -237,6 +243,12 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
     }
     __syncthreads();
     for (int i = threadIdx.x; i < tokens * kTopK; i += blockDim.x) {
+        if (!row_live(w, i / kTopK)) {
+            if (le == 0) {
+                w.pair_slot[i] = -1;
+            }
+            continue;
+        }
         const int e = w.top_idx[i];
         const int l = e - expert_begin;
         if (e < 0 || e >= experts) {
@@ -293,7 +305,7 @@ __global__ void __launch_bounds__(1024) prefill_route_kernel(PrefillWork w, int 
     for (int t0 = 0; t0 < tokens; t0 += blockDim.x) {
         const int t = t0 + threadIdx.x;
         int rank = -1;
-        if (t < tokens) {
+        if (t < tokens && row_live(w, t)) {
             const int4 q = *reinterpret_cast<const int4 *>(w.top_idx + size_t(t) * 4);
             rank = q.x == e ? 0 : q.y == e ? 1 : q.z == e ? 2 : q.w == e ? 3 : -1;
         }

@@ -10,13 +10,13 @@
 // MMAs, M = 128 weight rows, K = 64, N = 96 per group: A is the expert's
 // packed E2M1 weights with their own E8M0 scales (the decode kernel's tensor
 // maps and scale blocks, untouched), B is the unit's activations in block
-// fixed point -- per slot and 32-value K-block, the 17-bit magnitude
-// m = |v| * 2^(16 - e) (e the exponent of the block's largest |v|, truncated)
-// written as six balanced radix-8 digits, m = sum_d c_d 8^d with c_d in
+// fixed point -- per slot and 32-value K-block, the magnitude
+// m = |v| * 2^(16 - e) rounded to the nearest integer (e the exponent of the
+// block's largest |v|, so m <= 2^17) written as six balanced radix-8 digits, m = sum_d c_d 8^d with c_d in
 // [-4, 4] (E2M1 values, the sign of v applied), digit row d scaled by
 // 2^(e - 16 + 3d) -- so 16 slots x 6 digits fill N = 96 and a unit of two
-// groups N = 192.  The digits are exact to 2^-16 of each K-block's largest
-// value; the epilogue adds a slot's 6 digit columns.
+// groups N = 192.  Each value is within 2^-17 of its K-block's largest |v|;
+// the epilogue adds a slot's 6 digit columns.
 //
 //   prefill_split_kernel   one CTA per (unit, group, quarter of K): the B rows
 //                          of its slots (x of each slot's token) and their
@@ -35,6 +35,8 @@
 // tile at about the same time (from L2 after the first).
 // Every wait is bounded; on timeout the kernels record kStatusWaitTimeout.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -70,7 +72,7 @@ __device__ __forceinline__ uint32_t digit_scales6(uint32_t codes4, int d) {
     return (v & ~nan) | nan;
 }
 
-// E2M1 codes of the six balanced radix-8 digits of m < 2^17, digit d in
+// E2M1 codes of the six balanced radix-8 digits of m <= 2^17, digit d in
 // nibble d (nibbles 6, 7 zero).  With m' = m + 4 * (1 + 8 + ... + 8^4) and o_d
 // the octal digits of m', the digits are c_d = o_d - 4 (in [-4, 3]) for
 // d < 5 and c_5 = o_5 (in [0, 4]), since m = sum_d c_d 8^d.  Magnitudes 0, 1,
@@ -106,8 +108,8 @@ __device__ __forceinline__ uint32_t digit_split6_store(float v, uint8_t *dst, in
         code = 127u;
     } else {
         const int e = int(mb >> 23) - 127;
-        // |v| * 2^(16-e) < 2^17, truncated
-        m = __float2uint_rz(__fmul_rn(fabsf(v), __uint_as_float(uint32_t(143 - e) << 23)));
+        // |v| * 2^(16-e) < 2^17 is exact in f32; rounded to nearest, m <= 2^17
+        m = __float2uint_rn(__fmul_rn(fabsf(v), __uint_as_float(uint32_t(143 - e) << 23)));
         code = uint32_t(e + 127);
     }
     const uint32_t neg = __float_as_uint(v) >> 31;
@@ -138,57 +140,61 @@ __device__ __forceinline__ int unit_scale_offset(int m, int kb) {
     return (kb >> 2) * 1024 + (m >> 7) * 512 + (m & 31) * 16 + ((m >> 5) & 3) * 4 + (kb & 3);
 }
 
-// One CTA per (unit, group j, quarter h of the K-blocks), warp w = slot w:
-// the group's B rows of the unit ([96 K-blocks][192 rows][16 B], row =
+// Item b = (unit, group j, quarter h of the K-blocks), warp w = slot w: the
+// group's B rows of the unit ([96 K-blocks][192 rows][16 B], row =
 // j * 96 + slot * 6 + digit; slots past the group's end are zero rows) for
 // K-blocks 24 h .. 24 h + 23, and their scale bytes (6 of the unit's 24
 // chunks).  A one-group unit's second group is left unwritten: its products
-// use N = 96 and never read those rows.
-constexpr int kSplitBlocks = kPadBlocks / 4;  // K-blocks per split CTA
+// use N = 96 and never read those rows.  The CTAs stride over the items of
+// the routed units (the count is on the device), so the grid does not grow
+// with the token capacity.
+constexpr int kSplitBlocks = kPadBlocks / 4;  // K-blocks per split item
 __global__ void __launch_bounds__(32 * kGroup) prefill_split_kernel(PrefillWork w, const float *__restrict__ x) {
     __shared__ __align__(4) uint8_t codes[kGroup][kSplitBlocks];
-    const int u = blockIdx.x >> 3;
-    const int j = (blockIdx.x >> 2) & 1;
-    const int kb_first = (blockIdx.x & 3) * kSplitBlocks;
-    if (u >= *w.unit_count) {
-        return;
-    }
-    const int2 ug = unit_groups(w, u);
-    if (j >= ug.y) {
-        return;
-    }
+    const int items = 8 * *w.unit_count;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int slot = warp;
-    const int2 gs = group_slots(w, ug.x + j);
-    const float *row = slot < gs.y ? x + size_t(w.pair_token[gs.x + slot]) * kDim : nullptr;
-    uint8_t *dst = w.bdig + size_t(u) * kPrefillUnitBytes + (j * kGroupRows + slot * kDigits) * 16;
-    static_assert(kSplitBlocks % 8 == 0, "K-blocks in batches of 8");
-    for (int k0 = 0; k0 < kSplitBlocks; k0 += 8) {
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int kb = kb_first + k0 + q;
-            v[q] = (row && kb < kBlocks) ? __ldcg(row + kb * 32 + lane) : 0.0f;
+#pragma unroll 1
+    for (int b = blockIdx.x; b < items; b += gridDim.x) {
+        const int u = b >> 3;
+        const int j = (b >> 2) & 1;
+        const int kb_first = (b & 3) * kSplitBlocks;
+        const int2 ug = unit_groups(w, u);
+        if (j >= ug.y) {
+            continue;  // uniform over the CTA
         }
+        const int2 gs = group_slots(w, ug.x + j);
+        const float *row = slot < gs.y ? x + size_t(w.pair_token[gs.x + slot]) * kDim : nullptr;
+        uint8_t *dst = w.bdig + size_t(u) * kPrefillUnitBytes + (j * kGroupRows + slot * kDigits) * 16;
+        static_assert(kSplitBlocks % 8 == 0, "K-blocks in batches of 8");
+        for (int k0 = 0; k0 < kSplitBlocks; k0 += 8) {
+            float v[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int kb = kb_first + k0 + q;
-            const uint32_t c = digit_split6_store(v[q], dst + size_t(kb) * kUnitKbBytes, lane);
-            if (lane == 0) {
-                codes[slot][k0 + q] = uint8_t(c);
+            for (int q = 0; q < 8; ++q) {
+                const int kb = kb_first + k0 + q;
+                v[q] = (row && kb < kBlocks) ? __ldcg(row + kb * 32 + lane) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int kb = kb_first + k0 + q;
+                const uint32_t c = digit_split6_store(v[q], dst + size_t(kb) * kUnitKbBytes, lane);
+                if (lane == 0) {
+                    codes[slot][k0 + q] = uint8_t(c);
+                }
             }
         }
-    }
-    __syncthreads();
-    // one word per (chunk, row): the row's scale bytes of the chunk's 4 K-blocks
-    uint8_t *sfb = w.bsfb + size_t(u) * kPrefillUnitScaleBytes;
-    for (int idx = threadIdx.x; idx < (kSplitBlocks / 4) * kGroupRows; idx += blockDim.x) {
-        const int chunk = idx / kGroupRows;
-        const int r = idx - chunk * kGroupRows;
-        const int s = r / kDigits;
-        *reinterpret_cast<uint32_t *>(sfb + unit_scale_offset(j * kGroupRows + r, kb_first + 4 * chunk)) =
-            digit_scales6(*reinterpret_cast<const uint32_t *>(&codes[s][4 * chunk]), r - s * kDigits);
+        __syncthreads();
+        // one word per (chunk, row): the row's scale bytes of the chunk's 4 K-blocks
+        uint8_t *sfb = w.bsfb + size_t(u) * kPrefillUnitScaleBytes;
+        for (int idx = threadIdx.x; idx < (kSplitBlocks / 4) * kGroupRows; idx += blockDim.x) {
+            const int chunk = idx / kGroupRows;
+            const int r = idx - chunk * kGroupRows;
+            const int s = r / kDigits;
+            *reinterpret_cast<uint32_t *>(sfb + unit_scale_offset(j * kGroupRows + r, kb_first + 4 * chunk)) =
+                digit_scales6(*reinterpret_cast<const uint32_t *>(&codes[s][4 * chunk]), r - s * kDigits);
+        }
+        __syncthreads();  // codes is rewritten by the next item
     }
 }
 
@@ -525,7 +531,7 @@ void configure_prefill_tc() {
 void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,
                            const float *x, cudaStream_t stream) {
     const int units = int(prefill_units(size_t(s.tokens), size_t(s.expert_count)));
-    prefill_split_kernel<<<8 * units, 32 * kGroup, 0, stream>>>(w, x);
+    prefill_split_kernel<<<std::min(8 * units, 8 * s.sms), 32 * kGroup, 0, stream>>>(w, x);
     prefill_mma_kernel<true><<<s.sms, kThreads, sizeof(PSmem<true>) + 1024, stream>>>(L, tma, w);
 }
 

@@ -27,7 +27,10 @@ const NcclApi *nccl(const char **why) {
             ok = ok && fn != nullptr;
         };
         get(api.GetUniqueId, "ncclGetUniqueId");
-        get(api.CommInitRank, "ncclCommInitRank");
+        get(api.CommInitRankConfig, "ncclCommInitRankConfig");
+        get(api.CommGetAsyncError, "ncclCommGetAsyncError");
+        get(api.CommFinalize, "ncclCommFinalize");
+        get(api.CommAbort, "ncclCommAbort");
         get(api.CommDestroy, "ncclCommDestroy");
         get(api.AllReduce, "ncclAllReduce");
         get(api.AllGather, "ncclAllGather");

@@ -78,6 +78,16 @@ def lib():
         "ttl_moe_upload_norm": (i32, [vp, i32, fp]),
         "ttl_moe_upload_layer_packed": (i32, [vp, i32, fp, fp, vp, fp, vp, fp, vp, fp]),
         "ttl_requant_gpu": (i32, [ctypes.c_char_p, ctypes.c_char_p, i32, i32, i32]),
+        "ttl_moe_resync": (i32, [vp]),
+        "ttl_attn_create": (i32, [vp, ctypes.POINTER(vp)]),
+        "ttl_attn_destroy": (None, [vp]),
+        "ttl_attn_last_error": (ctypes.c_char_p, [vp]),
+        "ttl_attn_upload_layer": (i32, [vp, i32, fp, vp, fp, vp, fp, vp, fp, vp, fp, fp]),
+        "ttl_attn_forward_async": (i32, [vp, i32, sz, vp, vp]),
+        "ttl_attn_forward": (i32, [vp, i32, sz, vp, vp, vp]),
+        "ttl_attn_sync": (i32, [vp]),
+        "ttl_attn_stream": (vp, [vp]),
+        "ttl_moe_set_timeout": (i32, [vp, u32]),
         "ttl_moe_decode": (i32, [vp, i32, fp, fp, vp, fp]),
         "ttl_moe_prefill": (i32, [vp, i32, fp, sz, fp, vp, fp]),
         "ttl_moe_forward": (i32, [vp, i32, i32, fp, fp, sz]),
@@ -250,6 +260,13 @@ class MoE:
     def sync(self):
         self._check(lib().ttl_moe_sync(self.h))
 
+    def resync(self):
+        """Collective: brings the ranks back into agreement after a failed call."""
+        self._check(lib().ttl_moe_resync(self.h))
+
+    def set_timeout(self, ms):
+        self._check(lib().ttl_moe_set_timeout(self.h, int(ms)))
+
     def stream(self) -> int:
         return lib().ttl_moe_stream(self.h) or 0
 
@@ -379,6 +396,67 @@ class Head:
 
     def stream(self) -> int:
         return lib().ttl_head_stream(self.h) or 0
+
+
+class AttnConfig(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_uint32), ("token_capacity", ctypes.c_uint32), ("device", ctypes.c_int32),
+                ("stream", ctypes.c_void_p)]
+
+
+class Attention:
+    """One ttl_attn handle: the attention block of GptOssModel::forward
+    (rms_norm, Q/K/V Q8_0 projections, RoPE, KV cache, attention with sinks,
+    output projection, residual) for `layers` layers."""
+
+    def __init__(self, layers=1, token_capacity=256, device=-1, stream=None):
+        cfg = AttnConfig(layers, token_capacity, device, stream)
+        h = ctypes.c_void_p()
+        check(lib().ttl_attn_create(ctypes.byref(cfg), ctypes.byref(h)))
+        self.h = h
+
+    def _check(self, rc):
+        if rc != TTL_OK:
+            msg = lib().ttl_attn_last_error(self.h)
+            raise RuntimeError(f"cuda attention ({rc}): {msg.decode() if msg else ''}")
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().ttl_attn_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def upload_layer(self, layer, t):
+        self._check(lib().ttl_attn_upload_layer(
+            self.h, layer, _ptr(t["attn_norm"]), _ptr(t["q_w"]), _ptr(t["q_b"]), _ptr(t["k_w"]), _ptr(t["k_b"]),
+            _ptr(t["v_w"]), _ptr(t["v_b"]), _ptr(t["o_w"]), _ptr(t["o_b"]), _ptr(t["sinks"])))
+
+    def forward(self, layer, position, x):
+        """Host x [2880] -> (residual [2880], attended [4096])."""
+        x = np.ascontiguousarray(x, np.float32)
+        res = np.empty(DIM, np.float32)
+        att = np.empty(4096, np.float32)
+        self._check(lib().ttl_attn_forward(self.h, layer, position, _ptr(x), _ptr(res), _ptr(att)))
+        return res, att
+
+    def forward_async(self, layer, position, x, residual):
+        self._check(lib().ttl_attn_forward_async(self.h, layer, position, _ptr(x), _ptr(residual)))
+
+    def sync(self):
+        self._check(lib().ttl_attn_sync(self.h))
+
+    def stream(self) -> int:
+        return lib().ttl_attn_stream(self.h) or 0
 
 
 class TtqWriter:

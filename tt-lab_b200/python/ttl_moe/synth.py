@@ -129,3 +129,30 @@ def q8_0_host(blocks, seed, stream_id) -> np.ndarray:
 def inputs_host(seed, tokens, batch=0, sigma=1.0) -> np.ndarray:
     """Activations [tokens, 2880] ~ N(0, sigma)."""
     return normal_host(tokens * DIM, seed, INPUT_STREAM_BASE + batch, sigma).reshape(tokens, DIM)
+
+
+ATTN_STREAM = 1 << 37
+_ATTN_KINDS = {"attn_norm": 0, "q_w": 1, "q_b": 2, "k_w": 3, "k_b": 4, "v_w": 5, "v_b": 6, "o_w": 7, "o_b": 8,
+               "sinks": 9}
+
+
+def attention_layer_host(seed, layer) -> dict:
+    """One layer's attention tensors in GGUF layout (numpy): attn_norm ~
+    N(1, 0.02); Q8_0 Q [4096 x 2880], K, V [512 x 2880], O [2880 x 4096]
+    (the generator's Q8_0 blocks; the Q and K block scales divided by 4 so
+    that scores q.k / 8 stay of order 1); biases ~ N(0, 0.02); sinks ~ N(0, 1)."""
+    st = lambda k: ATTN_STREAM + layer * 16 + _ATTN_KINDS[k]  # noqa: E731
+    t = {"attn_norm": normal_host(DIM, seed, st("attn_norm"), 0.02, 1.0)}
+    for name, rows, cols in (("q_w", 4096, DIM), ("k_w", 512, DIM), ("v_w", 512, DIM), ("o_w", DIM, 4096)):
+        w = q8_0_host(rows * cols // 32, seed, st(name))
+        if name in ("q_w", "k_w"):
+            blk = w.reshape(-1, 34)
+            bits = blk[:, 0].astype(np.uint16) | (blk[:, 1].astype(np.uint16) << 8)
+            bits = bits - np.uint16(0x0800)  # fp16 exponent - 2: the scale / 4
+            blk[:, 0] = (bits & 0xFF).astype(np.uint8)
+            blk[:, 1] = (bits >> 8).astype(np.uint8)
+        t[name] = w
+    for name, n in (("q_b", 4096), ("k_b", 512), ("v_b", 512), ("o_b", DIM)):
+        t[name] = normal_host(n, seed, st(name), 0.02)
+    t["sinks"] = normal_host(64, seed, st("sinks"), 1.0)
+    return t
