@@ -638,6 +638,10 @@ def main():
     ap.add_argument("--no-120b", action="store_true", help="skip the cfg3 (120b, 36-layer) decode line")
     ap.add_argument("--no-attention", action="store_true",
                     help="skip the attention block / GPU-resident decode token measurement")
+    ap.add_argument("--attention-only", action="store_true",
+                    help="run only the attention block / decode-token measurement (profiling)")
+    ap.add_argument("--attention-context", type=int, default=1024,
+                    help="positions already in the KV cache for the attention measurement")
     ap.add_argument("--prefill-only", action="store_true",
                     help="only the cfg2 prefill measurement (one JSON line with its figures)")
     args = ap.parse_args()
@@ -652,6 +656,13 @@ def main():
     from ttl_moe import parallel, synth
 
     torch.cuda.set_device(local)
+    if args.attention_only:
+        if rank == 0:
+            at = attention_decode(torch, ttl_moe, synth, peaks()[0], context=args.attention_context,
+                                  iters=max(1, args.steps))
+            print(json.dumps({"metric": "attention block ms/layer (gpt-oss-20b)", "value": at["ms_per_layer"],
+                              "unit": "ms", "n_gpus": 1, "higher_is_better": False, "attention": at}))
+        return 0
     if args.prefill_only:
         if rank == 0:
             pf = prefill_cfg2(torch, ttl_moe, synth, local, iters=max(1, args.steps),
@@ -795,7 +806,7 @@ def main():
     if world == 1 and not args.no_attention:
         moe.close()
         torch.cuda.empty_cache()
-        attention = attention_decode(torch, ttl_moe, synth, peaks()[0])
+        attention = attention_decode(torch, ttl_moe, synth, peaks()[0], context=args.attention_context)
     decode_120b = None
     if not args.no_120b:
         moe.close()
