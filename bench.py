@@ -451,7 +451,7 @@ def attention_decode(torch, ttl_moe, synth, hbm_peak, context=1024, layers=24, i
     dev = torch.cuda.current_device()
     attn_t = [synth.attention_layer_host(5, l) for l in range(layers)]
     with ttl_moe.MoE(experts=32, layers=layers, device=dev) as m, \
-            ttl_moe.Attention(layers=layers, token_capacity=context + iters + 8, device=dev, stream=m.stream()) as a, \
+            ttl_moe.Attention(layers=layers, token_capacity=context + 2 * iters + 8, device=dev, stream=m.stream()) as a, \
             ttl_moe.Head(vocab=VOCAB, device=dev) as h:
         for l in range(layers):
             a.upload_layer(l, attn_t[l])
@@ -743,15 +743,24 @@ def main():
 
     # the drop-in call of tt-lab's GptOssModel::moe: one (token, layer) per
     # blocking ttl_moe_decode on host buffers (H2D, one launch, D2H, sync)
+    # (the C function called directly on preallocated buffers, so the figure
+    # is the library call's and not Python's array handling)
     calls = 200
     xh = np.ascontiguousarray(x_host[0])
-    moe.moe(0, xh)
+    oh = np.empty(DIM, np.float32)
+    ih = np.empty(4, np.int32)
+    wh = np.empty(4, np.float32)
+    decode_fn = ttl_moe.lib().ttl_moe_decode
+    hptr, xa, oa, ia, wa = moe.h, xh.ctypes.data, oh.ctypes.data, ih.ctypes.data, wh.ctypes.data
+    ttl_moe.check(decode_fn(hptr, 0, xa, oa, ia, wa), hptr)
     if dist:
         dist.barrier()
+    bad = 0
     t0 = time.perf_counter()
     for i in range(calls):
-        moe.moe(i % layers, xh)
+        bad |= decode_fn(hptr, i % layers, xa, oa, ia, wa)
     call_us = (time.perf_counter() - t0) / calls * 1e6
+    ttl_moe.check(bad, hptr)
     if dist:
         call_us = parallel.max_over_ranks(dist, [call_us], device="cuda")[0]
 

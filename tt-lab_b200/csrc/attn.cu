@@ -54,6 +54,15 @@ constexpr int kWindow = 128;
 constexpr int kMaxSplits = 32;
 constexpr int kQkvThreads = 512;
 constexpr int kOutThreads = 256;
+constexpr int kQkvRowBytes = 90 * 34;                     // 3060: a row of 2880 Q8_0 columns
+constexpr int kOutRowBytes = 128 * 34;                    // 4352: a row of 4096
+// staging pitches: 8 banks apart, so the four rows a warp reads at once hit
+// different banks
+constexpr int kQkvRowPitch = 3104;
+constexpr int kOutRowPitch = 4384;
+constexpr int kRowsPerWarp = 4;                           // 8 lanes per row
+constexpr int kQkvSmem = (kQkvThreads / 32) * kRowsPerWarp * kQkvRowPitch + kDim * 4;
+constexpr int kOutSmem = (kOutThreads / 32) * kRowsPerWarp * kOutRowPitch + 4096 * 4;
 constexpr int kTile = 32;  // positions per staged K / V tile
 
 struct AttnLayer {
@@ -76,29 +85,44 @@ __device__ __forceinline__ float h2f(uint16_t h) {
     return __half2float(__ushort_as_half(h));
 }
 
-// y = the dot product of one Q8_0 row with x (cols = 32 * blocks), as the
-// reference's AVX-512 clone orders it: lane c accumulates element (c & 15)
-// + 16 (c >> 4) of every block, product of the dequantized weight and x
-// rounded before the add; then acc0[i] + acc1[i] and a sequential sum over
-// i.  Returns the value on every lane.
-__device__ __forceinline__ float q8_row_dot(const uint8_t *__restrict__ row, const float *__restrict__ xs, int blocks,
-                                            int lane) {
-    float acc = 0.0f;
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src)
+                 : "memory");
+}
+
+// Starts the copy of `bytes` (a multiple of 4) of a Q8_0 row into the warp's
+// shared-memory slot: every word of the row in flight at once (one 4-byte
+// asynchronous copy per word, lanes on consecutive words).
+__device__ __forceinline__ void stage_row(uint8_t *slot, const uint8_t *__restrict__ row, int bytes, int lane) {
+    for (int w = lane; w < bytes / 4; w += 32) {
+        cp_async4(slot + 4 * w, row + 4 * w);
+    }
+}
+
+// The dot product of one staged Q8_0 row with x (cols = 32 * blocks) by the
+// 8 lanes of a row group: lane j takes elements 4j .. 4j + 3 of every block
+// (two 16-bit loads of its quants, the block's scale, four x values in one
+// 16-byte load).  Returns the row's value on all 8 lanes.
+__device__ __forceinline__ float q8_dot8(const uint8_t *row, const float *xs, int blocks, int j) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
 #pragma unroll 4
     for (int b = 0; b < blocks; ++b) {
-        const uint8_t *blk = row + size_t(b) * 34;
-        const uint16_t sbits = uint16_t(__ldg(blk)) | uint16_t(uint16_t(__ldg(blk + 1)) << 8);
-        const int8_t q = int8_t(__ldg(blk + 2 + lane));
-        const float w = __fmul_rn(float(q), h2f(sbits));
-        acc = __fadd_rn(acc, __fmul_rn(w, xs[b * 32 + lane]));
+        const uint8_t *blk = row + b * 34;
+        const float sc = h2f(*reinterpret_cast<const uint16_t *>(blk));
+        const uint32_t q4 = uint32_t(*reinterpret_cast<const uint16_t *>(blk + 2 + 4 * j)) |
+                            (uint32_t(*reinterpret_cast<const uint16_t *>(blk + 4 + 4 * j)) << 16);
+        const float4 xv = *reinterpret_cast<const float4 *>(xs + b * 32 + 4 * j);
+        a0 = fmaf(float(int8_t(q4)) * sc, xv.x, a0);
+        a1 = fmaf(float(int8_t(q4 >> 8)) * sc, xv.y, a1);
+        a2 = fmaf(float(int8_t(q4 >> 16)) * sc, xv.z, a2);
+        a3 = fmaf(float(int8_t(q4 >> 24)) * sc, xv.w, a3);
     }
-    const float pair = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 16));  // acc0[i] + acc1[i]
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, pair, i));
-    }
-    return sum;
+    float v = (a0 + a1) + (a2 + a3);
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    return v;
 }
 
 struct QkvArgs {
@@ -113,15 +137,51 @@ struct QkvArgs {
     float *kc, *vc;      // this layer's caches
 };
 
-// Work items: 2048 Q pairs, 256 K pairs (rows r, r + 32 of a head), 256 V
-// row pairs.
-constexpr int kQPairs = kQWidth / 2;
-constexpr int kKPairs = kKvWidth / 2;
-constexpr int kQkvItems = kQPairs + 2 * kKPairs;
+// Work items, four rows each (one per 8-lane row group): 1024 Q items and
+// 128 K items -- rows (r, r + 32, r + 1, r + 33) of a head, two RoPE pairs --
+// and 128 V items of four consecutive rows.
+constexpr int kQItems = kQWidth / 4;
+constexpr int kKItems = kKvWidth / 4;
+constexpr int kQkvItems = kQItems + kKItems + kKvWidth / 4;
+
+// Rows of QKV item `item` (see above); returns the matrix they are rows of.
+__device__ __forceinline__ const uint8_t *qkv_item_rows(const QkvArgs &a, int item, int rows4[4]) {
+    if (item < kQItems + kKItems) {
+        const bool is_q = item < kQItems;
+        const int local = is_q ? item : item - kQItems;
+        const int r0 = (local / 16) * kHead + (local % 16) * 2;
+        rows4[0] = r0;
+        rows4[1] = r0 + kHead / 2;
+        rows4[2] = r0 + 1;
+        rows4[3] = r0 + 1 + kHead / 2;
+        return is_q ? a.q : a.k;
+    }
+    const int r0 = 4 * (item - kQItems - kKItems);
+    for (int k = 0; k < 4; ++k) {
+        rows4[k] = r0 + k;
+    }
+    return a.v;
+}
 
 __global__ void __launch_bounds__(kQkvThreads) attn_qkv_kernel(QkvArgs a) {
-    __shared__ float xs[kDim];
+    extern __shared__ __align__(16) uint8_t dyn[];
+    uint8_t *rows = dyn;                                                    // [warps][4][3104]
+    float *xs = reinterpret_cast<float *>(dyn + (kQkvThreads / 32) * kRowsPerWarp * kQkvRowPitch);
     __shared__ float red[kQkvThreads / 32];
+    const int lane = threadIdx.x & 31;
+    uint8_t *slots = rows + size_t(threadIdx.x >> 5) * kRowsPerWarp * kQkvRowPitch;
+    // items spread over the CTAs first (warp w of every CTA, then w + 1); the
+    // first item's rows are requested before the norm, so the weight stream
+    // overlaps it
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    const int first = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
+    if (first < kQkvItems) {
+        int r4[4];
+        const uint8_t *base = qkv_item_rows(a, first, r4);
+        for (int k = 0; k < 4; ++k) {
+            stage_row(slots + k * kQkvRowPitch, base + size_t(r4[k]) * kQkvRowBytes, kQkvRowBytes, lane);
+        }
+    }
     // rms_norm (src/tensor.cpp:568-580) of x: a tree over the block, the
     // same in every CTA
     float ss = 0.0f;
@@ -146,43 +206,48 @@ __global__ void __launch_bounds__(kQkvThreads) attn_qkv_kernel(QkvArgs a) {
         xs[i] = a.x[i] * scale * a.norm[i];
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    for (int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); item < kQkvItems; item += warps) {
-        if (item < kQPairs + kKPairs) {
-            // a Q or K pair of one head: rows r and r + 32, rotated together
-            const bool is_q = item < kQPairs;
-            const int local = is_q ? item : item - kQPairs;
-            const int head = local / 32, pair = local % 32;
-            const int r0 = head * kHead + pair, r1 = r0 + kHead / 2;
-            const uint8_t *w = is_q ? a.q : a.k;
-            const float *bias = is_q ? a.qb : a.kb;
-            const float d0 = q8_row_dot(w + size_t(r0) * 90 * 34, xs, 90, lane);
-            const float d1 = q8_row_dot(w + size_t(r1) * 90 * 34, xs, 90, lane);
-            if (lane == 0) {
-                const float x0 = __fadd_rn(bias[r0], d0);
-                const float x1 = __fadd_rn(bias[r1], d1);
+    const int g = lane >> 3;   // row group
+    const int j = lane & 7;
+    for (int item = first; item < kQkvItems; item += stride) {
+        int rows4[4];
+        const uint8_t *base = qkv_item_rows(a, item, rows4);
+        const bool rope = item < kQItems + kKItems;
+        const bool is_q = item < kQItems;
+        if (item != first) {
+            __syncwarp();  // the slots' previous rows are consumed
+            for (int k = 0; k < 4; ++k) {
+                stage_row(slots + k * kQkvRowPitch, base + size_t(rows4[k]) * kQkvRowBytes, kQkvRowBytes, lane);
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+        const int row = rows4[g];
+        const float d = q8_dot8(slots + g * kQkvRowPitch, xs, 90, j);
+        if (rope) {
+            // groups (0, 1) and (2, 3) hold rows (r, r + 32): lane 0 of
+            // groups 0 and 2 rotates its pair
+            const float other = __shfl_xor_sync(0xffffffffu, d, 8);
+            if (j == 0 && (g & 1) == 0) {
+                const float *bias = is_q ? a.qb : a.kb;
+                const int r1 = rows4[g + 1];
+                const int pair = row % kHead;
+                const float x0 = __fadd_rn(bias[row], d);
+                const float x1 = __fadd_rn(bias[r1], other);
                 const float theta = __fmul_rn(float(a.position), a.freq[pair]);
                 const float c = __fmul_rn(cosf(theta), a.magnitude);
-                const float s = __fmul_rn(sinf(theta), a.magnitude);
-                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-                const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+                const float sn = __fmul_rn(sinf(theta), a.magnitude);
+                const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+                const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
                 if (is_q) {
-                    a.qout[r0] = y0;
+                    a.qout[row] = y0;
                     a.qout[r1] = y1;
                 } else {
-                    a.kc[size_t(a.position) * kKvWidth + r0] = y0;
+                    a.kc[size_t(a.position) * kKvWidth + row] = y0;
                     a.kc[size_t(a.position) * kKvWidth + r1] = y1;
                 }
             }
-        } else {
-            const int r0 = 2 * (item - kQPairs - kKPairs);
-            const float d0 = q8_row_dot(a.v + size_t(r0) * 90 * 34, xs, 90, lane);
-            const float d1 = q8_row_dot(a.v + size_t(r0 + 1) * 90 * 34, xs, 90, lane);
-            if (lane == 0) {
-                a.vc[size_t(a.position) * kKvWidth + r0] = __fadd_rn(a.vb[r0], d0);
-                a.vc[size_t(a.position) * kKvWidth + r0 + 1] = __fadd_rn(a.vb[r0 + 1], d1);
-            }
+        } else if (j == 0) {
+            a.vc[size_t(a.position) * kKvWidth + row] = __fadd_rn(a.vb[row], d);
         }
     }
 }
@@ -275,24 +340,33 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(DecodeArgs a) {
         return;
     }
     __threadfence();
-    // merge the splits of this warp's head with its sink (src/model.cpp:270-288)
+    // merge the splits of this warp's head with its sink (src/model.cpp:270-288):
+    // lane s holds split s's max and sum (all loads in flight together)
     const float sink = a.sinks[head];
     const float *ph = a.part + size_t(head) * kMaxSplits * 66;
-    float mx = sink;
-    for (int sp = 0; sp < int(gridDim.y); ++sp) {
-        mx = fmaxf(mx, __ldcg(ph + sp * 66));
+    const int ns = int(gridDim.y);
+    const float ms = (lane < ns) ? __ldcg(ph + lane * 66) : -INFINITY;
+    const float ls = (lane < ns) ? __ldcg(ph + lane * 66 + 1) : 0.0f;
+    float mx = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    float den = expf(sink - mx);
+    mx = fmaxf(mx, sink);
+    const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+    float den = ls * f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        den += __shfl_xor_sync(0xffffffffu, den, o);
+    }
+    den += expf(sink - mx);
     float o0 = 0.0f, o1 = 0.0f;
-    for (int sp = 0; sp < int(gridDim.y); ++sp) {
-        const float ms = __ldcg(ph + sp * 66);
-        if (ms == -INFINITY) {
-            continue;
-        }
-        const float f = expf(ms - mx);
-        den = fmaf(__ldcg(ph + sp * 66 + 1), f, den);
-        o0 = fmaf(__ldcg(ph + sp * 66 + 2 + 2 * lane), f, o0);
-        o1 = fmaf(__ldcg(ph + sp * 66 + 3 + 2 * lane), f, o1);
+#pragma unroll 8
+    for (int sp = 0; sp < ns; ++sp) {
+        const float fs = __shfl_sync(0xffffffffu, f, sp);
+        const float2 v = __ldcg(reinterpret_cast<const float2 *>(ph + sp * 66 + 2) + lane);
+        o0 = fmaf(v.x, fs, o0);
+        o1 = fmaf(v.y, fs, o1);
     }
     a.out[head * kHead + 2 * lane] = o0 / den;
     a.out[head * kHead + 2 * lane + 1] = o1 / den;
@@ -306,16 +380,37 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(DecodeArgs a) {
 __global__ void __launch_bounds__(kOutThreads) attn_out_kernel(const uint8_t *__restrict__ o, const float *__restrict__ ob,
                                                               const float *__restrict__ att, const float *__restrict__ x,
                                                               float *__restrict__ residual) {
-    __shared__ float as[kQWidth];
+    extern __shared__ __align__(16) uint8_t dyn[];
+    float *as = reinterpret_cast<float *>(dyn);                              // [4096]
+    uint8_t *slots = dyn + kQWidth * 4 + size_t(threadIdx.x >> 5) * kRowsPerWarp * kOutRowPitch;
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 3, j = lane & 7;
+    constexpr int kItems = kDim / kRowsPerWarp;  // 720
+    const int stride = gridDim.x * (blockDim.x >> 5);
+    int item = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
+    if (item < kItems) {  // the first rows' copies go out before the attention output is staged
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            stage_row(slots + k * kOutRowPitch, o + size_t(item * kRowsPerWarp + k) * kOutRowBytes, kOutRowBytes,
+                      lane);
+        }
+    }
     for (int i = threadIdx.x; i < kQWidth; i += blockDim.x) {
         as[i] = att[i];
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < kDim; r += warps) {
-        const float d = q8_row_dot(o + size_t(r) * 128 * 34, as, 128, lane);
-        if (lane == 0) {
+    for (; item < kItems; item += stride) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+        const int r = item * kRowsPerWarp + g;
+        const float d = q8_dot8(slots + g * kOutRowPitch, as, 128, j);
+        __syncwarp();
+        if (item + stride < kItems) {
+            for (int k = 0; k < kRowsPerWarp; ++k) {
+                stage_row(slots + k * kOutRowPitch, o + size_t((item + stride) * kRowsPerWarp + k) * kOutRowBytes,
+                          kOutRowBytes, lane);
+            }
+        }
+        if (j == 0) {
             residual[r] = __fadd_rn(x[r], __fadd_rn(ob[r], d));
         }
     }
@@ -459,6 +554,10 @@ int ttl_attn_create(const ttl_attn_config *c, ttl_attn **out) {
     if (rc) {
         return bail(attn_fail(nullptr, rc, h->error));
     }
+    if (cudaFuncSetAttribute(attn_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQkvSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOutSmem) != cudaSuccess) {
+        return bail(attn_fail(nullptr, TTL_ERR_CUDA, "cannot configure the attention kernels"));
+    }
     float freq[kHead / 2];
     rope_table(freq, &h->magnitude);
     if (cudaMemcpy(h->freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -555,7 +654,7 @@ int ttl_attn_forward_async(ttl_attn *h, int layer, size_t position, const float 
     const AttnLayer &s = h->L[size_t(layer)];
     QkvArgs qa{x, s.norm, s.q, s.k, s.v, s.qb, s.kb, s.vb, h->freq, h->magnitude, int(position), h->q, s.kc, s.vc};
     const int qkv_ctas = std::min(h->sms, (kQkvItems + kQkvThreads / 32 - 1) / (kQkvThreads / 32));
-    attn_qkv_kernel<<<qkv_ctas, kQkvThreads, 0, h->stream>>>(qa);
+    attn_qkv_kernel<<<qkv_ctas, kQkvThreads, kQkvSmem, h->stream>>>(qa);
     // window (src/model.cpp:261-262): even layers attend to the last 128 positions
     const size_t first = (layer % 2 == 0 && position + 1 > size_t(kWindow)) ? position + 1 - kWindow : 0;
     const int count = int(position + 1 - first);
@@ -563,7 +662,7 @@ int ttl_attn_forward_async(ttl_attn *h, int layer, size_t position, const float 
     const int per_split = (count + splits - 1) / splits;
     DecodeArgs da{h->q, s.kc, s.vc, s.sinks, int(first), count, per_split, h->part, h->arrive, h->att};
     attn_decode_kernel<<<dim3(kKvHeads, splits), 256, 0, h->stream>>>(da);
-    attn_out_kernel<<<h->sms, kOutThreads, 0, h->stream>>>(s.o, s.ob, h->att, x, residual);
+    attn_out_kernel<<<h->sms, kOutThreads, kOutSmem, h->stream>>>(s.o, s.ob, h->att, x, residual);
     TTL_ATTN_CUDA(h, cudaGetLastError());
     return TTL_OK;
 }

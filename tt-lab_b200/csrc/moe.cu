@@ -683,6 +683,11 @@ int capture_decode_graph(ttl_moe *h, int layer) {
     if (inst != cudaSuccess) {
         return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
     }
+    // uploaded now, so the first decode call of the layer does not pay for it
+    if (cudaGraphUpload(exec, h->stream) != cudaSuccess) {
+        cudaGraphExecDestroy(exec);
+        return fail(h, TTL_ERR_CUDA, "graph upload failed");
+    }
     h->decode_graphs.emplace(layer, std::make_pair(exec, uint64_t(1)));
     return TTL_OK;
 }
@@ -1494,6 +1499,10 @@ int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const floa
         cudaGraphDestroy(graph);
         if (inst != cudaSuccess) {
             return fail(h, TTL_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(inst));
+        }
+        if (cudaGraphUpload(exec, h->stream) != cudaSuccess) {
+            cudaGraphExecDestroy(exec);
+            return fail(h, TTL_ERR_CUDA, "graph upload failed");
         }
         const uint64_t per_replay = h->launches - launches;
         h->launches = launches;  // counted per replay below
