@@ -564,14 +564,37 @@ def decode_cfg3(torch, ttl_moe, synth, local, world, rank, dist, tokens=64, step
         m.sync()
         ms = e0.elapsed_time(e1) / steps
         persistent = m.counters()["persistent_decode"]
+        # the routing of one launch (the kernel's step log), for the bytes
+        # each GPU streams: its own selected experts per step, plus the
+        # replicated router and the row in / out
+        n = tokens * layers
+        y_log = torch.empty((n, DIM), dtype=torch.float32, device="cuda")
+        idx_log = torch.empty((n, 4), dtype=torch.int32, device="cuda")
+        w_log = torch.empty((n, 4), dtype=torch.float32, device="cuda")
+        m.record(n, y_log, idx_log, w_log)
+        m.forward_async(0, layers, x, y, tokens)
+        m.sync()
+        m.record(0)
+        own = idx_log.cpu().numpy() // (E // world)
+        del y_log
     if dist:
         ms = parallel.max_over_ranks(dist, [ms], device="cuda")[0]
     tps = tokens / (ms * 1e-3)
+    per_rank = np.array([(own == r).sum() for r in range(world)], np.float64) * 3 * (GGUF_MATRIX + BIAS)
+    per_rank += n * (E * DIM * 4 + E * 4 + 2 * DIM * 4)
+    hbm = peaks()[0]
+    busiest = float(per_rank.max())
     return {"workload": f"cfg3: gpt-oss-120b 36-layer MoE stack, decode T=1, {tokens} sequential tokens, "
                         f"experts sharded 128/{world} per GPU",
             "tokens_per_s": tps, "ms_per_step": ms, "n_gpus": world, "persistent_kernel": bool(persistent),
             "algorithmic_gbs": tps * layers * LAYER_BYTES_120B / 1e9,
             "bytes_per_token_layer": LAYER_BYTES_120B,
+            "per_gpu_bytes_per_launch": [int(v) for v in per_rank],
+            "roofline_busiest_gpu": {"bound": "hbm", "achieved": busiest / (ms * 1e-3) / 1e9, "peak": hbm,
+                                     "unit": "GB/s", "frac": busiest / (ms * 1e-3) / 1e9 / hbm,
+                                     "what": "bytes the most-loaded GPU streams per launch (its selected experts "
+                                             "from the kernel's step log, the replicated router, rows in/out) "
+                                             "over the launch time"},
             "timing": f"CUDA events on the library stream around {steps} launches of {tokens} tokens x {layers} "
                       "layers, max over ranks"}
 
@@ -580,9 +603,9 @@ def prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist, iters=10):
     """one gpt-oss-120b layer (128 experts), prefill
     of T = 2048 tokens with Zipf(1.2)-skewed routing, expert-parallel over the
     job's ranks: rank r passes tokens [r T / N, (r + 1) T / N), which go to
-    their experts' owners and come back as weighted rows (the library's NCCL
-    send/recv).  Time per call: CUDA events on the library's stream (the call
-    waits once inside for the ranks' send counts), max over ranks."""
+    their experts' owners and come back as weighted rows (peer stores into the
+    ranks' receive blocks).  Time per call: CUDA events on the library's
+    stream, max over ranks."""
     from ttl_moe import parallel
     E, T = 128, 2048
     lo, hi = rank * T // world, (rank + 1) * T // world
@@ -614,11 +637,40 @@ def prefill_cfg4(torch, ttl_moe, synth, local, world, rank, dist, iters=10):
         e1.synchronize()
         m.sync()
         ms = e0.elapsed_time(e1) / iters
+        # the routing of the call, for the bytes each GPU streams: the local
+        # experts any token selects (each read once), the token rows it
+        # receives and the weighted rows it returns
+        idx_d = torch.empty((hi - lo, 4), dtype=torch.int32, device="cuda")
+        m.prefill_async(0, x, hi - lo, out, idx_d)
+        m.sync()
+        owner = idx_d.long() // (E // world)
+        active = torch.zeros(E, dtype=torch.int32, device="cuda")
+        active[idx_d.long().flatten()] = 1
+        rows = torch.zeros(world, dtype=torch.int64, device="cuda")
+        pairs = torch.zeros(world, dtype=torch.int64, device="cuda")
+        for r in range(world):
+            hit = (owner == r)
+            rows[r] = hit.any(dim=1).sum()
+            pairs[r] = hit.sum()
+        if dist:
+            dist.all_reduce(active, op=dist.ReduceOp.MAX)
+            dist.all_reduce(rows)
+            dist.all_reduce(pairs)
+        act = active.view(world, E // world).sum(dim=1).cpu().numpy().astype(np.float64)
+        per_rank = act * 3 * (GGUF_MATRIX + BIAS) + (rows.cpu().numpy() + pairs.cpu().numpy()) * DIM * 4.0
     if dist:
         ms = parallel.max_over_ranks(dist, [ms], device="cuda")[0]
+    hbm = peaks()[0]
+    busiest = float(per_rank.max())
     return {"workload": "cfg4: gpt-oss-120b single MoE layer, prefill T=2048, router bias Zipf(1.2), "
                         f"expert-parallel over {world} GPU(s), tokens sharded T/N per rank",
             "ms_per_layer": ms, "tokens_per_s": T / (ms * 1e-3), "n_gpus": world,
+            "per_gpu_bytes": [int(v) for v in per_rank],
+            "roofline_busiest_gpu": {"bound": "hbm", "achieved": busiest / (ms * 1e-3) / 1e9, "peak": hbm,
+                                     "unit": "GB/s", "frac": busiest / (ms * 1e-3) / 1e9 / hbm,
+                                     "what": "bytes the most-loaded GPU streams per call (its active experts' "
+                                             "weights once, received token rows, returned rows) over the call "
+                                             "time"},
             "timing": "CUDA events on the library stream around 10 calls, max over ranks"}
 
 
@@ -761,6 +813,19 @@ def main():
         bad |= decode_fn(hptr, i % layers, xa, oa, ia, wa)
     call_us = (time.perf_counter() - t0) / calls * 1e6
     ttl_moe.check(bad, hptr)
+    # the same calls answered by a resident decode server (ttl_moe_serve),
+    # single-GPU handles only
+    serve_us = None
+    if world == 1:
+        moe.serve(100000)
+        for i in range(20):
+            bad |= decode_fn(hptr, i % layers, xa, oa, ia, wa)
+        t0 = time.perf_counter()
+        for i in range(calls):
+            bad |= decode_fn(hptr, i % layers, xa, oa, ia, wa)
+        serve_us = (time.perf_counter() - t0) / calls * 1e6
+        ttl_moe.check(bad, hptr)
+        moe.serve(0)
     if dist:
         call_us = parallel.max_over_ranks(dist, [call_us], device="cuda")[0]
 
@@ -871,8 +936,10 @@ def main():
                     "d2h_bytes_per_step": tokens * DIM * 4},
             "gpu_launches": launches,
             "decode_call": {"us_per_call": call_us, "calls": calls,
+                            "us_per_call_served": serve_us,
                             "what": "ttl_moe_decode (tt-lab's GptOssModel::moe drop-in): one token-layer per "
-                                    "blocking call on host buffers, wall clock, max over ranks"},
+                                    "blocking call on host buffers, wall clock, max over ranks; 'served': the "
+                                    "same calls answered by a resident decode kernel (ttl_moe_serve)"},
             "prefill": prefill,
             "prefill_ep": prefill_ep,
             "logits_head": head,

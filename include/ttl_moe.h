@@ -167,6 +167,19 @@ int ttl_moe_sync(ttl_moe *handle);
  * the handle refuses everything but ttl_moe_destroy.  World 1:
  * ttl_moe_resync waits for the stream and clears the status word. */
 int ttl_moe_resync(ttl_moe *handle);
+
+/* Decode server (single-GPU handles): with idle_us > 0, blocking
+ * ttl_moe_decode calls are answered by a resident launch of the decode kernel
+ * fed through a mailbox in mapped pinned memory -- no kernel launch, copy or
+ * stream synchronisation per call.  This is for callers that make one
+ * blocking MoE call per (token, layer) with the rest of the model elsewhere
+ * (tt-lab's GptOssModel::moe hook).  While the launch is resident it holds
+ * every SM, so no other kernel runs on the GPU: it leaves after idle_us
+ * microseconds without a request (at most 1 s) and is started again by the
+ * next call, and every other call on the handle stops it first.  Requires
+ * every layer uploaded.  idle_us = 0 turns it off.  Results equal those of
+ * the ordinary blocking call bit for bit.  Allocates its mailbox on first use. */
+int ttl_moe_serve(ttl_moe *handle, uint32_t idle_us);
 int ttl_moe_set_timeout(ttl_moe *handle, uint32_t milliseconds);
 
 /* The handle's cudaStream_t, as void *. */

@@ -40,6 +40,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "tc.cuh"
 #include "ttl_attn.h"
 
 namespace {
@@ -61,6 +62,7 @@ constexpr int kOutRowBytes = 128 * 34;                    // 4352: a row of 4096
 constexpr int kQkvRowPitch = 3104;
 constexpr int kOutRowPitch = 4384;
 constexpr int kRowsPerWarp = 4;                           // 8 lanes per row
+constexpr size_t kRowPad = 64;                            // bytes after each matrix (rounded row copies)
 constexpr int kQkvSmem = (kQkvThreads / 32) * kRowsPerWarp * kQkvRowPitch + kDim * 4;
 constexpr int kOutSmem = (kOutThreads / 32) * kRowsPerWarp * kOutRowPitch + 4096 * 4;
 constexpr int kTile = 32;  // positions per staged K / V tile
@@ -85,19 +87,61 @@ __device__ __forceinline__ float h2f(uint16_t h) {
     return __half2float(__ushort_as_half(h));
 }
 
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-                 "l"(src)
-                 : "memory");
+__device__ __forceinline__ uint32_t su32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Starts the copy of `bytes` (a multiple of 4) of a Q8_0 row into the warp's
-// shared-memory slot: every word of the row in flight at once (one 4-byte
-// asynchronous copy per word, lanes on consecutive words).
-__device__ __forceinline__ void stage_row(uint8_t *slot, const uint8_t *__restrict__ row, int bytes, int lane) {
-    for (int w = lane; w < bytes / 4; w += 32) {
-        cp_async4(slot + 4 * w, row + 4 * w);
+// Bulk copies of a warp's four rows into its shared-memory slots, completed
+// on the warp's mbarrier (lane 0 issues them; one instruction per row).  A
+// row that does not start on 16 bytes is copied from the 16-byte boundary
+// below it to the one above its end, so `lead` (0, 4, 8 or 12 bytes) is where
+// the row starts in its slot; the weight buffers carry 64 bytes of padding,
+// so the rounded end stays inside them.
+__device__ __forceinline__ void stage_rows(uint64_t *bar, uint8_t *slots, int pitch, const uint8_t *const rows[4],
+                                           int bytes, int lane) {
+    if (lane == 0) {
+        // the slots' earlier contents were read through the generic proxy
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        uint32_t total = 0;
+        uint32_t size[4];
+        const uint8_t *src[4];
+        for (int k = 0; k < 4; ++k) {
+            const uintptr_t a = reinterpret_cast<uintptr_t>(rows[k]);
+            const uintptr_t lo = a & ~uintptr_t(15), hi = (a + bytes + 15) & ~uintptr_t(15);
+            src[k] = reinterpret_cast<const uint8_t *>(lo);
+            size[k] = uint32_t(hi - lo);
+            total += size[k];
+        }
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(total) : "memory");
+        for (int k = 0; k < 4; ++k) {
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                             su32(slots + k * pitch)),
+                         "l"(src[k]), "r"(size[k]), "r"(su32(bar))
+                         : "memory");
+        }
     }
+}
+
+__device__ __forceinline__ int row_lead(const uint8_t *row) {
+    return int(reinterpret_cast<uintptr_t>(row) & 15);
+}
+
+// Waits (bounded, 2 s) for the warp's staged rows; on a timeout it records
+// kStatusWaitTimeout, waits once more for the copies in flight and returns
+// false.
+__device__ __forceinline__ bool wait_rows(uint64_t *bar, uint32_t &phase, uint32_t *status) {
+    const uint32_t p = phase;
+    phase ^= 1u;
+    // every lane observes the phase (so the copied bytes are visible to it);
+    // the warp decides together, so no lane leaves a later shuffle
+    const bool ok = __all_sync(0xffffffffu, ttl::tc::mbar_wait(bar, p));
+    if (!ok) {
+        if ((threadIdx.x & 31) == 0) {
+            ttl::set_status(status, ttl::kStatusWaitTimeout);
+        }
+        ttl::tc::mbar_wait(bar, p);  // the copies in flight, bounded again
+    }
+    return ok;
 }
 
 // The dot product of one staged Q8_0 row with x (cols = 32 * blocks) by the
@@ -135,6 +179,7 @@ struct QkvArgs {
     int position;
     float *qout;         // [4096] rotated
     float *kc, *vc;      // this layer's caches
+    uint32_t *status;
 };
 
 // Work items, four rows each (one per 8-lane row group): 1024 Q items and
@@ -168,8 +213,16 @@ __global__ void __launch_bounds__(kQkvThreads) attn_qkv_kernel(QkvArgs a) {
     uint8_t *rows = dyn;                                                    // [warps][4][3104]
     float *xs = reinterpret_cast<float *>(dyn + (kQkvThreads / 32) * kRowsPerWarp * kQkvRowPitch);
     __shared__ float red[kQkvThreads / 32];
+    __shared__ __align__(8) uint64_t wbar[kQkvThreads / 32];
     const int lane = threadIdx.x & 31;
     uint8_t *slots = rows + size_t(threadIdx.x >> 5) * kRowsPerWarp * kQkvRowPitch;
+    uint64_t *bar = &wbar[threadIdx.x >> 5];
+    if (lane == 0) {
+        ttl::tc::mbar_init(bar, 1);
+        ttl::tc::fence_mbar_init();
+    }
+    __syncwarp();
+    uint32_t phase = 0;
     // items spread over the CTAs first (warp w of every CTA, then w + 1); the
     // first item's rows are requested before the norm, so the weight stream
     // overlaps it
@@ -178,9 +231,11 @@ __global__ void __launch_bounds__(kQkvThreads) attn_qkv_kernel(QkvArgs a) {
     if (first < kQkvItems) {
         int r4[4];
         const uint8_t *base = qkv_item_rows(a, first, r4);
+        const uint8_t *src[4];
         for (int k = 0; k < 4; ++k) {
-            stage_row(slots + k * kQkvRowPitch, base + size_t(r4[k]) * kQkvRowBytes, kQkvRowBytes, lane);
+            src[k] = base + size_t(r4[k]) * kQkvRowBytes;
         }
+        stage_rows(bar, slots, kQkvRowPitch, src, kQkvRowBytes, lane);
     }
     // rms_norm (src/tensor.cpp:568-580) of x: a tree over the block, the
     // same in every CTA
@@ -213,16 +268,19 @@ __global__ void __launch_bounds__(kQkvThreads) attn_qkv_kernel(QkvArgs a) {
         const uint8_t *base = qkv_item_rows(a, item, rows4);
         const bool rope = item < kQItems + kKItems;
         const bool is_q = item < kQItems;
+        const uint8_t *src[4];
+        for (int k = 0; k < 4; ++k) {
+            src[k] = base + size_t(rows4[k]) * kQkvRowBytes;
+        }
         if (item != first) {
             __syncwarp();  // the slots' previous rows are consumed
-            for (int k = 0; k < 4; ++k) {
-                stage_row(slots + k * kQkvRowPitch, base + size_t(rows4[k]) * kQkvRowBytes, kQkvRowBytes, lane);
-            }
+            stage_rows(bar, slots, kQkvRowPitch, src, kQkvRowBytes, lane);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncwarp();
+        if (!wait_rows(bar, phase, a.status)) {
+            break;
+        }
         const int row = rows4[g];
-        const float d = q8_dot8(slots + g * kQkvRowPitch, xs, 90, j);
+        const float d = q8_dot8(slots + g * kQkvRowPitch + row_lead(src[g]), xs, 90, j);
         if (rope) {
             // groups (0, 1) and (2, 3) hold rows (r, r + 32): lane 0 of
             // groups 0 and 2 rotates its pair
@@ -376,39 +434,51 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(DecodeArgs a) {
 }
 
 // residual[r] = x[r] + (bias[r] + the row's dot product with the attention
-// output), one warp per row of the 2880 x 4096 output projection.
+// output), four rows per warp (8 lanes each) of the 2880 x 4096 output
+// projection; rows arrive by bulk copies, the next item's while the current
+// one is summed.
 __global__ void __launch_bounds__(kOutThreads) attn_out_kernel(const uint8_t *__restrict__ o, const float *__restrict__ ob,
                                                               const float *__restrict__ att, const float *__restrict__ x,
-                                                              float *__restrict__ residual) {
+                                                              float *__restrict__ residual, uint32_t *status) {
     extern __shared__ __align__(16) uint8_t dyn[];
+    __shared__ __align__(8) uint64_t wbar[kOutThreads / 32];
     float *as = reinterpret_cast<float *>(dyn);                              // [4096]
     uint8_t *slots = dyn + kQWidth * 4 + size_t(threadIdx.x >> 5) * kRowsPerWarp * kOutRowPitch;
     const int lane = threadIdx.x & 31;
     const int g = lane >> 3, j = lane & 7;
+    uint64_t *bar = &wbar[threadIdx.x >> 5];
+    if (lane == 0) {
+        ttl::tc::mbar_init(bar, 1);
+        ttl::tc::fence_mbar_init();
+    }
+    __syncwarp();
+    uint32_t phase = 0;
     constexpr int kItems = kDim / kRowsPerWarp;  // 720
     const int stride = gridDim.x * (blockDim.x >> 5);
+    auto issue = [&](int it) {
+        const uint8_t *src[4];
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            src[k] = o + size_t(it * kRowsPerWarp + k) * kOutRowBytes;
+        }
+        stage_rows(bar, slots, kOutRowPitch, src, kOutRowBytes, lane);
+    };
     int item = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;
     if (item < kItems) {  // the first rows' copies go out before the attention output is staged
-        for (int k = 0; k < kRowsPerWarp; ++k) {
-            stage_row(slots + k * kOutRowPitch, o + size_t(item * kRowsPerWarp + k) * kOutRowBytes, kOutRowBytes,
-                      lane);
-        }
+        issue(item);
     }
     for (int i = threadIdx.x; i < kQWidth; i += blockDim.x) {
         as[i] = att[i];
     }
     __syncthreads();
     for (; item < kItems; item += stride) {
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncwarp();
+        if (!wait_rows(bar, phase, status)) {
+            break;
+        }
         const int r = item * kRowsPerWarp + g;
-        const float d = q8_dot8(slots + g * kOutRowPitch, as, 128, j);
+        const float d = q8_dot8(slots + g * kOutRowPitch, as, 128, j);  // rows of 4352 B start on 16 B
         __syncwarp();
         if (item + stride < kItems) {
-            for (int k = 0; k < kRowsPerWarp; ++k) {
-                stage_row(slots + k * kOutRowPitch, o + size_t((item + stride) * kRowsPerWarp + k) * kOutRowBytes,
-                          kOutRowBytes, lane);
-            }
+            issue(item + stride);
         }
         if (j == 0) {
             residual[r] = __fadd_rn(x[r], __fadd_rn(ob[r], d));
@@ -435,6 +505,7 @@ struct ttl_attn {
     unsigned *arrive = nullptr;  // [8]
     float *d_x = nullptr;        // host-call staging [2880] x, [2880] residual
     float *d_res = nullptr;
+    uint32_t *status = nullptr;  // device status word (kStatusWaitTimeout)
     std::string error;
 };
 
@@ -483,6 +554,17 @@ void rope_table(float freq[kHead / 2], float *magnitude) {
         freq[pair] = scale * theta_extrap * (1.0f - ramp) + theta_extrap * ramp;
     }
     *magnitude = 1.0f + 0.1f * std::log(1.0f / scale);
+}
+
+// Reads and clears the device status word; a set bit is TTL_ERR_DEVICE.
+int check_status(ttl_attn *h) {
+    uint32_t st = 0;
+    TTL_ATTN_CUDA(h, cudaMemcpy(&st, h->status, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st) {
+        cudaMemset(h->status, 0, sizeof(uint32_t));
+        return attn_fail(h, TTL_ERR_DEVICE, "device status: bounded-wait-timeout");
+    }
+    return TTL_OK;
 }
 
 int check_layer(ttl_attn *h, int layer) {
@@ -551,17 +633,28 @@ int ttl_attn_create(const ttl_attn_config *c, ttl_attn **out) {
     rc = rc ? rc : attn_alloc(h, &h->arrive, kKvHeads);
     rc = rc ? rc : attn_alloc(h, &h->d_x, kDim);
     rc = rc ? rc : attn_alloc(h, &h->d_res, kDim);
+    rc = rc ? rc : attn_alloc(h, &h->status, 1);
     if (rc) {
         return bail(attn_fail(nullptr, rc, h->error));
     }
+    // all three kernels ask for the largest shared-memory carveout (as the
+    // MoE kernels on the same stream need), so consecutive launches never
+    // wait for the SMs to repartition L1 and shared memory
     if (cudaFuncSetAttribute(attn_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kQkvSmem) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOutSmem) != cudaSuccess) {
+        cudaFuncSetAttribute(attn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOutSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_qkv_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_out_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             int(cudaSharedmemCarveoutMaxShared)) != cudaSuccess) {
         return bail(attn_fail(nullptr, TTL_ERR_CUDA, "cannot configure the attention kernels"));
     }
     float freq[kHead / 2];
     rope_table(freq, &h->magnitude);
     if (cudaMemcpy(h->freq, freq, sizeof(freq), cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(h->arrive, 0, kKvHeads * sizeof(unsigned)) != cudaSuccess) {
+        cudaMemset(h->arrive, 0, kKvHeads * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(h->status, 0, sizeof(uint32_t)) != cudaSuccess) {
         return bail(attn_fail(nullptr, TTL_ERR_CUDA, "device initialisation failed"));
     }
     *out = h;
@@ -607,13 +700,13 @@ int ttl_attn_upload_layer(ttl_attn *h, int layer, const float *attn_norm, const 
     const size_t obytes = size_t(kDim) * 128 * 34;
     if (!s.norm) {
         int rc = attn_alloc(h, &s.norm, kDim);
-        rc = rc ? rc : attn_alloc(h, &s.q, qbytes);
+        rc = rc ? rc : attn_alloc(h, &s.q, qbytes + kRowPad);
         rc = rc ? rc : attn_alloc(h, &s.qb, kQWidth);
-        rc = rc ? rc : attn_alloc(h, &s.k, kbytes);
+        rc = rc ? rc : attn_alloc(h, &s.k, kbytes + kRowPad);
         rc = rc ? rc : attn_alloc(h, &s.kb, kKvWidth);
-        rc = rc ? rc : attn_alloc(h, &s.v, kbytes);
+        rc = rc ? rc : attn_alloc(h, &s.v, kbytes + kRowPad);
         rc = rc ? rc : attn_alloc(h, &s.vb, kKvWidth);
-        rc = rc ? rc : attn_alloc(h, &s.o, obytes);
+        rc = rc ? rc : attn_alloc(h, &s.o, obytes + kRowPad);
         rc = rc ? rc : attn_alloc(h, &s.ob, kDim);
         rc = rc ? rc : attn_alloc(h, &s.sinks, kHeads);
         rc = rc ? rc : attn_alloc(h, &s.kc, size_t(h->capacity) * kKvWidth);
@@ -652,7 +745,8 @@ int ttl_attn_forward_async(ttl_attn *h, int layer, size_t position, const float 
     }
     TTL_ATTN_CUDA(h, cudaSetDevice(h->device));
     const AttnLayer &s = h->L[size_t(layer)];
-    QkvArgs qa{x, s.norm, s.q, s.k, s.v, s.qb, s.kb, s.vb, h->freq, h->magnitude, int(position), h->q, s.kc, s.vc};
+    QkvArgs qa{x,  s.norm, s.q, s.k, s.v, s.qb, s.kb, s.vb, h->freq, h->magnitude, int(position), h->q, s.kc, s.vc,
+               h->status};
     const int qkv_ctas = std::min(h->sms, (kQkvItems + kQkvThreads / 32 - 1) / (kQkvThreads / 32));
     attn_qkv_kernel<<<qkv_ctas, kQkvThreads, kQkvSmem, h->stream>>>(qa);
     // window (src/model.cpp:261-262): even layers attend to the last 128 positions
@@ -662,7 +756,7 @@ int ttl_attn_forward_async(ttl_attn *h, int layer, size_t position, const float 
     const int per_split = (count + splits - 1) / splits;
     DecodeArgs da{h->q, s.kc, s.vc, s.sinks, int(first), count, per_split, h->part, h->arrive, h->att};
     attn_decode_kernel<<<dim3(kKvHeads, splits), 256, 0, h->stream>>>(da);
-    attn_out_kernel<<<h->sms, kOutThreads, kOutSmem, h->stream>>>(s.o, s.ob, h->att, x, residual);
+    attn_out_kernel<<<h->sms, kOutThreads, kOutSmem, h->stream>>>(s.o, s.ob, h->att, x, residual, h->status);
     TTL_ATTN_CUDA(h, cudaGetLastError());
     return TTL_OK;
 }
@@ -685,7 +779,7 @@ int ttl_attn_forward(ttl_attn *h, int layer, size_t position, const float *x, fl
         TTL_ATTN_CUDA(h, cudaMemcpyAsync(attended, h->att, kQWidth * sizeof(float), cudaMemcpyDefault, h->stream));
     }
     TTL_ATTN_CUDA(h, cudaStreamSynchronize(h->stream));
-    return TTL_OK;
+    return check_status(h);
 }
 
 int ttl_attn_sync(ttl_attn *h) {
@@ -694,7 +788,7 @@ int ttl_attn_sync(ttl_attn *h) {
     }
     TTL_ATTN_CUDA(h, cudaSetDevice(h->device));
     TTL_ATTN_CUDA(h, cudaStreamSynchronize(h->stream));
-    return TTL_OK;
+    return check_status(h);
 }
 
 void *ttl_attn_stream(ttl_attn *h) {

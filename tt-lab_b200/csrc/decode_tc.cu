@@ -183,6 +183,10 @@ struct alignas(1024) Smem {
     int abort;
     int last;
     float nscale;  // scalar the gate/up partials are multiplied by (the RMSNorm scale; 1 in mode 0)
+    int step_layer;  // mode 2: the layer of the step in hand (for the loads warp)
+    int srv_layer;   // mode 2: the request's layer, or -1 when the server leaves
+    int srv_exit;    // mode 2: the compute group left the step loop (the loads warp follows)
+    uint32_t steps_run;  // steps this launch ran (mode 2: requests served), written by thread 0 only
 };
 
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory per CTA");
@@ -777,6 +781,12 @@ struct TileOps {
     float rw[kPreE];       // down: next layer's router weights of this row
 };
 
+// Steps per token of a launch: its layers, or 1 in the server mode (each
+// request is one step on its own layer).
+__device__ __forceinline__ int steps_per_token(const StackArgs &a) {
+    return a.mode == 2 ? 1 : a.layer_end - a.layer_begin;
+}
+
 template <bool kWideRouter>
 __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int tile, int t_token, int li, bool next_router,
                                               TileOps &o) {
@@ -830,7 +840,8 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
         }
     }
     if (a.mode == 1) {
-        const float *xcur = (li == 0) ? a.x + size_t(t_token) * kDim : a.y + size_t(t_token) * kDim;
+        const int tr = t_token & a.row_mask;
+        const float *xcur = (li == 0) ? a.x + size_t(tr) * kDim : a.y + size_t(tr) * kDim;
         o.resid = __ldcg(xcur + row);
     }
     if (next_router) {
@@ -859,7 +870,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const int w = i >> 5;
     const int lane = i & 31;
     const int E = a.experts;
-    const int nl = a.layer_end - a.layer_begin;
+    const int nl = steps_per_token(a);
     const bool more_layers = (li + 1 < nl);
     const int tile = et.tile;
     const int step = t_token * nl + li;
@@ -928,7 +939,13 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         }
     }
     if (!next_router && row < kDim) {
-        a.y[size_t(t_token) * kDim + row] = yv;
+        a.y[size_t(t_token & a.row_mask) * kDim + row] = yv;
+    }
+    if (!next_router && a.mode == 2 && row < kDim) {
+        // the server's row goes straight to the mailbox in host memory, tagged
+        // with the request's number (the host polls the words themselves)
+        const unsigned long long w = tagged(a.mbox_base + uint32_t(step) + 1u, yv);
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.mbox->y + row), "l"(w) : "memory");
     }
     if (next_router) {
         // router sums of the next (token, layer) over these rows: per warp,
@@ -994,7 +1011,7 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         // (digit terms of x * g; the RMSNorm scale is a scalar applied to the
         // products), counted on their own
         if (row < kDim) {
-            a.y[size_t(t_token) * kDim + row] = yv;
+            a.y[size_t(t_token & a.row_mask) * kDim + row] = yv;
         }
         // the next step's gate/up B operand: digit terms of x * g (the RMSNorm
         // scale is a scalar applied to the products)
@@ -1028,7 +1045,7 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
             first_owned = pl.seg[g].tile;
         }
     }
-    const int step = t_token * (a.layer_end - a.layer_begin) + li;
+    const int step = t_token * steps_per_token(a) + li;
     const uint32_t tag = step_tag(s, step);
     TileOps ops;
     if (first_owned >= 0) {
@@ -1396,6 +1413,14 @@ __device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, b
         if (export_top) {
             a.top_idx[q] = e;
             a.top_w[q] = __fdiv_rn(wq, sum);
+            if (a.mode == 2) {  // the server's top-4, tagged with the request's number
+                const uint32_t r = a.mbox_base + uint32_t(step) + 1u;
+                const unsigned long long wi = (static_cast<unsigned long long>(r) << 32) | uint32_t(e);
+                asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.mbox->top + q), "l"(wi) : "memory");
+                asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(a.mbox->top + 4 + q),
+                             "l"(tagged(r, __fdiv_rn(wq, sum)))
+                             : "memory");
+            }
         }
         if (a.ilog && blockIdx.x == 0 && step < a.log_steps) {
             a.ilog[size_t(step) * kTopK + q] = e;
@@ -1413,11 +1438,121 @@ __device__ __forceinline__ void publish_selection(Smem &s, const StackArgs &a, b
 
 // Load warp: every step's stages, following the published selections; at the
 // end it waits until every load it issued has landed.
+// ---- the decode server (mode 2) ----
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The layer of step `step`'s request, on every compute thread of every CTA,
+// or -1 when the server leaves.  CTA 0 polls the mailbox in host memory
+// (bounded by the idle limit, or until the host asks it to stop), copies the
+// request's x into device memory and publishes (step tag, layer) in a.go;
+// the other CTAs poll that word (bounded by the idle limit + 2 s).
+__device__ int server_next(Smem &s, const StackArgs &a, int step) {
+    const int ct = threadIdx.x;
+    const uint32_t tag = step_tag(s, step);
+    if (blockIdx.x == 0) {
+        if (ct == 0) {
+            int layer = -1;
+            const uint32_t want = a.mbox_base + uint32_t(step) + 1u;
+            const unsigned long long t0 = tc::now_ns();
+            for (;;) {
+                unsigned long long w;
+                asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(&a.mbox->reqw) : "memory");
+                if (uint32_t(w >> 32) == want) {
+                    layer = int(uint32_t(w));
+                    if (layer < a.layer_begin || layer >= a.layer_end) {
+                        set_status(a.status, kStatusBadShape);  // the host checks the layer first
+                        layer = -1;
+                    }
+                    break;
+                }
+                if (ld_acquire_sys(&a.mbox->stop) != 0u || tc::now_ns() - t0 > a.idle_ns) {
+                    break;
+                }
+            }
+            if (layer < 0) {
+                st_release_sys(&a.mbox->alive, 0u);  // no request is taken after this
+            }
+            s.srv_layer = layer;
+        }
+        compute_sync();
+        if (s.srv_layer >= 0) {
+            // 720 float4 over PCIe: each thread's loads all in flight, then stored
+            constexpr int kVec = kDim / 4;
+            constexpr int kPer = (kVec + kComputeThreads - 1) / kComputeThreads;  // 3
+            const float4 *__restrict__ src = reinterpret_cast<const float4 *>(a.mbox->x);
+            float4 *__restrict__ dst = reinterpret_cast<float4 *>(a.srv_x);
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int k = ct + j * kComputeThreads;
+                if (k < kVec) {
+                    dst[k] = __ldcv(src + k);
+                }
+            }
+            __threadfence();
+        }
+        compute_sync();
+        if (ct == 0) {
+            const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | uint32_t(s.srv_layer);
+            asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(a.go), "l"(w) : "memory");
+        }
+    } else {
+        if (ct == 0) {
+            int layer = -1;
+            const unsigned long long t0 = tc::now_ns();
+            for (;;) {
+                unsigned long long w;
+                asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(a.go) : "memory");
+                if (uint32_t(w >> 32) == tag) {
+                    layer = int(uint32_t(w));
+                    break;
+                }
+                if (tc::now_ns() - t0 > a.idle_ns + kGridWaitNs) {
+                    fail_wait(s, a.status);
+                    break;
+                }
+            }
+            s.srv_layer = layer;
+        }
+        compute_sync();
+    }
+    if (ct == 0) {
+        s.step_layer = s.srv_layer;
+    }
+    compute_sync();
+    return s.srv_layer;
+}
+
+// CTA 0 reports a step that failed: when the device status word is set at
+// the step's end, it goes to the mailbox with the request's number in `resp`
+// (the host then stops the server and reads the status).  A step that went
+// well needs nothing here: its rows and top-4 are tagged words.
+__device__ void server_answer(Smem &s, const StackArgs &a, int step) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) {
+        return;
+    }
+    const uint32_t st = *reinterpret_cast<const volatile uint32_t *>(a.status);
+    if (st) {
+        a.mbox->status = st;
+        __threadfence_system();
+        st_release_sys(&a.mbox->resp, a.mbox_base + uint32_t(step) + 1u);
+    }
+}
+
 __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps, int nl) {
     Pipe pp;
     for (int step = 0; step < steps; ++step) {
         if (!wait_bar(s, &s.sel_full, uint32_t(step) & 1, a.status)) {
             break;
+        }
+        if (a.mode == 2 && *reinterpret_cast<const volatile int *>(&s.srv_exit)) {
+            break;  // the server took no further request
         }
         int le[kTopK];
         const int n = s.n_local;
@@ -1426,12 +1561,12 @@ __device__ void run_loads(const Ctx &c0, Smem &s, const StackArgs &a, int steps,
             le[q] = (q < n) ? s.local[s.slot_of[q]] : 0;
         }
         Ctx c = c0;
-        c.L = &a.layers[a.layer_begin + step % nl];
+        c.L = &a.layers[a.mode == 2 ? s.step_layer : a.layer_begin + step % nl];
         if (!produce_phase(c, s.plan[n][0], 0, le, pp) || !produce_phase(c, s.plan[n][1], 1, le, pp)) {
             break;
         }
         // the next step's tensor maps, while this step's loads are in flight
-        if (step + 1 < steps) {
+        if (a.mode != 2 && step + 1 < steps) {
             const TmaDesc *nt = a.layers[a.layer_begin + (step + 1) % nl].tma;
 #pragma unroll
             for (int m = 0; m < kTmaCount; ++m) {
@@ -1458,12 +1593,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int E = a.experts;
-    const int nl = a.layer_end - a.layer_begin;
+    const int nl = steps_per_token(a);
     const int steps = a.tokens * nl;
     unsigned gen = 0;
 
     if (threadIdx.x == 0) {
         s.abort = 0;
+        s.srv_exit = 0;
+        s.steps_run = uint32_t(steps);
         // the tag base lives on the device, so a replayed graph of this launch
         // gets new tags: the last CTA to finish advances it by the steps
         s.seq = *reinterpret_cast<const volatile uint32_t *>(a.seq_state);
@@ -1535,11 +1672,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
 
         for (int t = 0; ok && t < a.tokens; ++t) {
             for (int li = 0; ok && li < nl; ++li) {
-                const int l = a.layer_begin + li;
-                const StackLayer &L = a.layers[l];
                 const int step = t * nl + li;
-                const float *xcur = (li == 0) ? a.x + size_t(t) * kDim : a.y + size_t(t) * kDim;
-                const bool export_top = (blockIdx.x == 0 && t == a.tokens - 1 && li == nl - 1);
+                int l = a.layer_begin + li;
+                if (a.mode == 2) {
+                    // the server: the next request's layer (x is in a.srv_x), or leave
+                    l = server_next(s, a, step);
+                    if (l < 0) {
+                        if (threadIdx.x == 0) {
+                            s.steps_run = uint32_t(step) + 1u;  // the exit word used this step's tag
+                            s.srv_exit = 1;
+                            mbar_arrive(&s.sel_full);  // the loads warp sees the exit
+                        }
+                        ok = false;
+                        break;
+                    }
+                }
+                const StackLayer &L = a.layers[l];
+                const int tr = t & a.row_mask;
+                const float *xcur = (a.mode == 2) ? a.srv_x
+                                    : (li == 0)   ? a.x + size_t(tr) * kDim
+                                                  : a.y + size_t(tr) * kDim;
+                const bool export_top =
+                    blockIdx.x == 0 && (a.mode == 2 || (t == a.tokens - 1 && li == nl - 1));
 
                 stamp(a, step, 0);
                 // The gate/up B operand: digit terms of x * g (mode 1) or of h
@@ -1551,13 +1705,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 // the split loop is not unrolled: it runs once per launch, so
                 // its code is fetched cold, and unrolled it would miss the
                 // instruction cache once per pass.
-                const bool split_here = (a.mode == 0) || (step == 0);
+                const bool split_here = (a.mode != 1) || (step == 0);
                 constexpr int kPasses = kBlocks / kComputeWarps;  // 10
                 static_assert(kPasses * kComputeWarps == kBlocks, "split passes");
                 static_assert(sizeof(Smem::bdown) >= 2 * kDim * sizeof(float), "split staging");
                 float *xs = reinterpret_cast<float *>(&s.bdown[0][0][0]);
                 float *gs = xs + kDim;
-                if (split_here) {
+                if (split_here && a.mode == 2) {
+                    // the server's input changes per request: read through L2
+#pragma unroll 1
+                    for (int k = ct; k < kDim; k += kComputeThreads) {
+                        xs[k] = __ldcg(xcur + k);
+                    }
+                } else if (split_here) {
 #pragma unroll 1
                     for (int k = ct; k < kDim; k += kComputeThreads) {
                         cp_async4(xs + k, xcur + k);
@@ -1823,6 +1983,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                 stamp(a, step, 6);
                 // every compute thread leaves or stays together
                 compute_sync();
+                if (a.mode == 2) {
+                    server_answer(s, a, step);
+                }
                 if (threadIdx.x == 0) {
                     s.go = aborted(s) ? 0 : 1;
                 }
@@ -1855,11 +2018,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tbase, kTmemCols);
     }
+    if (a.mode == 2 && blockIdx.x == 0 && threadIdx.x == 0) {
+        st_release_sys(&a.mbox->alive, 0u);  // however the server ends, it takes no more requests
+    }
     if (threadIdx.x == 0) {
         unsigned done;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(done) : "l"(a.seq_state + 1) : "memory");
         if (done == gridDim.x - 1) {
-            a.seq_state[0] = s.seq + uint32_t(steps);
+            a.seq_state[0] = s.seq + s.steps_run;
             a.seq_state[1] = 0u;
         }
     }

@@ -1,6 +1,8 @@
 // kernels.h -- launchers of the MoE kernels (internal to libttl_moe).
 #pragma once
 
+#include <cstddef>
+
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -90,6 +92,27 @@ struct StackLayer {
     const TmaDesc *tma;  // [kTmaCount] in device memory (tensor-core decode)
 };
 
+// The decode server's mailbox (mode 2): pinned host memory mapped into the
+// device's address space.  The host writes x, then the request word (number
+// and layer).  The answer comes as tagged 8-byte words (the request's number
+// in the high half, the value's bits in the low half): the down reducers
+// store y, CTA 0 the top-4, so a word carrying the current number is the
+// data -- no fence, no completion count.  `resp` / `status` report a failed
+// step; `alive` drops to 0 once the kernel takes no more requests.
+struct DecodeMailbox {
+    unsigned long long reqw;  // (number of the last request << 32) | its layer (host, one store)
+    uint32_t stop;    // nonzero: the kernel leaves after the request in hand (host)
+    uint32_t alive;   // 1 while the kernel takes requests (kernel clears it)
+    uint32_t resp;    // number of a request whose step failed (kernel)
+    uint32_t status;  // the device status word of that step (kernel)
+    uint32_t pad[2];
+    unsigned long long top[8];   // tagged: the 4 expert ids, then the 4 weights (kernel)
+    float x[2880];               // 16-byte aligned: the kernel reads it as float4 (host)
+    unsigned long long y[2880];  // tagged output row (kernel)
+};
+static_assert(offsetof(DecodeMailbox, reqw) % 8 == 0, "mailbox request word");
+static_assert(offsetof(DecodeMailbox, x) % 16 == 0 && offsetof(DecodeMailbox, y) % 8 == 0, "mailbox rows");
+
 struct StackArgs {
     const StackLayer *layers;  // device array indexed by layer
     int layer_begin;
@@ -97,7 +120,14 @@ struct StackArgs {
     const float *x;            // [tokens][2880] input (h in mode 0, residual x in mode 1)
     float *y;                  // [tokens][2880] output
     int tokens;
-    int mode;                  // 0: one plain MoE per token (h given); 1: RMSNorm + MoE + residual
+    int mode;                  // 0: one plain MoE per token (h given); 1: RMSNorm + MoE + residual;
+                               // 2: decode server (mode 0 steps on requests from `mbox`)
+    int row_mask;              // token row of x / y = token & row_mask (0 in mode 2: one row)
+    DecodeMailbox *mbox;       // mode 2: the mailbox (device address of mapped host memory)
+    float *srv_x;              // mode 2: [2880] the request's input, copied from the mailbox
+    unsigned long long *go;    // mode 2: [1] (step tag << 32) | layer, published by CTA 0
+    uint32_t mbox_base;        // mode 2: requests answered before this launch
+    unsigned long long idle_ns;  // mode 2: the kernel leaves after this long without a request
     int experts;
     int expert_begin;
     int expert_count;
@@ -264,6 +294,7 @@ struct EpPeers {
     void *base[kMaxWorld];  // every rank's receive block as this GPU addresses it (own included)
 };
 
+void configure_prefill_ep();
 void launch_ep_plan(const int32_t *idx, int tokens, int world, int per_rank, int32_t *tok_off, int32_t *cnt,
                     cudaStream_t stream);
 void launch_ep_send(const float *x, const int32_t *idx, const float *wts, int tokens, int world, int rank, int cap,

@@ -126,6 +126,16 @@ struct ttl_moe {
         DecodeBlock out;
     };
     DecodePin *pin = nullptr;        // pinned host staging, allocated at create
+    // the decode server (ttl_moe_serve): a resident launch fed through a
+    // mailbox in mapped pinned memory
+    DecodeMailbox *mbox = nullptr;      // host address
+    DecodeMailbox *mbox_dev = nullptr;  // the same memory as the device addresses it
+    float *d_srv_x = nullptr;           // [2880] the request's input on the device
+    unsigned long long *d_go = nullptr; // the server's per-step go word
+    uint32_t serve_idle_us = 0;         // 0: no server
+    bool serving = false;               // a server launch may still be on the stream
+    uint32_t req = 0;                   // requests submitted to the mailbox
+    uint32_t mbox_base = 0;             // requests answered before the current server launch
     DecodeBlock *d_dblk = nullptr;   // device side
     std::map<int, std::pair<cudaGraphExec_t, uint64_t>> decode_graphs;  // per layer, captured at upload
     bool profile = false;
@@ -594,6 +604,14 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.y = y;
     a.tokens = int(tokens);
     a.mode = mode;
+    a.row_mask = (mode == 2) ? 0 : 0x7fffffff;
+    if (mode == 2) {
+        a.mbox = h->mbox_dev;
+        a.srv_x = h->d_srv_x;
+        a.go = h->d_go;
+        a.mbox_base = h->mbox_base;
+        a.idle_ns = uint64_t(h->serve_idle_us) * 1000ull;
+    }
     a.experts = int(h->cfg.experts);
     a.expert_begin = h->expert_begin;
     a.expert_count = h->expert_count;
@@ -647,6 +665,140 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
         h->stack_steps = int(tokens) * (end - begin);
     }
     h->launches += 1;
+    return TTL_OK;
+}
+
+// ---- the decode server (ttl_moe_serve) ----
+// A resident launch of the decode kernel in mode 2 answers blocking decode
+// calls through the mailbox: no launch, copy or stream synchronisation per
+// call.  While it is resident no other kernel can run on the GPU, so it
+// leaves after the handle's idle limit without a request, and every other
+// use of the handle's stream stops it first.
+
+int check_status(ttl_moe *h);
+
+uint32_t mbox_load(const uint32_t *p) {
+    return __atomic_load_n(p, __ATOMIC_ACQUIRE);
+}
+void mbox_store(uint32_t *p, uint32_t v) {
+    __atomic_store_n(p, v, __ATOMIC_RELEASE);
+}
+
+// Stops a resident server (it leaves at its next wait for a request) and
+// waits for the launch to end.
+int stop_server(ttl_moe *h) {
+    if (!h->serving) {
+        return TTL_OK;
+    }
+    mbox_store(&h->mbox->stop, 1u);
+    const cudaError_t e = cudaStreamSynchronize(h->stream);
+    h->serving = false;
+    mbox_store(&h->mbox->stop, 0u);
+    TTL_TRY_CUDA(h, e);
+    return TTL_OK;
+}
+
+// Launches the server; request number `base` + 1 is its first step.
+int launch_server(ttl_moe *h, uint32_t base) {
+    h->mbox_base = base;
+    mbox_store(&h->mbox->stop, 0u);
+    mbox_store(&h->mbox->alive, 1u);
+    const int rc = enqueue_stack(h, 0, int(h->cfg.layers), h->d_srv_x, h->d_y, size_t(1) << 30, 2);
+    if (rc) {
+        mbox_store(&h->mbox->alive, 0u);
+        return rc;
+    }
+    h->serving = true;
+    return TTL_OK;
+}
+
+// One blocking decode through the server: x and the layer into the mailbox,
+// the request number bumped, then a spin on the answer.  A launch that left
+// (idle) before taking the request is replaced by one whose first step is it.
+int serve_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
+    for (uint32_t l = 0; l < h->cfg.layers; ++l) {
+        if (!h->layers[l].uploaded) {
+            return fail(h, TTL_ERR_STATE, "the decode server needs every layer uploaded");
+        }
+    }
+    DecodeMailbox *mb = h->mbox;
+    if (!h->serving || mbox_load(&mb->alive) == 0u) {
+        const int rc = stop_server(h);  // a launch that left: wait for its end
+        if (rc) {
+            return rc;
+        }
+        const int lrc = launch_server(h, h->req);
+        if (lrc) {
+            return lrc;
+        }
+    }
+    std::memcpy(mb->x, x, kDim * sizeof(float));
+    const uint32_t r = ++h->req;
+    __atomic_store_n(&mb->reqw, (static_cast<unsigned long long>(r) << 32) | uint32_t(layer), __ATOMIC_RELEASE);
+    const auto deadline = Clock::now() + std::chrono::milliseconds(h->timeout_ms);
+    // the answer is tagged words carrying r: the top-4, then every row value
+    auto tag_of = [](const unsigned long long *p) {
+        return uint32_t(__atomic_load_n(p, __ATOMIC_ACQUIRE) >> 32);
+    };
+    int next = 0;  // rows [0, next) carry r
+    int top = 0;   // top-4 words [0, top) carry r
+    for (uint32_t spins = 0;; ++spins) {
+        while (top < 8 && tag_of(&mb->top[top]) == r) {
+            ++top;
+        }
+        while (next < kDim && tag_of(&mb->y[next]) == r) {
+            ++next;
+        }
+        if (top == 8 && next == kDim) {
+            break;
+        }
+        if (mbox_load(&mb->resp) == r) {  // the step reported a failure
+            stop_server(h);
+            return check_status(h);
+        }
+        if (mbox_load(&mb->alive) == 0u) {
+            // the launch ended without answering: an error it recorded, or
+            // it left idle just before the request came
+            const int rc = stop_server(h);
+            uint32_t st = 0;
+            TTL_TRY_CUDA(h, cudaMemcpy(&st, h->d_status, sizeof(st), cudaMemcpyDeviceToHost));
+            if (rc || st) {
+                return rc ? rc : check_status(h);
+            }
+            const int lrc = launch_server(h, r - 1);
+            if (lrc) {
+                return lrc;
+            }
+            continue;
+        }
+        if ((spins & 1023u) == 0u) {
+            // a launch that failed is reported at once, not at the deadline
+            const cudaError_t q = cudaStreamQuery(h->stream);
+            if (q != cudaErrorNotReady && q != cudaSuccess) {
+                h->serving = false;
+                return fail(h, TTL_ERR_CUDA, std::string("decode server: ") + cudaGetErrorString(q));
+            }
+            if (Clock::now() > deadline) {
+                return fail(h, TTL_ERR_DEVICE, "the decode server did not answer within the handle's timeout");
+            }
+        }
+#if defined(__x86_64__)
+        __builtin_ia32_pause();
+#endif
+    }
+    for (int k = 0; k < kDim; ++k) {
+        const uint32_t bits = uint32_t(mb->y[k]);
+        std::memcpy(out + k, &bits, sizeof(float));
+    }
+    for (int q = 0; q < 4; ++q) {
+        if (top4_idx) {
+            top4_idx[q] = int32_t(uint32_t(mb->top[q]));
+        }
+        if (top4_w) {
+            const uint32_t bits = uint32_t(mb->top[4 + q]);
+            std::memcpy(top4_w + q, &bits, sizeof(float));
+        }
+    }
     return TTL_OK;
 }
 
@@ -943,6 +1095,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     configure_decode_kernels();
     configure_prefill_kernels();
     configure_prefill_tc();
+    configure_prefill_ep();
     configure_decode_tc();
     if (cudaEventCreate(&h->stack_ev[0]) != cudaSuccess || cudaEventCreate(&h->stack_ev[1]) != cudaSuccess) {
         return bail(fail(h, TTL_ERR_CUDA, "cudaEventCreate failed"));
@@ -1102,8 +1255,12 @@ void ttl_moe_destroy(ttl_moe *h) {
         return;
     }
     cudaSetDevice(h->device);
+    stop_server(h);
     if (h->stream) {
         stream_wait(h);  // bounded for a multi-rank handle
+    }
+    if (h->mbox) {
+        cudaFreeHost(h->mbox);
     }
     for (auto &g : h->graphs) {
         cudaGraphExecDestroy(g.second.exec);
@@ -1168,6 +1325,9 @@ int upload_layer(ttl_moe *h, int layer, const float *router_w, const float *rout
                  bool packed) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     if (layer < 0 || layer >= int(h->cfg.layers)) {
         return fail(h, TTL_ERR_ARGUMENT, "layer out of range");
@@ -1263,6 +1423,9 @@ int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
+    }
     if (layer < 0 || layer >= int(h->cfg.layers) || !norm_w) {
         return fail(h, TTL_ERR_ARGUMENT, "bad layer or null weights");
     }
@@ -1281,6 +1444,9 @@ int ttl_moe_upload_norm(ttl_moe *h, int layer, const float *norm_w) {
 int ttl_moe_decode_async(ttl_moe *h, int layer, const float *x, float *out, int32_t *top4_idx, float *top4_w) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     if (const int frc = ep_ready(h)) {
         return frc;
@@ -1323,6 +1489,9 @@ int ttl_moe_decode(ttl_moe *h, int layer, const float *x, float *out, int32_t *t
     rc = rc ? rc : set_device(h);
     if (rc) {
         return rc;
+    }
+    if (h->serve_idle_us) {
+        return serve_decode(h, layer, x, out, top4_idx, top4_w);
     }
     if (!stack_path(h)) {
         TTL_TRY_CUDA(h, cudaMemcpyAsync(h->d_x, x, kDim * sizeof(float), cudaMemcpyHostToDevice, h->stream));
@@ -1374,6 +1543,9 @@ int ttl_moe_prefill_async(ttl_moe *h, int layer, const float *x, size_t tokens, 
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
+    }
     if (const int frc = ep_ready(h)) {
         return frc;
     }
@@ -1410,6 +1582,9 @@ int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
                     float *top4_w) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     if (const int frc = ep_ready(h)) {
         return frc;
@@ -1448,6 +1623,9 @@ int ttl_moe_prefill(ttl_moe *h, int layer, const float *x, size_t tokens, float 
 int ttl_moe_forward_async(ttl_moe *h, int layer_begin, int layer_end, const float *x, float *y, size_t tokens) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     if (const int frc = ep_ready(h)) {
         return frc;
@@ -1548,6 +1726,9 @@ int ttl_moe_profile(ttl_moe *h, int enable) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
+    }
     int rc = set_device(h);
     if (rc) {
         return rc;
@@ -1568,6 +1749,9 @@ int ttl_moe_profile(ttl_moe *h, int enable) {
 int ttl_moe_trace(ttl_moe *h, int steps, uint64_t *out) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     int rc = set_device(h);
     if (rc) {
@@ -1594,6 +1778,9 @@ int ttl_moe_trace(ttl_moe *h, int steps, uint64_t *out) {
 int ttl_moe_record(ttl_moe *h, size_t steps, float *y_log, int32_t *idx_log, float *w_log) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     if (steps > 0 && (!y_log || !idx_log || !w_log)) {
         return fail(h, TTL_ERR_ARGUMENT, "step log needs its three buffers");
@@ -1649,8 +1836,48 @@ int ttl_moe_sync(ttl_moe *h) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
     }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
+    }
     int rc = set_device(h);
     return rc ? rc : sync_and_check(h);
+}
+
+int ttl_moe_serve(ttl_moe *h, uint32_t idle_us) {
+    if (!h) {
+        return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (idle_us > 1000000u) {
+        return fail(h, TTL_ERR_ARGUMENT, "the idle limit is at most 1000000 us");
+    }
+    if (idle_us && h->cfg.world != 1) {
+        return fail(h, TTL_ERR_UNSUPPORTED, "the decode server runs on single-GPU handles");
+    }
+    int rc = set_device(h);
+    rc = rc ? rc : stop_server(h);
+    if (rc) {
+        return rc;
+    }
+    if (idle_us && !h->mbox) {
+        void *p = nullptr;
+        if (cudaHostAlloc(&p, sizeof(DecodeMailbox), cudaHostAllocMapped) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(h, TTL_ERR_CUDA, "cannot allocate the decode server's mailbox");
+        }
+        std::memset(p, 0, sizeof(DecodeMailbox));
+        h->mbox = static_cast<DecodeMailbox *>(p);
+        void *dev = nullptr;
+        TTL_TRY_CUDA(h, cudaHostGetDevicePointer(&dev, p, 0));
+        h->mbox_dev = static_cast<DecodeMailbox *>(dev);
+        rc = alloc_n(h, &h->d_srv_x, kDim);
+        rc = rc ? rc : alloc_n(h, &h->d_go, 1);
+        if (rc) {
+            return rc;
+        }
+        TTL_TRY_CUDA(h, cudaMemset(h->d_go, 0, sizeof(unsigned long long)));
+    }
+    h->serve_idle_us = idle_us;
+    return TTL_OK;
 }
 
 int ttl_moe_set_timeout(ttl_moe *h, uint32_t ms) {
@@ -1675,6 +1902,9 @@ int ttl_moe_set_timeout(ttl_moe *h, uint32_t ms) {
 int ttl_moe_resync(ttl_moe *h) {
     if (!h) {
         return fail(nullptr, TTL_ERR_ARGUMENT, "null handle");
+    }
+    if (const int src = stop_server(h)) {  // a resident decode server leaves the stream first
+        return src;
     }
     int rc = set_device(h);
     if (rc) {

@@ -377,9 +377,15 @@ __global__ void prefill_combine_kernel(PrefillWork w, int tokens, float *__restr
 
 } // namespace
 
+// The prefill kernels alternate with the tensor-core kernels (about 200 KB
+// of shared memory each) on one stream: every kernel asks for the largest
+// shared-memory carveout, so no launch waits for the SMs to repartition L1.
 void configure_prefill_kernels() {
     cudaFuncSetAttribute(prefill_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          int(router_smem_bytes(kMaxExperts)));
+    cudaFuncSetAttribute(prefill_router_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(prefill_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
 }
 
 void launch_prefill_router(const LayerDev &L, const PrefillWork &w, const PrefillShape &s, const float *x,

@@ -254,6 +254,16 @@ __global__ void ep_combine_kernel(const int32_t *__restrict__ idx, const float *
 
 }  // namespace
 
+// Largest shared-memory carveout for the dispatch kernels too (they run
+// between the tensor-core kernels on the same stream).
+void configure_prefill_ep() {
+    cudaFuncSetAttribute(ep_plan_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(ep_send_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(ep_wait_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(ep_back_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+    cudaFuncSetAttribute(ep_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
+}
+
 void launch_ep_plan(const int32_t *idx, int tokens, int world, int per_rank, int32_t *tok_off, int32_t *cnt,
                     cudaStream_t stream) {
     ep_plan_kernel<<<world, 1024, 0, stream>>>(idx, tokens, world, per_rank, tok_off, cnt);

@@ -526,6 +526,7 @@ void configure_prefill_tc() {
                          int(sizeof(PSmem<true>) + 1024));
     cudaFuncSetAttribute(prefill_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          int(sizeof(PSmem<false>) + 1024));
+    cudaFuncSetAttribute(prefill_split_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, int(cudaSharedmemCarveoutMaxShared));
 }
 
 void launch_prefill_gateup(const LayerDev &L, const TmaDesc *tma, const PrefillWork &w, const PrefillShape &s,

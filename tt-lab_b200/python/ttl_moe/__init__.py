@@ -88,6 +88,7 @@ def lib():
         "ttl_attn_sync": (i32, [vp]),
         "ttl_attn_stream": (vp, [vp]),
         "ttl_moe_set_timeout": (i32, [vp, u32]),
+        "ttl_moe_serve": (i32, [vp, u32]),
         "ttl_moe_decode": (i32, [vp, i32, fp, fp, vp, fp]),
         "ttl_moe_prefill": (i32, [vp, i32, fp, sz, fp, vp, fp]),
         "ttl_moe_forward": (i32, [vp, i32, i32, fp, fp, sz]),
@@ -266,6 +267,10 @@ class MoE:
 
     def set_timeout(self, ms):
         self._check(lib().ttl_moe_set_timeout(self.h, int(ms)))
+
+    def serve(self, idle_us):
+        """Blocking decode calls through a resident decode kernel (0: off)."""
+        self._check(lib().ttl_moe_serve(self.h, int(idle_us)))
 
     def stream(self) -> int:
         return lib().ttl_moe_stream(self.h) or 0
