@@ -747,8 +747,9 @@ int ttl_attn_forward_async(ttl_attn *h, int layer, size_t position, const float 
     const AttnLayer &s = h->L[size_t(layer)];
     QkvArgs qa{x,  s.norm, s.q, s.k, s.v, s.qb, s.kb, s.vb, h->freq, h->magnitude, int(position), h->q, s.kc, s.vc,
                h->status};
-    const int qkv_ctas = std::min(h->sms, (kQkvItems + kQkvThreads / 32 - 1) / (kQkvThreads / 32));
-    attn_qkv_kernel<<<qkv_ctas, kQkvThreads, kQkvSmem, h->stream>>>(qa);
+    // every SM: items are spread over the CTAs first, so each CTA gets about
+    // 1280 / 148 of them
+    attn_qkv_kernel<<<h->sms, kQkvThreads, kQkvSmem, h->stream>>>(qa);
     // window (src/model.cpp:261-262): even layers attend to the last 128 positions
     const size_t first = (layer % 2 == 0 && position + 1 > size_t(kWindow)) ? position + 1 - kWindow : 0;
     const int count = int(position + 1 - first);
