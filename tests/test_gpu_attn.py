@@ -50,6 +50,26 @@ def test_attention_matches_reference_position_by_position(layers):
             assert worst_res <= TOL, (l, worst_res)
 
 
+def test_attention_long_context_tiles(layers):
+    """A full-attention layer to 1040 positions: each of the 8 splits of the
+    window then spans three staged tiles of 64 positions (the third refills
+    the first buffer), checked at every position."""
+    import ttl_moe
+    from ttl_moe import synth
+    P = 1040
+    x = synth.inputs_host(91, P)
+    r_res, r_att = oracle.attention_steps(layers[1], 1, x, impl=impl())
+    with ttl_moe.Attention(layers=2, token_capacity=P, device=0) as a:
+        a.upload_layer(1, layers[1])
+        worst_res = worst_att = 0.0
+        for p in range(P):
+            res, att = a.forward(1, p, x[p])
+            worst_res = max(worst_res, rel(res, r_res[p]))
+            worst_att = max(worst_att, rel(att, r_att[p]))
+    assert worst_att <= TOL, worst_att
+    assert worst_res <= TOL, worst_res
+
+
 def test_attention_errors_follow_reference(layers):
     import ttl_moe
     x = np.zeros(2880, np.float32)
