@@ -1275,64 +1275,54 @@ __device__ float exact_logit(const float *__restrict__ wrow, float bias, const f
     return acc;
 }
 
-// Order key of expert e: larger logits first, the lower index first among
-// equal logits, NaN after every number (-0 and +0 compare equal).  Keys of
-// different experts differ; an absent expert's key (kAbsentKey) is below all.
-constexpr long long kAbsentKey = static_cast<long long>(0x8000000000000000ull);
-__device__ __forceinline__ long long order_key(float v, int e) {
+// Order key of a logit: larger logits larger, -0 and +0 equal, NaN below
+// every number (INT_MIN, which no number maps to).
+__device__ __forceinline__ int logit_key(float v) {
     int b = __float_as_int(v + 0.0f);
     b = (b >= 0) ? b : (b ^ 0x7fffffff);
-    b = (v == v) ? b : int(0x80000000u);
-    return static_cast<long long>((static_cast<unsigned long long>(unsigned(b)) << 32) | unsigned(kMaxExperts - e));
+    return (v == v) ? b : int(0x80000000u);
 }
 
-// Ranks of this lane's NPER experts against all 32 * NPER keys, through
-// register shuffles and without branches.
-template <int NPER>
-__device__ __forceinline__ void rank_keys(const long long (&key)[4], int (&rank)[4]) {
-#pragma unroll
-    for (int c = 0; c < NPER; ++c) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const long long kj = __shfl_sync(0xffffffffu, key[c], j);
-#pragma unroll
-            for (int k = 0; k < NPER; ++k) {
-                rank[k] += (kj > key[k]) ? 1 : 0;
-            }
-        }
-    }
-}
-
-// Top-4 of s.logit, by warp 0: lane l ranks experts l, l + 32, ... against
-// all of them, and the experts of rank 0-3 land in s.sel (the keys are a
-// total order, so s.sel is always filled).  Selection sort with a strict
-// ">" (src/model.cpp:296-309) gives the same order whenever the logits are
-// distinct; equal logits are the ambiguous case the callers resolve.
+// Top-4 of s.logit, by warp 0, in four rounds of warp reductions: lane l holds
+// experts l, l + 32, l + 64, l + 96; each round takes the largest key still in
+// play (redux.sync max), then the lowest expert index among its holders
+// (redux.sync min), writes it to s.sel[round] and retires it.  The order --
+// larger logits first, the lower index first among equal logits, NaN after
+// every number -- is the selection sort's with a strict ">"
+// (src/model.cpp:296-309) whenever the logits are distinct; equal logits are
+// the ambiguous case the callers resolve.  With at least kTopK experts every
+// round finds one.
 __device__ __forceinline__ void warp_top4(Smem &s, int experts) {
     const int lane = threadIdx.x & 31;
-    long long key[4];
-    int rank[4];
+    static_assert(kMaxExperts == 128, "four experts per lane");
+    int key[4];
+    unsigned live = 0u;  // bit k: expert lane + 32 k is present and not yet taken
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int e = lane + 32 * k;
-        key[k] = (e < experts) ? order_key(s.logit[e], e) : kAbsentKey;
-        rank[k] = 0;
-    }
-    static_assert(kMaxExperts == 128, "four keys per lane");
-    if (experts <= 32) {
-        rank_keys<1>(key, rank);
-    } else if (experts <= 64) {
-        rank_keys<2>(key, rank);
-    } else if (experts <= 96) {
-        rank_keys<3>(key, rank);
-    } else {
-        rank_keys<4>(key, rank);
+        key[k] = (e < experts) ? logit_key(s.logit[e]) : int(0x80000000u);
+        live |= (e < experts) ? (1u << k) : 0u;
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int e = lane + 32 * k;
-        if (e < experts && rank[k] < kTopK) {
-            s.sel[rank[k]] = e;
+    for (int r = 0; r < kTopK; ++r) {
+        // this lane's best expert in play: the largest key, the lowest k among equal keys
+        int best = int(0x80000000u);
+        int bk = -1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if (((live >> k) & 1u) && (bk < 0 || key[k] > best)) {
+                best = key[k];
+                bk = k;
+            }
+        }
+        const int m = __reduce_max_sync(0xffffffffu, best);
+        const unsigned cand = (bk >= 0 && best == m) ? unsigned(lane + 32 * bk) : 0xffffffffu;
+        const unsigned win = __reduce_min_sync(0xffffffffu, cand);
+        if (lane == 0) {
+            s.sel[r] = (win < unsigned(experts)) ? int(win) : 0;
+        }
+        if (bk >= 0 && cand == win) {
+            live &= ~(1u << bk);
         }
     }
 }
