@@ -113,6 +113,7 @@ constexpr uint32_t kColSfbD = kColSfbG + kSfbCols;             // kDownSlots x k
 constexpr int kDownSlots = 2;                 // down-projection experts a CTA touches (checked)
 static_assert(kColSfbD + kSfbCols * kDownSlots <= kTmemCols, "tensor memory map");
 constexpr int kPreE = 32;                     // next-layer router weights the down epilogue loads early
+static_assert(kPreE == kRouterMapFirstExpert, "the router tensor map's box starts past the preloaded experts");
 constexpr int kOwnMax = 3;                    // tiles a CTA reduces in one phase (checked)
 constexpr unsigned long long kGridWaitNs = 2000000000ull;
 
@@ -787,6 +788,21 @@ __device__ __forceinline__ int steps_per_token(const StackArgs &a) {
     return a.mode == 2 ? 1 : a.layer_end - a.layer_begin;
 }
 
+// Loads of a tile's epilogue operands, issued where they stand: as volatile
+// asm they stay ahead of the accumulator waits that follow them (a plain load
+// of read-only data may be moved down to its first use, which would put a
+// memory round trip on the reducer's critical path).
+__device__ __forceinline__ float ld_early_nc(const float *p) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ float ld_early_cg(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
 template <bool kWideRouter>
 __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int tile, int t_token, int li, bool next_router,
                                               TileOps &o) {
@@ -814,15 +830,12 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
     const int row = 128 * tile + i;
     if (kWideRouter && next_router) {
         // the next layer's router weights of this tile's rows for the experts
-        // past kPreE (loaded by the reducer after the exchange, when the sums
-        // are on the step's critical path) go to L2 now: one bulk prefetch of
-        // the tile's row slice per expert
-        const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
-        const uint32_t bytes = uint32_t(min(128, kDim - 128 * tile)) * 4u;
-        for (int e = kPreE + i; e < a.experts; e += 32 * kEpiWarps) {
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(N.router_w + size_t(e) * kDim + 128 * tile),
-                         "r"(bytes)
-                         : "memory");
+        // past kPreE (staged by the reducer after the exchange, when the sums
+        // are on the step's critical path) go to L2 now: one tensor prefetch
+        // of the box the staging copies
+        if (i == 0) {
+            const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
+            tc::tma_prefetch_2d(N.tma + kTmaRouter, 128 * tile, kPreE);
         }
     }
     if (row >= kDim) {
@@ -831,7 +844,7 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
     float b[kTopK];
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-        b[k] = (k < s.n_local) ? __ldg(L.down_b + size_t(s.local[s.slot_of[k]]) * kDim + row) : 0.0f;
+        b[k] = (k < s.n_local) ? ld_early_nc(L.down_b + size_t(s.local[s.slot_of[k]]) * kDim + row) : 0.0f;
     }
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
@@ -842,18 +855,19 @@ __device__ __forceinline__ void load_tile_ops(const Ctx &c, const Phase &p, int 
     if (a.mode == 1) {
         const int tr = t_token & a.row_mask;
         const float *xcur = (li == 0) ? a.x + size_t(tr) * kDim : a.y + size_t(tr) * kDim;
-        o.resid = __ldcg(xcur + row);
+        o.resid = ld_early_cg(xcur + row);
     }
     if (next_router) {
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
         const float *nrw = N.router_w;
-        o.nw = __ldg(N.norm_w + row);
+        o.nw = ld_early_nc(N.norm_w + row);
         if (!more_layers) {
-            o.xnext = __ldcg(a.x + size_t(t_token + 1) * kDim + row);
+            o.xnext = ld_early_cg(a.x + size_t(t_token + 1) * kDim + row);
         }
+        static_assert(kPreE <= 32, "every handle has at least kPreE experts (32 or 128)");
 #pragma unroll
         for (int e = 0; e < kPreE; ++e) {
-            o.rw[e] = (e < a.experts) ? __ldg(nrw + size_t(e) * kDim + row) : 0.0f;
+            o.rw[e] = ld_early_nc(nrw + size_t(e) * kDim + row);
         }
     }
 }
@@ -882,14 +896,12 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
     const bool stage_rw = kWideRouter && p.kind == 1 && next_router;
     const uint32_t rw_parity = kWideRouter ? (s.rw_uses & 1u) : 0u;
     if (stage_rw && i == 0) {
+        // one tensor copy: [E - kPreE experts][128 rows] f32 (rows past 2880
+        // read as zero), the layout the products below index
         const StackLayer &N = a.layers[more_layers ? a.layer_begin + li + 1 : a.layer_begin];
-        const uint32_t rb = uint32_t(min(128, kDim - 128 * tile)) * 4u;
         ++s.rw_issued;
-        tc::mbar_expect_tx(&s.rwbar, uint32_t(E - kPreE) * rb);
-        float *dst = reinterpret_cast<float *>(&s.a[0][0][0][0]);
-        for (int e = kPreE; e < E; ++e) {
-            bulk_load(dst + size_t(e - kPreE) * 128, N.router_w + size_t(e) * kDim + 128 * tile, rb, &s.rwbar);
-        }
+        tc::mbar_expect_tx(&s.rwbar, uint32_t(E - kPreE) * 128u * 4u);
+        tc::tma_load_2d(&s.a[0][0][0][0], N.tma + kTmaRouter, 128 * tile, kPreE, &s.rwbar);
     }
     if (et.nslot > 1) {
         // the other contributors' tagged partials (after an abort the sums
@@ -952,33 +964,46 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
         // f32 products transposed-summed over the 32 rows (f64 from there on)
         const float xr = more_layers ? yv : o.xnext;
         const float xg = __fmul_rn(xr, o.nw);  // 0 past the last row
-        for (int b = 0; 16 * b < E; ++b) {
+        // 16 experts' products of this row -> their sums over the warp's rows
+        const auto route16 = [&](float (&v)[16], int b) {
+            const float tot = transpose_sum16(v, lane);
+            const int e = 16 * b + transpose_index(lane);
+            if ((lane & 1) == 0 && e < E) {
+                s.rsum[w][e] = double(tot);
+            }
+        };
+        // the first kPreE experts from registers (static indices: o.rw stays
+        // in registers)
+        static_assert(kPreE == 32, "two groups of 16 preloaded experts");
+        {
             float v[16];
-            if (b < kPreE / 16) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    v[j] = __fmul_rn(b == 0 ? o.rw[j] : o.rw[16 + j], xg);
-                }
-            } else if (kWideRouter) {
-                if (b == kPreE / 16) {
-                    // every thread waits for the staged weights (bounded, and
-                    // not cut short by an abort; a wait that gives up leaves
-                    // the copies to the drain before the CTA exits)
-                    if (!tc::mbar_wait(&s.rwbar, rw_parity)) {
-                        fail_wait(s, a.status);
-                    }
-                }
-                const float *rws = reinterpret_cast<const float *>(&s.a[0][0][0][0]);
+            for (int j = 0; j < 16; ++j) {
+                v[j] = __fmul_rn(o.rw[j], xg);
+            }
+            route16(v, 0);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                v[j] = __fmul_rn(o.rw[16 + j], xg);
+            }
+            route16(v, 1);
+        }
+        if (kWideRouter) {
+            // every thread waits for the staged weights (bounded, and not cut
+            // short by an abort; a wait that gives up leaves the copies to
+            // the drain before the CTA exits)
+            if (!tc::mbar_wait(&s.rwbar, rw_parity)) {
+                fail_wait(s, a.status);
+            }
+            const float *rws = reinterpret_cast<const float *>(&s.a[0][0][0][0]);
+            for (int b = kPreE / 16; 16 * b < E; ++b) {
+                float v[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int e = 16 * b + j;
                     v[j] = (e < E && row < kDim) ? __fmul_rn(rws[size_t(e - kPreE) * 128 + i], xg) : 0.0f;
                 }
-            }
-            const float tot = transpose_sum16(v, lane);
-            const int e = 16 * b + transpose_index(lane);
-            if ((lane & 1) == 0 && e < E) {
-                s.rsum[w][e] = double(tot);
+                route16(v, b);
             }
         }
         const double sq = warp_sum_d(row < kDim ? double(__fmul_rn(xr, xr)) : 0.0);
@@ -1160,11 +1185,13 @@ __device__ void run_epilogue(const Ctx &c, const Phase &p, const Plan &pl, Pipe 
 // then thread e <= E adds expert e's 23 tile partials in tile
 // order (every CTA gets the same sums) into s.rsum[0][e].  Called by every
 // compute thread; needs a compute_sync before s.rsum is read.
+// kItems (tile, expert) items per thread cover all of them in one round of
+// polls: 3 for 32 experts (23 x 33 <= 288 x 3), 11 for 128 (23 x 129 <= 288 x 11).
+template <int kItems>
 __device__ __forceinline__ void gather_router_sums(Smem &s, const StackArgs &a, int step, int E) {
     static_assert(offsetof(Smem, bdown) == offsetof(Smem, bgu) + sizeof(Smem::bgu) &&
                       sizeof(Smem::bgu) + sizeof(Smem::bdown) >= sizeof(double) * kTiles * (kMaxExperts + 1),
                   "router scratch: the two B-operand areas, adjacent");
-    constexpr int kItems = 6;
     const int ct = threadIdx.x;
     const int per = E + 1;
     const int items = kTiles * per;
@@ -1726,7 +1753,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                     // router sums: the kernel's opening pass (step 0) or the
                     // previous step's down reducers
                     if (step > 0) {
-                        gather_router_sums(s, a, step, E);
+                        static_assert(kTiles * (kPreE + 1) <= kComputeThreads * 3 &&
+                                          kTiles * (kMaxExperts + 1) <= kComputeThreads * 11,
+                                      "router sums in one round of polls");
+                        gather_router_sums<kWideRouter ? 11 : 3>(s, a, step, E);
                     }
                     compute_sync();
                     stamp(a, step, 4);

@@ -72,12 +72,18 @@ struct alignas(64) TmaDesc {
 // Tensor maps of one layer's packed expert matrices: the nibble rows as bytes
 // (all local experts; box coordinates (byte of the row, row, expert); boxes
 // of 128 bytes x 128 rows, 128-byte swizzle; bytes past 1440 read as zero).
+// kTmaRouter (handles of more than 32 experts only): the router weights f32
+// [experts][2880], box (128 rows of the hidden dimension, experts 32..E-1),
+// no swizzle, rows past 2880 read as zero -- the decode kernel's staging of
+// one down tile's next-layer router weights in a single copy.
 enum TmaIndex {
     kTmaGate,
     kTmaUp,
     kTmaDown,
+    kTmaRouter,
     kTmaCount
 };
+constexpr int kRouterMapFirstExpert = 32;
 
 struct StackLayer {
     const float *router_w;

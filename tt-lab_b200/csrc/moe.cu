@@ -570,6 +570,16 @@ int build_layer_maps(ttl_moe *h, const LayerStore &st, TmaDesc *out) {
     weights(kTmaGate, st.gate);
     weights(kTmaUp, st.up);
     weights(kTmaDown, st.down);
+    std::memset(&maps[kTmaRouter], 0, sizeof(maps[kTmaRouter]));
+    const int E = int(h->cfg.experts);
+    if (E > kRouterMapFirstExpert) {
+        const cuuint64_t dims[2] = {cuuint64_t(kDim), cuuint64_t(E)};
+        const cuuint64_t strides[1] = {cuuint64_t(kDim) * sizeof(float)};
+        const cuuint32_t box[2] = {128, cuuint32_t(E - kRouterMapFirstExpert)};
+        ok = ok && enc(&maps[kTmaRouter], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, st.router_w, dims, strides, box, ones,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
     if (!ok) {
         return fail(h, TTL_ERR_CUDA, "cuTensorMapEncodeTiled rejected a weight tensor map");
     }

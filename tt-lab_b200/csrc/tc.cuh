@@ -163,6 +163,22 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// Tiled 2-D load of one box of `tmap` at element coordinates (x, y);
+// completes the box's bytes on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Prefetch of one box of a 2-D `tmap` at (x, y) into L2.  No multicast.
+__device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap), "r"(x), "r"(y)
+                 : "memory");
+}
+
 // Tiled 3-D load of one box of `tmap` (a CUtensorMap in global memory) at
 // element coordinates (x, y, z); completes `bytes` of the barrier's
 // transaction count.  No multicast.
