@@ -1029,8 +1029,11 @@ __device__ void finish_tile(const Ctx &c, const Phase &p, const EpiTile &et, con
             }
             const float hi = __double2float_rn(tot);
             const float lo = __double2float_rn(tot - double(hi));
-            st_tagged(rp + 2 * e, tagged(tag, hi));
-            st_tagged(rp + 2 * e + 1, tagged(tag, lo));
+            // both words in one 16-byte store (each half is single-copy atomic
+            // and carries the tag)
+            asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(rp + 2 * e), "l"(tagged(tag, hi)),
+                         "l"(tagged(tag, lo))
+                         : "memory");
         }
         // then this tile's output rows and the next step's gate/up B operand
         // (digit terms of x * g; the RMSNorm scale is a scalar applied to the
@@ -1194,32 +1197,59 @@ __device__ __forceinline__ void gather_router_sums(Smem &s, const StackArgs &a, 
                   "router scratch: the two B-operand areas, adjacent");
     const int ct = threadIdx.x;
     const int per = E + 1;
-    const int items = kTiles * per;
+    const int items = kTiles * per;  // <= kComputeThreads * kItems (checked by the caller)
     const uint32_t tag = step_tag(s, step - 1);
     const unsigned long long *rp = a.rpt + size_t((step - 1) & 1) * kTiles * (kMaxExperts + 1) * 2;
     double *rs = reinterpret_cast<double *>(&s.bgu[0][0]);
-    for (int base = 0; base < items; base += kComputeThreads * kItems) {
-        float v[2 * kItems];
-        uint32_t want = 0u;
+    // item i = (tile, expert): its two tagged words (hi, lo) are adjacent and
+    // 16-byte aligned, so one vector load fetches both (each 8-byte half is
+    // single-copy atomic and carries its own tag)
+    const unsigned long long *addr[kItems];
+    uint32_t miss = 0u;
+#pragma unroll
+    for (int m = 0; m < kItems; ++m) {
+        const int i = ct + kComputeThreads * m;
+        const int t = i / per;
+        addr[m] = rp + (size_t(t) * (kMaxExperts + 1) + size_t(i - t * per)) * 2;
+        miss |= (i < items) ? (1u << m) : 0u;
+    }
+    double v[kItems];
+    unsigned long long t0 = 0ull;
+    while (miss != 0u) {
+        unsigned long long w0[kItems], w1[kItems];
 #pragma unroll
         for (int m = 0; m < kItems; ++m) {
-            v[2 * m] = v[2 * m + 1] = 0.0f;
-            want |= (base + ct + kComputeThreads * m < items) ? (3u << (2 * m)) : 0u;
-        }
-        poll_tagged<2 * kItems>(
-            s,
-            [&](int k) {
-                const int i = base + ct + kComputeThreads * (k >> 1);
-                const int t = i / per;
-                return rp + (size_t(t) * (kMaxExperts + 1) + size_t(i - t * per)) * 2 + (k & 1);
-            },
-            want, tag, v, a.status);
-#pragma unroll
-        for (int m = 0; m < kItems; ++m) {
-            const int i = base + ct + kComputeThreads * m;
-            if (i < items) {
-                rs[i] = double(v[2 * m]) + double(v[2 * m + 1]);
+            w0[m] = w1[m] = 0ull;
+            if ((miss >> m) & 1u) {
+                asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];"
+                             : "=l"(w0[m]), "=l"(w1[m])
+                             : "l"(addr[m])
+                             : "memory");
             }
+        }
+#pragma unroll
+        for (int m = 0; m < kItems; ++m) {
+            if (((miss >> m) & 1u) && uint32_t(w0[m] >> 32) == tag && uint32_t(w1[m] >> 32) == tag) {
+                v[m] = double(__uint_as_float(uint32_t(w0[m]))) + double(__uint_as_float(uint32_t(w1[m])));
+                miss &= ~(1u << m);
+            }
+        }
+        if (miss == 0u || aborted(s)) {
+            break;
+        }
+        const unsigned long long now = tc::now_ns();
+        if (t0 == 0ull) {
+            t0 = now;
+        } else if (now - t0 > kGridWaitNs) {
+            fail_wait(s, a.status);
+            break;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kItems; ++m) {
+        const int i = ct + kComputeThreads * m;
+        if (i < items) {
+            rs[i] = ((miss >> m) & 1u) ? 0.0 : v[m];
         }
     }
     compute_sync();
