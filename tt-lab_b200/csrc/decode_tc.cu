@@ -1858,26 +1858,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_tc_kernel(StackArgs a) {
                                 abs_total += s.red[k];
                             }
                             const double logit = double(L.router_b[e]) + total;
-                            a.logits[(step & 1) * kMaxExperts + e] = float(logit);
-                            a.bounds[(step & 1) * kMaxExperts + e] = float((1.02 * 5.9604644775390625e-08 * abs_total +
-                                                 5.9604644775390625e-08 * fabs(logit) + 1e-30) *
-                                                1.0001);
+                            const float bound = float((1.02 * 5.9604644775390625e-08 * abs_total +
+                                                       5.9604644775390625e-08 * fabs(logit) + 1e-30) *
+                                                      1.0001);
+                            // (logit, bound) as two tagged words in one 16-byte store
+                            asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(
+                                             a.rlog + (size_t(step & 1) * kMaxExperts + size_t(e)) * 2),
+                                         "l"(tagged(step_tag(s, step), float(logit))), "l"(tagged(step_tag(s, step), bound))
+                                         : "memory");
                         }
                         compute_sync();
                     }
-                    ok = grid_barrier(a.barrier, gen, a.status, s);
+                    // every expert's (logit, bound) pair, polled as soon as its CTA
+                    // stored it (no grid barrier: a CTA cannot be two steps ahead of
+                    // another, since each step's reductions need every CTA's partials)
+                    static_assert(kMaxExperts <= kComputeThreads, "one expert per compute thread");
+                    if (ct < E) {
+                        float lv[2] = {0.0f, 0.0f};
+                        poll_tagged<2>(
+                            s, [&](int k) { return a.rlog + (size_t(step & 1) * kMaxExperts + size_t(ct)) * 2 + k; },
+                            3u, step_tag(s, step), lv, a.status);
+                        s.logit[ct] = lv[0];
+                        s.bound[ct] = lv[1];
+                        s.val[ct] = lv[0];
+                    }
+                    compute_sync();
+                    if (threadIdx.x == 0) {
+                        s.amb = 0;
+                        s.go = aborted(s) ? 0 : 1;
+                    }
+                    compute_sync();
+                    ok = s.go != 0;
                     if (!ok) {
                         break;
                     }
-                    for (int e = ct; e < E; e += kComputeThreads) {
-                        s.logit[e] = __ldcg(a.logits + (step & 1) * kMaxExperts + e);
-                        s.bound[e] = __ldcg(a.bounds + (step & 1) * kMaxExperts + e);
-                        s.val[e] = s.logit[e];
-                    }
-                    if (threadIdx.x == 0) {
-                        s.amb = 0;
-                    }
-                    compute_sync();
                     if (warp == 0) {
                         warp_top4(s, E);
                     }

@@ -138,8 +138,8 @@ struct StackArgs {
     int expert_begin;
     int expert_count;
     double *acc;               // [2][129] router sums (f64), zeroed by the host before a launch
-    float *logits;             // [2][128] mode 0 (steps of even and odd index in turn)
-    float *bounds;             // [2][128] mode 0
+    unsigned long long *rlog;  // [2][128][2] modes 0 and 2: each expert's fast logit and its error
+                               // bound as two tagged words (16 bytes), steps of even and odd index in turn
     float *hidden;             // [4][2880]
     int32_t *top_idx;          // [4] selection of the last (token, layer)
     float *top_w;              // [4]
@@ -191,6 +191,7 @@ constexpr int kTracePoints = 10;
 constexpr size_t kPartGuWords = size_t(2) * 4 * 23 * 16 * 256;
 constexpr size_t kPartDnWords = size_t(2) * 23 * 16 * 128;
 constexpr size_t kRptWords = size_t(2) * 23 * 129 * 2;
+constexpr size_t kRlogWords = size_t(2) * 128 * 2;
 constexpr size_t kBdownBytes = size_t(2) * 4 * 90 * 256;
 constexpr size_t kSfbDownBytes = size_t(2) * 4 * 96;
 constexpr size_t kBnextBytes = size_t(2) * 90 * 256;

@@ -145,6 +145,7 @@ struct ttl_moe {
     unsigned long long *d_part_gu = nullptr;  // tagged tile partials, [2] x gate/up and down
     unsigned long long *d_part_dn = nullptr;
     unsigned long long *d_rpt = nullptr;  // tagged router sums per down tile
+    unsigned long long *d_rlog = nullptr;  // tagged (logit, bound) pairs of the exact-router steps
     unsigned *d_cnt = nullptr;        // [5] gate/up tiles reduced per expert slot, down tiles with y and B written
     uint8_t *d_bdown = nullptr;
     uint8_t *d_sfb_down = nullptr;
@@ -626,8 +627,7 @@ int enqueue_stack(ttl_moe *h, int begin, int end, const float *x, float *y, size
     a.expert_begin = h->expert_begin;
     a.expert_count = h->expert_count;
     a.acc = h->d_acc;
-    a.logits = h->dw.logits;
-    a.bounds = h->dw.bounds;
+    a.rlog = h->d_rlog;
     a.hidden = h->dw.hidden;
     a.top_idx = h->dw.top_idx;
     a.top_w = h->dw.top_w;
@@ -1146,6 +1146,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
     rc = rc ? rc : alloc_n(h, &h->d_part_gu, kPartGuWords);
     rc = rc ? rc : alloc_n(h, &h->d_part_dn, kPartDnWords);
     rc = rc ? rc : alloc_n(h, &h->d_rpt, kRptWords);
+    rc = rc ? rc : alloc_n(h, &h->d_rlog, kRlogWords);
     rc = rc ? rc : alloc_n(h, &h->d_cnt, 5);
     rc = rc ? rc : alloc_n(h, &h->d_seq, 2);
     rc = rc ? rc : alloc_n(h, &h->d_bdown, kBdownBytes);
@@ -1224,6 +1225,7 @@ int ttl_moe_create(const ttl_moe_config *config, ttl_moe **handle_out) {
         cudaMemset(h->d_part_gu, 0, kPartGuWords * 8) != cudaSuccess ||
         cudaMemset(h->d_part_dn, 0, kPartDnWords * 8) != cudaSuccess ||
         cudaMemset(h->d_rpt, 0, kRptWords * 8) != cudaSuccess ||
+        cudaMemset(h->d_rlog, 0, kRlogWords * 8) != cudaSuccess ||
         cudaMemset(h->d_bdown, 0, kBdownBytes) != cudaSuccess ||
         cudaMemset(h->d_sfb_down, 0x7f, kSfbDownBytes) != cudaSuccess ||
         cudaMemset(h->d_bnext, 0, kBnextBytes) != cudaSuccess ||
@@ -1958,6 +1960,7 @@ int ttl_moe_resync(ttl_moe *h) {
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_part_gu, 0, kPartGuWords * 8, h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_part_dn, 0, kPartDnWords * 8, h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_rpt, 0, kRptWords * 8, h->stream));
+    TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_rlog, 0, kRlogWords * 8, h->stream));
     TTL_TRY_CUDA(h, cudaMemsetAsync(h->d_status, 0, sizeof(uint32_t), h->stream));
     rc = nccl_check(h, api->AllReduce(h->d_sync, h->d_sync + 2, 1, ncclUint32, ncclMax, h->comm, h->stream),
                     "ncclAllReduce (resync barrier)");
