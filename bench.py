@@ -365,7 +365,7 @@ HEAD_BYTES = VOCAB * 90 * 34 + VOCAB * 4 + 2 * DIM * 4  # Q8_0 output.weight, lo
 
 
 def logits_head(torch, ttl_moe, synth, hbm_peak, iters=20, cpu_seconds=6.0):
-    """SURVEY 8(f) rank 2, the output head of GptOssModel::forward: rms_norm
+    """The output head of GptOssModel::forward (src/model.cpp:598-612): rms_norm
     with output_norm.weight, matvec_q8_0 over the 201,088 x 2880 Q8_0
     output.weight (615 MB, far above L2) and greedy, on seeded synthetic
     weights.  Device time per call (CUDA events on the head's stream, x and
@@ -440,7 +440,7 @@ def attn_bytes(attended):
 
 
 def attention_decode(torch, ttl_moe, synth, hbm_peak, context=1024, layers=24, iters=10):
-    """the attention block of a 20b decode layer on the
+    """The attention block of a 20b decode layer (src/model.cpp:572-590) on the
     GPU (ttl_attn), on seeded synthetic weights, at `context` positions
     already in the KV cache: device time per layer (CUDA events on the
     handle's stream over all `layers` layers of one token; even layers attend
