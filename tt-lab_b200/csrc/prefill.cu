@@ -30,7 +30,6 @@ constexpr int kRouterStages = 4;                  // chunks in flight
 constexpr int kRouterRow = kRouterChunk + 4;      // padded shared row, floats (bank spread)
 constexpr int kRouterChunks = kDim / kRouterChunk;  // 30
 constexpr int kGroup = 16;                        // slots per expert-product group
-constexpr int kCombineThreads = 256;              // threads per token of the combine
 static_assert(kDim % kRouterChunk == 0, "router chunks");
 
 __host__ __device__ constexpr int router_threads(int experts) {
@@ -364,53 +363,15 @@ __global__ void prefill_combine_kernel(PrefillWork w, int tokens, float *__restr
         slot[i] = w.pair_slot[t * 4 + r[i]];
         wt[i] = w.top_w[t * 4 + r[i]];
     }
-    if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0u) {
-        // a caller's output not on 16 bytes: one column at a time
-        for (int c = threadIdx.x; c < kDim; c += blockDim.x) {
-            float o = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kTopK; ++i) {
-                if (slot[i] >= 0) {
-                    o = __fadd_rn(o, __fmul_rn(wt[i], w.down[size_t(slot[i]) * kDim + c]));
-                }
-            }
-            out[size_t(t) * kDim + c] = o;
-        }
-        return;
-    }
-    // four columns per float4 (the rows of w.down start on 16 bytes); every
-    // row's loads of this thread are in flight together (one memory latency
-    // per token, not one per column group)
-    constexpr int kVec = kDim / 4;                                       // 720
-    constexpr int kPer = (kVec + kCombineThreads - 1) / kCombineThreads;  // 3
-    static_assert(kDim % 4 == 0, "float4 columns");
-    float4 v[kPer][kTopK];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int c = int(threadIdx.x) + kCombineThreads * k;
+    for (int c = threadIdx.x; c < kDim; c += blockDim.x) {
+        float o = 0.0f;
 #pragma unroll
         for (int i = 0; i < kTopK; ++i) {
-            v[k][i] = (c < kVec && slot[i] >= 0)
-                          ? reinterpret_cast<const float4 *>(w.down + size_t(slot[i]) * kDim)[c]
-                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        }
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int c = int(threadIdx.x) + kCombineThreads * k;
-        if (c < kVec) {
-            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-            for (int i = 0; i < kTopK; ++i) {
-                if (slot[i] >= 0) {
-                    o.x = __fadd_rn(o.x, __fmul_rn(wt[i], v[k][i].x));
-                    o.y = __fadd_rn(o.y, __fmul_rn(wt[i], v[k][i].y));
-                    o.z = __fadd_rn(o.z, __fmul_rn(wt[i], v[k][i].z));
-                    o.w = __fadd_rn(o.w, __fmul_rn(wt[i], v[k][i].w));
-                }
+            if (slot[i] >= 0) {
+                o = __fadd_rn(o, __fmul_rn(wt[i], w.down[size_t(slot[i]) * kDim + c]));
             }
-            reinterpret_cast<float4 *>(out + size_t(t) * kDim)[c] = o;
         }
+        out[size_t(t) * kDim + c] = o;
     }
 }
 
@@ -440,7 +401,7 @@ void launch_prefill_route(const PrefillWork &w, const PrefillShape &s, cudaStrea
 }
 
 void launch_prefill_combine(const PrefillWork &w, const PrefillShape &s, float *out, cudaStream_t stream) {
-    prefill_combine_kernel<<<s.tokens, kCombineThreads, 0, stream>>>(w, s.tokens, out);
+    prefill_combine_kernel<<<s.tokens, 256, 0, stream>>>(w, s.tokens, out);
 }
 
 } // namespace ttl

@@ -219,8 +219,6 @@ __global__ void __launch_bounds__(256) ep_back_kernel(PrefillWork w, EpInbox in,
     publish_last(peers, world, cap, rank, true, arrive, [&](int) { return tagged_word(tag, 0u); });
 }
 
-constexpr int kEpCombineThreads = 256;  // threads per own token of the combine
-
 // One CTA per own token: out = sum over its experts in ascending id of the
 // returned rows w * down (src/model.cpp:450-459).
 __global__ void ep_combine_kernel(const int32_t *__restrict__ idx, const float *__restrict__ back,
@@ -244,46 +242,13 @@ __global__ void ep_combine_kernel(const int32_t *__restrict__ idx, const float *
         }
     }
     const float *rows = back + size_t(t) * 4 * kDim;
-    if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0u) {
-        // a caller's output not on 16 bytes: one column at a time
-        for (int c = threadIdx.x; c < kDim; c += blockDim.x) {
-            float o = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kTopK; ++i) {
-                o = __fadd_rn(o, __ldcg(rows + size_t(order[i]) * kDim + c));
-            }
-            out[size_t(t) * kDim + c] = o;
-        }
-        return;
-    }
-    // four columns per float4 (the returned rows start on 16 bytes); every
-    // row's loads of this thread are in flight together
-    constexpr int kVec = kDim / 4;
-    constexpr int kPer = (kVec + kEpCombineThreads - 1) / kEpCombineThreads;
-    float4 v[kPer][kTopK];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int c = int(threadIdx.x) + kEpCombineThreads * k;
+    for (int c = threadIdx.x; c < kDim; c += blockDim.x) {
+        float o = 0.0f;
 #pragma unroll
         for (int i = 0; i < kTopK; ++i) {
-            v[k][i] = (c < kVec) ? __ldcg(reinterpret_cast<const float4 *>(rows + size_t(order[i]) * kDim) + c)
-                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            o = __fadd_rn(o, __ldcg(rows + size_t(order[i]) * kDim + c));
         }
-    }
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-        const int c = int(threadIdx.x) + kEpCombineThreads * k;
-        if (c < kVec) {
-            float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-            for (int i = 0; i < kTopK; ++i) {
-                o.x = __fadd_rn(o.x, v[k][i].x);
-                o.y = __fadd_rn(o.y, v[k][i].y);
-                o.z = __fadd_rn(o.z, v[k][i].z);
-                o.w = __fadd_rn(o.w, v[k][i].w);
-            }
-            reinterpret_cast<float4 *>(out + size_t(t) * kDim)[c] = o;
-        }
+        out[size_t(t) * kDim + c] = o;
     }
 }
 
@@ -323,7 +288,7 @@ void launch_ep_back(const PrefillWork &w, const EpInbox &in, int world, int rank
 }
 
 void launch_ep_combine(const int32_t *idx, int tokens, const float *back, float *out, cudaStream_t stream) {
-    ep_combine_kernel<<<tokens, kEpCombineThreads, 0, stream>>>(idx, back, out);
+    ep_combine_kernel<<<tokens, 256, 0, stream>>>(idx, back, out);
 }
 
 }  // namespace ttl
