@@ -25,10 +25,10 @@ namespace ttl {
 namespace {
 
 constexpr int kRouterTokens = 4;                  // tokens per router CTA (one warp selects each)
-constexpr int kRouterChunk = 96;                  // columns per staged chunk
+constexpr int kRouterChunk = 64;                  // columns per staged chunk
 constexpr int kRouterStages = 4;                  // chunks in flight
 constexpr int kRouterRow = kRouterChunk + 4;      // padded shared row, floats (bank spread)
-constexpr int kRouterChunks = kDim / kRouterChunk;  // 30
+constexpr int kRouterChunks = kDim / kRouterChunk;  // 45
 constexpr int kGroup = 16;                        // slots per expert-product group
 static_assert(kDim % kRouterChunk == 0, "router chunks");
 
