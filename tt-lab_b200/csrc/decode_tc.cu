@@ -32,17 +32,20 @@
 //
 // Per step (token x layer), with no grid barrier:
 //   A  select   Every CTA polls the router sums the previous step's 23 down
-//               tiles published as tagged words, adds them in tile order (so
+//               tiles published as tagged words (each f64 sum as a hi / lo
+//               pair in one 16-byte word pair), adds them in tile order (so
 //               all CTAs get the same sums -- the RMSNorm scale is a scalar, so
 //               logit_e = b_e + s * sum_c W_ec g_c x_c splits over row slices)
-//               and picks the same top 4; then it loads the B operand those
+//               and picks the same top 4 (four rounds of warp max / min
+//               reductions over order keys); then it loads the B operand those
 //               tiles wrote (digit terms of x*g, counted separately: it is off
 //               the critical path, behind the first weight loads).  The first
 //               step of a launch splits h = RMSNorm(x)*g itself.
 //               Mode 0 (one plain MoE, h given) computes the logits in a
-//               router phase with an error bound instead and re-evaluates
-//               near-ties exactly in the reference's order, so its indices
-//               equal the reference's.
+//               router phase with an error bound instead (CTA e publishes
+//               expert e's logit and bound as a tagged 16-byte pair that every
+//               CTA polls) and re-evaluates near-ties exactly in the
+//               reference's order, so its indices equal the reference's.
 //   B  gate/up  Units are (tile, K-block pair): a tile is 128 gate rows and the 128
 //               up rows of the same outputs of one selected expert (two M = 128
 //               accumulators).  Each CTA takes an equal contiguous range of
@@ -73,7 +76,8 @@
 // tagged words stored into each other's buffers over NVLink and add them in
 // rank order (exchange_row), so every rank continues with the same bits.
 // With more than 32 experts (decode_tc_kernel<true>) the down reducers stage
-// the next layer's router weights of their rows in the idle stage ring.
+// the next layer's router weights of their rows in the idle stage ring (one
+// 2-D tensor copy per tile, kTmaRouter).
 // Every wait is bounded; on timeout the kernel records kStatusWaitTimeout,
 // drains its own copies and MMAs, frees its tensor memory and returns.
 #include <cuda_runtime.h>
